@@ -1,0 +1,257 @@
+/*
+ * qx.h -- C ABI of libqx, the B200 executor for compiled RV32IM transformer circuits.
+ *
+ * The reference drives this path from Python through one class, Executor2
+ * (experimental/riscv/chipformer/rv/tritonexec.py:173-289), plus the free-running decode of
+ * FreeRun (experimental/riscv/chipformer/rv/fastexec.py:236-340).  The reference has no C ABI
+ * of its own; the entry points below are the calls a binding of that class needs, each mapped
+ * to the method it replaces.  Plain pointers and sizes only; every call returns a qx_status and
+ * never aborts the process.  Device pointers are marked `dev`, host pointers `host`.
+ *
+ * Threading: one host thread per qx_t at a time.  Calls that take a cudaStream_t (passed as
+ * void*) only enqueue work on it; qx_step / qx_run allocate nothing and never synchronise, so
+ * they can be captured in a CUDA graph (as Executor2.step is, fastexec.py:418-428).
+ */
+#ifndef QX_H
+#define QX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define QX_API __attribute__((visibility("default")))
+#else
+#define QX_API
+#endif
+
+typedef enum {
+    QX_OK = 0,
+    QX_ERR_INVALID_PLAN = 1,   /* the plan blob failed validation */
+    QX_ERR_INVALID_ARG = 2,    /* a null pointer, a size out of range, a bad row index */
+    QX_ERR_CUDA = 3,           /* a CUDA runtime call failed (qx_last_error has the text) */
+    QX_ERR_OOM = 4,            /* device memory could not be allocated */
+    QX_ERR_DEVICE_FLAG = 5     /* the kernel set a per-machine error word (see qx_errors) */
+} qx_status;
+
+typedef struct qx_executor qx_t;
+
+/* ---- the plan blob (written by qwenputer_b200/plan.py) ------------------------------------- */
+
+#define QX_PLAN_MAGIC 0x314E414C50585151ull /* "QQXPLAN1" */
+#define QX_MPC 32                          /* machines per CTA: one per lane */
+#define QX_NONE 0xFFFFu                    /* "no row" in 16-bit row fields */
+
+enum { /* phase kinds of the per-token program */
+    QX_PH_ZERO = 1,     /* X rows [a, a + b) of the row list: set to 0 */
+    QX_PH_LOADX = 2,    /* step mode: X[row] = x[machine][dim] for pairs [a, a + b) */
+    QX_PH_STAGE = 3,    /* lag history of head sublayer c: entries [a, a + b) */
+    QX_PH_FORMS = 4,    /* forms [a, b); warp ranges warp_ptr[c .. c + NW] */
+    QX_PH_UNITS = 5,    /* FFN nodes [a, b); warp ranges warp_ptr[c .. c + NW] */
+    QX_PH_KSEL = 6,     /* key heads [a, b): key argmax and query top-k, per machine */
+    QX_PH_VH = 7,       /* value heads [a, b): decay, write, read, output, per machine */
+    QX_PH_APPLY = 8,    /* X[dst] += X[src] for pairs [a, a + b) */
+    QX_PH_WRITEOUT = 9, /* step mode: x[machine][dim] = X[row] for pairs [a, a + b) */
+    QX_PH_DECODE = 10,  /* run mode: output code -> token; next embedding into X */
+    QX_PH_END = 11
+};
+
+typedef struct {
+    uint32_t kind, a, b, c;
+} qx_phase;
+
+typedef struct {        /* a linear form over smem rows: sum of w * row, packed entries */
+    uint32_t nnz0;      /* first packed entry (a multiple of 4) */
+    uint16_t nnz4;      /* entries / 4 (zero-weight padded) */
+    uint16_t dst;       /* destination row (scratch) */
+} qx_form;
+
+typedef struct {        /* FFN node: X[out] += sum of its units */
+    uint32_t u0;
+    uint16_t nu;
+    uint16_t out;
+} qx_node;
+
+typedef struct {        /* coef * (F[a] + ca x0) * relu(F[b] + cb x0); QX_NONE rows read 0 */
+    float coef, ca, cb;
+    uint16_t a, b;
+} qx_unit;
+
+typedef struct {        /* lag history entry of a head sublayer */
+    uint32_t e;         /* index into that sublayer's history rows */
+    uint16_t x_row;     /* X row of the dim (the value that becomes lag 1) */
+    uint16_t ml;        /* deepest lag kept (1..3) */
+    uint16_t stage[3];  /* scratch row receiving lag 1, 2, 3 (QX_NONE: not read) */
+    uint16_t pad;
+} qx_stage;
+
+typedef struct {        /* key head: channel -> scratch row and constant, for k and q */
+    uint32_t chan;      /* offset into kq_row / kq_c: [2][128] (k then q) */
+    uint16_t qhot;      /* query rows read (QHOT) */
+    uint16_t slot;      /* its KSEL slot within the phase group */
+} qx_khead;
+
+typedef struct {        /* value head task */
+    uint32_t hl;        /* head sublayer (which S buffer) */
+    uint32_t vh;        /* value-head index within that sublayer */
+    uint32_t col;       /* offset into the per-column tables ([128] each) */
+    uint16_t slot;      /* KSEL slot of its key head */
+    uint16_t nrows;     /* decaying rows (0: the head never decays) */
+    uint16_t a_row, b_row;
+    float ca, cb, bconst;
+} qx_vhead;
+
+typedef struct {        /* a per-column lazily evaluated form (v or z): relu(sum + c x0) */
+    uint32_t nnz0;
+    uint16_t nnz4;
+    uint16_t live;      /* 0: the column has no form (reads 0) */
+    float c;
+} qx_colform;
+
+typedef struct {
+    uint64_t magic;
+    uint32_t version, D;
+    uint32_t n_slots, n_scratch;   /* X rows, scratch rows (smem rows of 33 floats each) */
+    uint32_t nw;                   /* warps per CTA the warp ranges were balanced for */
+    uint32_t n_head_levels;
+    uint32_t one_row;              /* X row of the constant-one dim */
+    uint32_t n_ksel_slots;         /* key-head slots one KSEL phase may fill */
+    uint32_t qhot_max;
+    uint32_t n_fam, n_pay, n_feat, n_emb_rows, n_families;
+    uint32_t vocab;
+    uint32_t n_born0;              /* PAIRS[0 : n_born0] = (row, dim) of the dims set by an
+                                      embedding (ONE and the token features) */
+    /* sections: byte offset from the blob start, element count */
+    uint64_t off[32];
+    uint64_t cnt[32];
+} qx_plan_header;
+
+enum { /* section ids of qx_plan_header.off / cnt */
+    QX_S_RUN_PROG = 0,   /* qx_phase: the run-mode program of one token */
+    QX_S_STEP_PROG,      /* qx_phase: the step-mode program */
+    QX_S_ROWS,           /* uint16: row lists */
+    QX_S_PAIRS,          /* uint32 pairs (row, dim) / (dst, src) */
+    QX_S_FORMS,          /* qx_form */
+    QX_S_NNZ,            /* uint32: row | bf16 weight << 16 */
+    QX_S_WARP_PTR,       /* uint32 */
+    QX_S_NODES,          /* qx_node */
+    QX_S_UNITS,          /* qx_unit */
+    QX_S_STAGES,         /* qx_stage */
+    QX_S_KHEADS,         /* qx_khead */
+    QX_S_KQ_ROW,         /* uint16 [kheads][2][128] */
+    QX_S_KQ_C,           /* float  [kheads][2][128] */
+    QX_S_VHEADS,         /* qx_vhead */
+    QX_S_VFORM,          /* qx_colform [vheads][128] */
+    QX_S_ZFORM,          /* qx_colform [vheads][128] */
+    QX_S_OUT_ROW,        /* uint16 [vheads][128] (QX_NONE: no output) */
+    QX_S_OUT_W,          /* float  [vheads][128] */
+    QX_S_HL_V,           /* uint32 [head levels]: value heads of each head sublayer */
+    QX_S_HL_NE,          /* uint32 [head levels]: lag-history rows of each head sublayer */
+    QX_S_FAM_ROW,        /* uint16 [n_fam]: X rows of the family-id code bits */
+    QX_S_PAY_ROW,        /* uint16 [n_pay]: X rows of the payload code bits */
+    QX_S_FEAT_ROW,       /* uint16 [n_feat]: X rows of ONE and the token features */
+    QX_S_FAM_IDS,        /* int32 [n_families]: first token of each family */
+    QX_S_FAM_SIZE,       /* int32 [n_families] */
+    QX_S_FAM_ROW0,       /* int32 [n_families]: first table row (small families), -1 big */
+    QX_S_EMB_BASE,       /* float [n_families][n_feat] */
+    QX_S_EMB_BITS,       /* float [n_families][n_pay][n_feat] */
+    QX_S_EMB_TABLE,      /* float [n_emb_rows][n_feat] */
+    QX_S_TABLES,         /* uint32 [99][2]: snapshot table -> (head level, first value head) */
+    QX_S_REG_COLS,       /* int32 [32][8] */
+    QX_S_COUNT
+};
+
+/* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */
+
+typedef struct {
+    const uint32_t *rom;    /* host: instruction words from 0x40000 (raw; pre-decoded on device) */
+    uint32_t rom_words;     /* <= 65536 */
+    const uint8_t *drom;    /* host: read-only data bytes from 0x20000, or NULL */
+    uint32_t drom_bytes;    /* <= 131072 */
+    const uint32_t *ram;    /* host: 8192 RAM words */
+    uint32_t x[32];         /* registers (x0 ignored) */
+    uint32_t anchor, n;     /* PC = 0x40000 + 4 (anchor + n) */
+    const uint8_t *bn;      /* host: the digit file [8][128], or NULL (all zero) */
+} qx_machine;
+
+typedef struct {
+    uint32_t x[32];
+    uint32_t anchor, n;
+    uint32_t ram[8192];
+} qx_state;
+
+/* ---- entry points -------------------------------------------------------------------------- */
+
+/* Executor2.__init__ (tritonexec.py:176-244): validate the plan, allocate the device buffers for
+ * `batch` machines on `device` (weights, residual x [batch][D], lag histories, head states S
+ * [batch][V][128][128] per head sublayer, zeroed), copy the plan. */
+QX_API qx_status qx_create(const void *plan /*host*/, size_t plan_bytes, int32_t batch, int32_t device,
+                    qx_t **out);
+
+/* Releases every device buffer of the executor. */
+QX_API qx_status qx_destroy(qx_t *ex);
+
+/* Device pointers of the executor's state buffers (stable for its lifetime), so that a binding
+ * can expose them as tensors mutated in place (Executor2.steps[i]["S"], ["hist"], .y).  kind:
+ * 0 = x [batch][D]; 1 = S of head sublayer i; 2 = lag history of head sublayer i
+ * [3][rows][batch_pad] (lag 1..3, machine fastest); 3 = per-machine error words uint32 [batch];
+ * 4 = token hashes uint64 [batch]; 5 = tokens generated int64 [batch]; 6 = index (1-based) of
+ * the first HALT token generated, int64 [batch], -1 if none; 7 = head-state bytes read or written
+ * by the token kernel so far (uint64 [1], 512 per row transfer: the roofline's touched rows). */
+QX_API qx_status qx_buffer(qx_t *ex, int32_t kind, int32_t i, void **dev_ptr, size_t *bytes);
+
+/* Executor2.reset (tritonexec.py:260-263): zero the lag histories of rows [row0, row0 + n). */
+QX_API qx_status qx_reset(qx_t *ex, int32_t row0, int32_t n, void *stream);
+
+/* core.snapshot + Executor2.load_init (core.py:1218-1270, tritonexec.py:246-258): build the
+ * head states of machines [row0, row0 + n) from host machine images, on the device.  The row's
+ * states are replaced entirely (rows the snapshot does not set become 0). */
+QX_API qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *images /*host*/,
+                           void *stream);
+
+/* Executor2.step (tritonexec.py:272-289): one token for every machine.  x (dev, [batch][D],
+ * the embeddings in) is updated in place to the residual after every node. */
+QX_API qx_status qx_step(qx_t *ex, float *x /*dev*/, void *stream);
+
+/* FreeRun.run (fastexec.py:298-340): n_tokens steps, each decoding the output code into the
+ * next token and its embedding, all on the device, starting from the executor's x buffer (the
+ * embedding of each machine's next input).  Generated token ids go to tokens (dev,
+ * [n_tokens][batch] int32, or NULL); every machine's token hash and counters are updated. */
+QX_API qx_status qx_run(qx_t *ex, int32_t n_tokens, int32_t *tokens /*dev*/, void *stream);
+
+/* Sets x row r to the embedding of token tok[r] for rows [row0, row0 + n) (FreeRun.load's first
+ * token, fastexec.py:292-296), and clears those rows' hashes and counters. */
+QX_API qx_status qx_set_tokens(qx_t *ex, int32_t row0, int32_t n, const int32_t *tok /*host*/,
+                        void *stream);
+
+/* The inverse of qx_load_machines for one row: registers, PC anchor / n, RAM words. */
+QX_API qx_status qx_readback(qx_t *ex, int32_t row, qx_state *out /*host*/, void *stream);
+
+/* Per-machine 64-bit checksums of (x1..x31, anchor, n, RAM) computed on the device into out
+ * (dev, [batch] uint64).  The FNV-1a 64 of those 8,225 words, little-endian. */
+QX_API qx_status qx_checksums(qx_t *ex, uint64_t *out /*dev*/, void *stream);
+
+/* OR of every machine's error word (dev -> host copy; synchronises the stream). */
+QX_API qx_status qx_errors(qx_t *ex, uint32_t *any /*host*/, void *stream);
+
+/* The text of the last error on this thread ("" if none). */
+QX_API const char *qx_last_error(void);
+
+/* ---- the gated delta-rule decode step (standalone microbenchmark path) ------------------- */
+
+/* For every (b, h) of BH heads: S <- alpha S; kv = S^T k; S <- S + k (x) beta (v - kv);
+ * o = S^T q; sums over the key index in order, each product rounded before it is added.  Keys
+ * with a single nonzero take a row path that touches only that row (plus the whole matrix when
+ * alpha != 1); other keys update the whole matrix.  All dev, fp32: S [BH][128][128], q/k/v/o
+ * [BH][128], alpha/beta [BH].  work: dev scratch of qx_gdn_work_bytes(BH) bytes. */
+QX_API size_t qx_gdn_work_bytes(int64_t BH);
+QX_API qx_status qx_gdn_step(int64_t BH, float *S, const float *q, const float *k, const float *v,
+                      const float *alpha, const float *beta, float *o, void *work, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QX_H */

@@ -1,0 +1,469 @@
+// qx_api.cu -- the C ABI of include/qx.h: plan validation, device buffers, launches.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "qx.h"
+#include "qx_exec.cuh"
+
+template <int RUN>
+__global__ void qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens);
+__global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok);
+__global__ void qx_predecode_kernel(const QxImage *img, uint32_t *pool, int32_t n);
+__global__ void qx_load_kernel(const __grid_constant__ QxDev d, const QxImage *img, const uint32_t *pool,
+                               int32_t row0, int32_t n);
+__global__ void qx_readback_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, qx_state *out);
+__global__ void qx_checksum_kernel(const qx_state *st, int32_t n, uint64_t *out);
+__global__ void qx_reset_kernel(float *H, uint32_t ne, uint32_t bpad, int32_t row0, int32_t n);
+size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
+                     const float *beta, float *o, uint32_t *work, cudaStream_t st);
+cudaError_t qx_gdn_prepare();
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+qx_status fail(qx_status s, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return s;
+}
+
+#define CU(call)                                                                                  \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess) return fail(QX_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+}  // namespace
+
+struct qx_executor {
+    int device = 0, B = 0, Bpad = 0;
+    qx_plan_header hdr{};
+    std::vector<uint8_t> host_plan;
+    void *dplan = nullptr;
+    QxDev d{};
+    int n_hl = 0;
+    size_t smem = 0;
+    int32_t *dtok = nullptr;      // [B] scratch for qx_set_tokens
+    qx_state *dstate = nullptr;   // readback staging
+    int32_t state_cap = 0;
+    uint32_t *err_host = nullptr;
+    std::vector<void *> allocs;
+    ~qx_executor() {
+        for (void *p : allocs) cudaFree(p);
+        if (dplan) cudaFree(dplan);
+        if (err_host) cudaFreeHost(err_host);
+        if (dstate) cudaFree(dstate);
+    }
+};
+
+namespace {
+
+qx_status dev_alloc(qx_t *ex, void **p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(e == cudaErrorMemoryAllocation ? QX_ERR_OOM : QX_ERR_CUDA, "cudaMalloc(%zu): %s", bytes,
+                    cudaGetErrorString(e));
+    }
+    ex->allocs.push_back(*p);
+    return QX_OK;
+}
+
+template <class T>
+const T *sec(const qx_executor *ex, int s) {
+    return reinterpret_cast<const T *>(static_cast<const uint8_t *>(ex->dplan) + ex->hdr.off[s]);
+}
+
+struct SecSpec {
+    int id;
+    size_t elem;
+};
+
+qx_status validate(const qx_plan_header &h, size_t bytes) {
+    if (bytes < sizeof(qx_plan_header)) return fail(QX_ERR_INVALID_PLAN, "plan shorter than its header");
+    if (h.magic != QX_PLAN_MAGIC) return fail(QX_ERR_INVALID_PLAN, "bad plan magic");
+    if (h.version != 1) return fail(QX_ERR_INVALID_PLAN, "plan version %u, expected 1", h.version);
+    if (h.nw != QX_NW) return fail(QX_ERR_INVALID_PLAN, "plan balanced for %u warps, kernel has %d", h.nw, QX_NW);
+    if (h.n_head_levels > QX_MAX_HL) return fail(QX_ERR_INVALID_PLAN, "too many head sublayers");
+    if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
+    if (h.n_born0 != h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
+    const SecSpec specs[] = {
+        {QX_S_RUN_PROG, sizeof(qx_phase)}, {QX_S_STEP_PROG, sizeof(qx_phase)}, {QX_S_ROWS, 2},
+        {QX_S_PAIRS, 8}, {QX_S_FORMS, sizeof(qx_form)}, {QX_S_NNZ, 4}, {QX_S_WARP_PTR, 4},
+        {QX_S_NODES, sizeof(qx_node)}, {QX_S_UNITS, sizeof(qx_unit)}, {QX_S_STAGES, sizeof(qx_stage)},
+        {QX_S_KHEADS, sizeof(qx_khead)}, {QX_S_KQ_ROW, 2}, {QX_S_KQ_C, 4}, {QX_S_VHEADS, sizeof(qx_vhead)},
+        {QX_S_VFORM, sizeof(qx_colform)}, {QX_S_ZFORM, sizeof(qx_colform)}, {QX_S_OUT_ROW, 2}, {QX_S_OUT_W, 4},
+        {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 2}, {QX_S_PAY_ROW, 2}, {QX_S_FEAT_ROW, 2},
+        {QX_S_FAM_IDS, 4}, {QX_S_FAM_SIZE, 4}, {QX_S_FAM_ROW0, 4}, {QX_S_EMB_BASE, 4}, {QX_S_EMB_BITS, 4},
+        {QX_S_EMB_TABLE, 4}, {QX_S_TABLES, 4}, {QX_S_REG_COLS, 4}};
+    for (const SecSpec &s : specs) {
+        if (h.off[s.id] % 16 || h.off[s.id] + h.cnt[s.id] * s.elem > bytes)
+            return fail(QX_ERR_INVALID_PLAN, "section %d out of bounds", s.id);
+    }
+    if (h.cnt[QX_S_TABLES] != 198 || h.cnt[QX_S_REG_COLS] != 256)
+        return fail(QX_ERR_INVALID_PLAN, "snapshot tables missing");
+    if (h.cnt[QX_S_HL_V] != h.n_head_levels || h.cnt[QX_S_FEAT_ROW] != h.n_feat ||
+        h.cnt[QX_S_FAM_ROW] != h.n_fam || h.cnt[QX_S_PAY_ROW] != h.n_pay)
+        return fail(QX_ERR_INVALID_PLAN, "section counts disagree with the header");
+    if (h.cnt[QX_S_NNZ] % 4) return fail(QX_ERR_INVALID_PLAN, "packed entries not padded to 4");
+    return QX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *qx_last_error(void) { return g_err; }
+
+qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t device, qx_t **out) {
+    g_err[0] = 0;
+    if (!plan || !out || batch < 1) return fail(QX_ERR_INVALID_ARG, "qx_create: bad arguments");
+    *out = nullptr;
+    qx_plan_header h;
+    if (plan_bytes < sizeof(h)) return fail(QX_ERR_INVALID_PLAN, "plan too short");
+    memcpy(&h, plan, sizeof(h));
+    qx_status s = validate(h, plan_bytes);
+    if (s != QX_OK) return s;
+    CU(cudaSetDevice(device));
+    qx_executor *ex = new (std::nothrow) qx_executor();
+    if (!ex) return fail(QX_ERR_OOM, "host allocation failed");
+    ex->device = device;
+    ex->hdr = h;
+    ex->B = batch;
+    ex->Bpad = (batch + 31) / 32 * 32;
+    ex->host_plan.assign(static_cast<const uint8_t *>(plan), static_cast<const uint8_t *>(plan) + plan_bytes);
+    auto bail = [&](qx_status st) {
+        delete ex;
+        return st;
+    };
+    cudaError_t e = cudaMalloc(&ex->dplan, plan_bytes);
+    if (e != cudaSuccess) return bail(fail(QX_ERR_OOM, "plan upload: %s", cudaGetErrorString(e)));
+    e = cudaMemcpy(ex->dplan, plan, plan_bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return bail(fail(QX_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e)));
+
+    QxDev &d = ex->d;
+    d.run_prog = sec<qx_phase>(ex, QX_S_RUN_PROG);
+    d.step_prog = sec<qx_phase>(ex, QX_S_STEP_PROG);
+    d.rows = sec<uint16_t>(ex, QX_S_ROWS);
+    d.pairs = sec<uint2>(ex, QX_S_PAIRS);
+    d.forms = sec<qx_form>(ex, QX_S_FORMS);
+    d.nnz = sec<uint32_t>(ex, QX_S_NNZ);
+    d.warp_ptr = sec<uint32_t>(ex, QX_S_WARP_PTR);
+    d.nodes = sec<qx_node>(ex, QX_S_NODES);
+    d.units = sec<qx_unit>(ex, QX_S_UNITS);
+    d.stages = sec<qx_stage>(ex, QX_S_STAGES);
+    d.kheads = sec<qx_khead>(ex, QX_S_KHEADS);
+    d.kq_row = sec<uint16_t>(ex, QX_S_KQ_ROW);
+    d.kq_c = sec<float>(ex, QX_S_KQ_C);
+    d.vheads = sec<qx_vhead>(ex, QX_S_VHEADS);
+    d.vform = sec<qx_colform>(ex, QX_S_VFORM);
+    d.zform = sec<qx_colform>(ex, QX_S_ZFORM);
+    d.out_row = sec<uint16_t>(ex, QX_S_OUT_ROW);
+    d.out_w = sec<float>(ex, QX_S_OUT_W);
+    d.fam_row = sec<uint16_t>(ex, QX_S_FAM_ROW);
+    d.pay_row = sec<uint16_t>(ex, QX_S_PAY_ROW);
+    d.feat_row = sec<uint16_t>(ex, QX_S_FEAT_ROW);
+    d.fam_ids = sec<int32_t>(ex, QX_S_FAM_IDS);
+    d.fam_size = sec<int32_t>(ex, QX_S_FAM_SIZE);
+    d.fam_row0 = sec<int32_t>(ex, QX_S_FAM_ROW0);
+    d.emb_base = sec<float>(ex, QX_S_EMB_BASE);
+    d.emb_bits = sec<float>(ex, QX_S_EMB_BITS);
+    d.emb_table = sec<float>(ex, QX_S_EMB_TABLE);
+    d.tables = sec<uint32_t>(ex, QX_S_TABLES);
+    d.reg_cols = sec<int32_t>(ex, QX_S_REG_COLS);
+    d.B = batch;
+    d.Bpad = ex->Bpad;
+    d.D = (int32_t)h.D;
+    d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
+    d.one_row = (int32_t)h.one_row;
+    d.n_fam = (int32_t)h.n_fam;
+    d.n_pay = (int32_t)h.n_pay;
+    d.n_feat = (int32_t)h.n_feat;
+    d.n_families = (int32_t)h.n_families;
+    d.n_emb_rows = (int32_t)h.n_emb_rows;
+    d.n_born0 = (int32_t)h.n_born0;
+    d.qhot_max = (int32_t)h.qhot_max;
+    d.ksel_slots = (int32_t)h.n_ksel_slots;
+    d.n_hl = (int32_t)h.n_head_levels;
+    {
+        // the HALT control token: the family whose first id is the largest below the vocab end is
+        // a control; HALT is the sixth control (spec.py:67)
+        const int32_t *ids = reinterpret_cast<const int32_t *>(ex->host_plan.data() + h.off[QX_S_FAM_IDS]);
+        const int32_t *sz = reinterpret_cast<const int32_t *>(ex->host_plan.data() + h.off[QX_S_FAM_SIZE]);
+        int32_t ctrl = -1;
+        for (uint32_t f = 0; f < h.n_families; f++)
+            if (sz[f] == 1 && (ctrl < 0 || ids[f] < ctrl)) ctrl = ids[f];
+        d.halt_tok = ctrl < 0 ? -1 : ctrl + 5;
+    }
+    ex->n_hl = (int)h.n_head_levels;
+    const uint32_t *hlv = reinterpret_cast<const uint32_t *>(ex->host_plan.data() + h.off[QX_S_HL_V]);
+    const uint32_t *hne = reinterpret_cast<const uint32_t *>(ex->host_plan.data() + h.off[QX_S_HL_NE]);
+    void *p;
+    for (int i = 0; i < ex->n_hl; i++) {
+        d.V[i] = hlv[i];
+        d.NE[i] = hne[i];
+        size_t sb = (size_t)batch * hlv[i] * QX_HD * QX_HD * 4;
+        if ((s = dev_alloc(ex, &p, sb)) != QX_OK) return bail(s);
+        d.S[i] = static_cast<float *>(p);
+        if (cudaMemset(p, 0, sb) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "memset S"));
+        size_t hb = (size_t)3 * hne[i] * ex->Bpad * 4;
+        if ((s = dev_alloc(ex, &p, hb)) != QX_OK) return bail(s);
+        d.hist[i] = static_cast<float *>(p);
+        if (cudaMemset(p, 0, hb) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "memset hist"));
+    }
+    size_t xb = (size_t)batch * h.D * 4;
+    if ((s = dev_alloc(ex, &p, xb)) != QX_OK) return bail(s);
+    d.x = static_cast<float *>(p);
+    if ((s = dev_alloc(ex, &p, (size_t)batch * 4)) != QX_OK) return bail(s);
+    d.err = static_cast<uint32_t *>(p);
+    if ((s = dev_alloc(ex, &p, (size_t)batch * 8)) != QX_OK) return bail(s);
+    d.hash = static_cast<uint64_t *>(p);
+    if ((s = dev_alloc(ex, &p, (size_t)batch * 8)) != QX_OK) return bail(s);
+    d.count = static_cast<int64_t *>(p);
+    if ((s = dev_alloc(ex, &p, (size_t)batch * 8)) != QX_OK) return bail(s);
+    d.halt_at = static_cast<int64_t *>(p);
+    if ((s = dev_alloc(ex, &p, (size_t)batch * 4)) != QX_OK) return bail(s);
+    ex->dtok = static_cast<int32_t *>(p);
+    if ((s = dev_alloc(ex, &p, 64)) != QX_OK) return bail(s);
+    d.state_bytes = static_cast<unsigned long long *>(p);
+    if (cudaMemset(p, 0, 64) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "counter init"));
+    if (cudaMemset(d.x, 0, xb) != cudaSuccess || cudaMemset(d.err, 0, (size_t)batch * 4) != cudaSuccess ||
+        cudaMemset(d.count, 0, (size_t)batch * 8) != cudaSuccess ||
+        cudaMemset(d.halt_at, 0xFF, (size_t)batch * 8) != cudaSuccess ||
+        cudaMemset(d.hash, 0, (size_t)batch * 8) != cudaSuccess)
+        return bail(fail(QX_ERR_CUDA, "buffer init"));
+    if (cudaMallocHost(&ex->err_host, (size_t)batch * 4) != cudaSuccess)
+        return bail(fail(QX_ERR_OOM, "pinned error buffer"));
+    ex->smem = qx_smem_bytes(d);
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if ((int)ex->smem > optin)
+        return bail(fail(QX_ERR_INVALID_PLAN, "plan needs %zu B of shared memory per CTA, device has %d", ex->smem,
+                         optin));
+    if (cudaFuncSetAttribute(qx_token_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(qx_token_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
+            cudaSuccess || qx_gdn_prepare() != cudaSuccess)
+        return bail(fail(QX_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError())));
+    if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(QX_ERR_CUDA, "init sync"));
+    *out = ex;
+    return QX_OK;
+}
+
+qx_status qx_destroy(qx_t *ex) {
+    if (!ex) return QX_OK;
+    cudaSetDevice(ex->device);
+    cudaDeviceSynchronize();
+    delete ex;
+    return QX_OK;
+}
+
+qx_status qx_buffer(qx_t *ex, int32_t kind, int32_t i, void **ptr, size_t *bytes) {
+    if (!ex || !ptr || !bytes) return fail(QX_ERR_INVALID_ARG, "qx_buffer: null argument");
+    const QxDev &d = ex->d;
+    switch (kind) {
+    case 0: *ptr = d.x; *bytes = (size_t)ex->B * d.D * 4; return QX_OK;
+    case 1:
+    case 2:
+        if (i < 0 || i >= ex->n_hl) return fail(QX_ERR_INVALID_ARG, "qx_buffer: head sublayer %d", i);
+        if (kind == 1) { *ptr = d.S[i]; *bytes = (size_t)ex->B * d.V[i] * QX_HD * QX_HD * 4; }
+        else { *ptr = d.hist[i]; *bytes = (size_t)3 * d.NE[i] * ex->Bpad * 4; }
+        return QX_OK;
+    case 3: *ptr = d.err; *bytes = (size_t)ex->B * 4; return QX_OK;
+    case 4: *ptr = d.hash; *bytes = (size_t)ex->B * 8; return QX_OK;
+    case 5: *ptr = d.count; *bytes = (size_t)ex->B * 8; return QX_OK;
+    case 6: *ptr = d.halt_at; *bytes = (size_t)ex->B * 8; return QX_OK;
+    case 7: *ptr = d.state_bytes; *bytes = 8; return QX_OK;
+    default: return fail(QX_ERR_INVALID_ARG, "qx_buffer: kind %d", kind);
+    }
+}
+
+qx_status qx_reset(qx_t *ex, int32_t row0, int32_t n, void *stream) {
+    if (!ex || row0 < 0 || n < 0 || row0 + n > ex->B) return fail(QX_ERR_INVALID_ARG, "qx_reset: rows");
+    if (n == 0) return QX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < ex->n_hl; i++)
+        qx_reset_kernel<<<256, 256, 0, st>>>(ex->d.hist[i], ex->d.NE[i], ex->Bpad, row0, n);
+    CU(cudaGetLastError());
+    return QX_OK;
+}
+
+qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *images, void *stream) {
+    if (!ex || !images || row0 < 0 || n < 0 || row0 + n > ex->B)
+        return fail(QX_ERR_INVALID_ARG, "qx_load_machines: rows");
+    if (n == 0) return QX_OK;
+    CU(cudaSetDevice(ex->device));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int chunk = 256;
+    for (int c0 = 0; c0 < n; c0 += chunk) {
+        const int cn = n - c0 < chunk ? n - c0 : chunk;
+        std::vector<QxImage> img(cn);
+        std::vector<uint32_t> pool;
+        for (int i = 0; i < cn; i++) {
+            const qx_machine &m = images[c0 + i];
+            if (m.rom_words > 65536 || m.drom_bytes > 131072 || (!m.rom && m.rom_words) || !m.ram)
+                return fail(QX_ERR_INVALID_ARG, "qx_load_machines: image %d", c0 + i);
+            QxImage &q = img[i];
+            q.rom_off = (uint32_t)pool.size();
+            q.rom_len = m.rom_words;
+            pool.insert(pool.end(), m.rom, m.rom + m.rom_words);
+            q.drom_off = (uint32_t)pool.size();
+            q.drom_words = (m.drom_bytes + 3) / 4;
+            for (uint32_t w = 0; w < q.drom_words; w++) {
+                uint32_t v = 0;
+                for (int b = 0; b < 4; b++)
+                    if (4 * w + b < m.drom_bytes) v |= (uint32_t)m.drom[4 * w + b] << (8 * b);
+                pool.push_back(v);
+            }
+            q.ram_off = (uint32_t)pool.size();
+            pool.insert(pool.end(), m.ram, m.ram + 8192);
+            if (m.bn) {
+                q.bn_off = (uint32_t)pool.size();
+                for (int w = 0; w < 256; w++) {
+                    uint32_t v = 0;
+                    for (int b = 0; b < 4; b++) v |= (uint32_t)m.bn[4 * w + b] << (8 * b);
+                    pool.push_back(v);
+                }
+            } else {
+                q.bn_off = 0xFFFFFFFFu;
+            }
+            memcpy(q.x, m.x, sizeof(q.x));
+            q.x[0] = 0;
+            q.anchor = m.anchor;
+            q.n = m.n;
+        }
+        void *dimg = nullptr, *dpool = nullptr;
+        CU(cudaMalloc(&dimg, img.size() * sizeof(QxImage)));
+        cudaError_t e = cudaMalloc(&dpool, pool.size() * 4);
+        if (e != cudaSuccess) {
+            cudaFree(dimg);
+            return fail(QX_ERR_OOM, "image pool: %s", cudaGetErrorString(e));
+        }
+        e = cudaMemcpyAsync(dimg, img.data(), img.size() * sizeof(QxImage), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dpool, pool.data(), pool.size() * 4, cudaMemcpyHostToDevice, st);
+        for (int i = 0; i < ex->n_hl && e == cudaSuccess; i++) {
+            size_t per = (size_t)ex->d.V[i] * QX_HD * QX_HD * 4;
+            e = cudaMemsetAsync(reinterpret_cast<uint8_t *>(ex->d.S[i]) + per * (row0 + c0), 0, per * cn, st);
+        }
+        if (e == cudaSuccess) {
+            qx_predecode_kernel<<<dim3(4, cn), 256, 0, st>>>(static_cast<QxImage *>(dimg),
+                                                            static_cast<uint32_t *>(dpool), cn);
+            qx_load_kernel<<<dim3(64, cn), 256, 0, st>>>(ex->d, static_cast<QxImage *>(dimg),
+                                                        static_cast<uint32_t *>(dpool), row0 + c0, cn);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        cudaFree(dimg);
+        cudaFree(dpool);
+        if (e != cudaSuccess) return fail(QX_ERR_CUDA, "qx_load_machines: %s", cudaGetErrorString(e));
+    }
+    return QX_OK;
+}
+
+qx_status qx_step(qx_t *ex, float *x, void *stream) {
+    if (!ex || !x) return fail(QX_ERR_INVALID_ARG, "qx_step: null argument");
+    QxDev d = ex->d;
+    d.x = x;
+    qx_token_kernel<0><<<ex->Bpad / 32, QX_NT, ex->smem, static_cast<cudaStream_t>(stream)>>>(d, 1, nullptr);
+    CU(cudaGetLastError());
+    return QX_OK;
+}
+
+qx_status qx_run(qx_t *ex, int32_t n_tokens, int32_t *tokens, void *stream) {
+    if (!ex || n_tokens < 0) return fail(QX_ERR_INVALID_ARG, "qx_run: bad arguments");
+    if (n_tokens == 0) return QX_OK;
+    qx_token_kernel<1><<<ex->Bpad / 32, QX_NT, ex->smem, static_cast<cudaStream_t>(stream)>>>(ex->d, n_tokens,
+                                                                                            tokens);
+    CU(cudaGetLastError());
+    return QX_OK;
+}
+
+qx_status qx_set_tokens(qx_t *ex, int32_t row0, int32_t n, const int32_t *tok, void *stream) {
+    if (!ex || !tok || row0 < 0 || n < 0 || row0 + n > ex->B) return fail(QX_ERR_INVALID_ARG, "qx_set_tokens");
+    if (n == 0) return QX_OK;
+    for (int i = 0; i < n; i++)
+        if (tok[i] < 0 || (uint32_t)tok[i] >= ex->hdr.vocab) return fail(QX_ERR_INVALID_ARG, "token %d", tok[i]);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CU(cudaMemcpyAsync(ex->dtok, tok, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    qx_embed_kernel<<<n, 256, 0, st>>>(ex->d, row0, n, ex->dtok);
+    CU(cudaGetLastError());
+    CU(cudaStreamSynchronize(st));
+    return QX_OK;
+}
+
+static qx_status ensure_states(qx_t *ex, int32_t n) {
+    if (ex->state_cap >= n) return QX_OK;
+    if (ex->dstate) cudaFree(ex->dstate);
+    ex->dstate = nullptr;
+    ex->state_cap = 0;
+    cudaError_t e = cudaMalloc(&ex->dstate, (size_t)n * sizeof(qx_state));
+    if (e != cudaSuccess) return fail(QX_ERR_OOM, "state staging: %s", cudaGetErrorString(e));
+    ex->state_cap = n;
+    return QX_OK;
+}
+
+qx_status qx_readback(qx_t *ex, int32_t row, qx_state *out, void *stream) {
+    if (!ex || !out || row < 0 || row >= ex->B) return fail(QX_ERR_INVALID_ARG, "qx_readback");
+    qx_status s = ensure_states(ex, 1);
+    if (s != QX_OK) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    qx_readback_kernel<<<1, 256, 0, st>>>(ex->d, row, 1, ex->dstate);
+    CU(cudaGetLastError());
+    CU(cudaMemcpyAsync(out, ex->dstate, sizeof(qx_state), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    return QX_OK;
+}
+
+qx_status qx_checksums(qx_t *ex, uint64_t *out, void *stream) {
+    if (!ex || !out) return fail(QX_ERR_INVALID_ARG, "qx_checksums");
+    const int chunk = ex->B < 1024 ? ex->B : 1024;
+    qx_status s = ensure_states(ex, chunk);
+    if (s != QX_OK) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int r0 = 0; r0 < ex->B; r0 += chunk) {
+        const int n = ex->B - r0 < chunk ? ex->B - r0 : chunk;
+        qx_readback_kernel<<<n, 256, 0, st>>>(ex->d, r0, n, ex->dstate);
+        qx_checksum_kernel<<<(n + 127) / 128, 128, 0, st>>>(ex->dstate, n, out + r0);
+    }
+    CU(cudaGetLastError());
+    return QX_OK;
+}
+
+qx_status qx_errors(qx_t *ex, uint32_t *any, void *stream) {
+    if (!ex || !any) return fail(QX_ERR_INVALID_ARG, "qx_errors");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    CU(cudaMemcpyAsync(ex->err_host, ex->d.err, (size_t)ex->B * 4, cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    uint32_t acc = 0;
+    for (int i = 0; i < ex->B; i++) acc |= ex->err_host[i];
+    *any = acc;
+    return QX_OK;
+}
+
+size_t qx_gdn_work_bytes(int64_t BH) { return 8 + 4 * (size_t)(BH > 0 ? BH : 0); }
+
+qx_status qx_gdn_step(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
+                      const float *beta, float *o, void *work, void *stream) {
+    if (BH < 0 || BH > (int64_t)1 << 30) return fail(QX_ERR_INVALID_ARG, "qx_gdn_step: BH %lld", (long long)BH);
+    if (BH == 0) return QX_OK;
+    if (!S || !q || !k || !v || !alpha || !beta || !o || !work)
+        return fail(QX_ERR_INVALID_ARG, "qx_gdn_step: null argument");
+    static thread_local int prepared = 0;
+    if (!prepared) {
+        CU(qx_gdn_prepare());
+        prepared = 1;
+    }
+    qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, static_cast<uint32_t *>(work), static_cast<cudaStream_t>(stream));
+    CU(cudaGetLastError());
+    return QX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,69 @@
+// qx_exec.cuh -- device-side view of a plan and of an executor's buffers (shared by the kernels).
+#pragma once
+#include <cstdint>
+
+#include "qx.h"
+
+#define QX_NW 16                 // warps per CTA
+#define QX_NT (QX_NW * 32)       // threads per CTA
+#define QX_RP 33                 // floats per smem row (32 machines + 1 pad)
+#define QX_MAX_HL 16             // head sublayers a plan may have
+#define QX_HD 128
+
+struct QxDev {
+    // plan sections (device)
+    const qx_phase *run_prog, *step_prog;
+    const uint16_t *rows;
+    const uint2 *pairs;
+    const qx_form *forms;
+    const uint32_t *nnz;
+    const uint32_t *warp_ptr;
+    const qx_node *nodes;
+    const qx_unit *units;
+    const qx_stage *stages;
+    const qx_khead *kheads;
+    const uint16_t *kq_row;
+    const float *kq_c;
+    const qx_vhead *vheads;
+    const qx_colform *vform, *zform;
+    const uint16_t *out_row;
+    const float *out_w;
+    const uint16_t *fam_row, *pay_row, *feat_row;
+    const int32_t *fam_ids, *fam_size, *fam_row0;
+    const float *emb_base, *emb_bits, *emb_table;
+    const uint32_t *tables;     // [99][2]
+    const int32_t *reg_cols;    // [32][8]
+    // executor buffers
+    float *S[QX_MAX_HL];        // [B][V][128][128]
+    float *hist[QX_MAX_HL];     // [3][NE][Bpad]
+    uint32_t V[QX_MAX_HL], NE[QX_MAX_HL];
+    float *x;                   // [B][D]
+    uint32_t *err;              // [B]
+    uint64_t *hash;             // [B]
+    int64_t *count;             // [B] tokens generated
+    int64_t *halt_at;           // [B] index (1-based) of the first HALT token, -1 none
+    unsigned long long *state_bytes;  // [1] head-state bytes the kernel read or wrote (512 B rows)
+    // sizes
+    int32_t B, Bpad, D;
+    int32_t smem_rows, one_row, n_fam, n_pay, n_feat, n_families, n_emb_rows, n_born0;
+    int32_t qhot_max, ksel_slots, n_hl, halt_tok;
+};
+
+// per-machine error bits
+#define QX_E_CODE 1u        // the output code names no token
+#define QX_E_KEY 2u         // a key with more than one positive channel
+#define QX_E_QUERY 4u       // a query with more positive channels than the head reads
+#define QX_E_BUSY 8u        // a bounded wait gave up
+
+struct QxImage {  // one machine inside a packed image upload (offsets into the word pool)
+    uint32_t rom_off, rom_len, drom_off, drom_words, ram_off, bn_off;  // bn_off: ~0 = none
+    uint32_t x[32];
+    uint32_t anchor, n;
+};
+
+// shared memory after the rows: key-select slots, the decode area ([2][32] ints, [16][32]
+// payload floats) and a 64-byte counter block
+static inline size_t qx_smem_bytes(const QxDev &d) {
+    return (size_t)d.smem_rows * QX_RP * 4 + (size_t)d.ksel_slots * 32 * (1 + d.qhot_max) * 4 +
+           (size_t)32 * (2 + 16) * 4 + 64;
+}

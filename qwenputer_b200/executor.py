@@ -1,0 +1,318 @@
+"""The executor as the reference's callers see it, over the C ABI of include/qx.h.
+
+``Executor`` keeps the surface of the reference's Triton executor
+(``ERV/chipformer/rv/tritonexec.py:173-289``, ``Executor2``): ``Executor(c, batch, device)``,
+``D``, ``B``, ``steps`` (one dict per sublayer; head sublayers expose ``"S"`` ``[B, V, 128, 128]``
+fp32 device tensors mutated in place and ``"hist"``), ``load_init(row)``, ``reset(rows)``,
+``embed(toks)`` and ``step(x)``; so ``chat.ExecRow``-style callers (clone / restore ``S`` and
+``hist``, capture ``step`` in a CUDA graph) work unchanged.  ``FreeRun`` keeps the surface of
+``ERV/chipformer/rv/fastexec.py:236-340`` (``load(row, first_token)``, ``run(n)``) with decode and
+next embedding on the device inside the same persistent kernel.
+
+Differences a caller can observe:
+  * ``hist`` is ``[B, 3, n]`` over the ``n`` dims that sublayer's heads read at lags 1..3 (the
+    only dims the history is kept for), not ``[B, 3, D]``; ``hist_dims[i]`` lists them;
+  * a machine can be loaded without a live graph: ``load_machines(row0, programs)`` builds the
+    head states on the device from program images (``core.snapshot``'s layout).
+
+There is no CPU fallback: without libqx.so or a CUDA device every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+from . import graphfile
+from .plan import compile_plan
+
+LIB_PATH = Path(__file__).resolve().parent / "libqx.so"
+HD = 128
+_lib = None
+_plans: dict = {}
+
+
+class QxError(RuntimeError):
+    pass
+
+
+def lib():
+    """libqx.so, loaded once; raises if it was not built (python -m qwenputer_b200.build)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise QxError(f"{LIB_PATH} is missing: build it with `python -m qwenputer_b200.build`")
+        L = C.CDLL(str(LIB_PATH))
+        L.qx_last_error.restype = C.c_char_p
+        for name in ("qx_create", "qx_destroy", "qx_buffer", "qx_reset", "qx_load_machines",
+                     "qx_step", "qx_run", "qx_set_tokens", "qx_readback", "qx_checksums",
+                     "qx_errors", "qx_gdn_step"):
+            getattr(L, name).restype = C.c_int
+        L.qx_gdn_work_bytes.restype = C.c_size_t
+        L.qx_gdn_work_bytes.argtypes = [C.c_int64]
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise QxError(f"{what}: status {status}: {lib().qx_last_error().decode()}")
+
+
+class Machine(C.Structure):
+    """qx_machine (include/qx.h)."""
+    _fields_ = [("rom", C.c_void_p), ("rom_words", C.c_uint32), ("drom", C.c_void_p),
+                ("drom_bytes", C.c_uint32), ("ram", C.c_void_p), ("x", C.c_uint32 * 32),
+                ("anchor", C.c_uint32), ("n", C.c_uint32), ("bn", C.c_void_p)]
+
+
+class State(C.Structure):
+    """qx_state: registers, PC anchor / n (PC = 0x40000 + 4 (anchor + n)), RAM words."""
+    _fields_ = [("x", C.c_uint32 * 32), ("anchor", C.c_uint32), ("n", C.c_uint32),
+                ("ram", C.c_uint32 * 8192)]
+
+
+class _DevArray:
+    """A device buffer of the executor seen by torch without a copy."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def _torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        raise QxError("the executor needs a CUDA device; there is no CPU path")
+    return torch
+
+
+def load_graph(c=None) -> graphfile.GraphData:
+    """A GraphData from: None (the standalone RV32IM core shipped with the package), a path, a
+    GraphData, or a live chipformer graph (exported on the fly)."""
+    if c is None:
+        return graphfile.load_graph(graphfile.default_graph_path())
+    if isinstance(c, graphfile.GraphData):
+        return c
+    if isinstance(c, (str, Path)):
+        return graphfile.load_graph(c)
+    return graphfile.export_graph(c)
+
+
+def plan_for(g: graphfile.GraphData):
+    key = id(g)
+    if key not in _plans:
+        _plans[key] = (g, compile_plan(g))
+    return _plans[key][1]
+
+
+def program_image(prog, keep: list) -> Machine:
+    """A qx_machine for a freshly loaded program (ref.Machine.from_program, ERV/chipformer/rv/
+    ref.py:401-414): text at 0x40000, data at data_base, rodata at 0x20000, sp = 0x8000."""
+    text = np.ascontiguousarray(np.asarray(prog.text, np.uint32))
+    ram = np.zeros(8192 * 4, np.uint8)
+    data = np.frombuffer(bytes(prog.data), np.uint8)
+    ram[prog.data_base:prog.data_base + len(data)] = data[:max(0, 8192 * 4 - prog.data_base)]
+    ramw = ram.view(np.uint32).copy()
+    rod = np.frombuffer(bytes(getattr(prog, "rodata", b"")) or b"\0", np.uint8).copy()
+    keep += [text, ramw, rod]
+    m = Machine()
+    m.rom, m.rom_words = text.ctypes.data, len(text)
+    m.drom, m.drom_bytes = rod.ctypes.data, len(getattr(prog, "rodata", b""))
+    m.ram = ramw.ctypes.data
+    m.x[2] = 0x8000
+    m.anchor = (prog.entry - 0x40000) >> 2
+    m.n = 0
+    m.bn = None
+    return m
+
+
+class Executor:
+    """Executor2's surface (tritonexec.py:173-289) on the B200 kernel."""
+
+    def __init__(self, c=None, batch: int = 1, device="cuda"):
+        torch = _torch()
+        self.g = load_graph(c)
+        self.c = c
+        self.plan = plan_for(self.g)
+        self.B = int(batch)
+        self.dev = torch.device(device)
+        if self.dev.index is None:
+            self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.D = int(self.g.D)
+        blob = self.plan.blob()
+        self._blob = C.create_string_buffer(blob, len(blob))
+        h = C.c_void_p()
+        with torch.cuda.device(self.dev):
+            check(lib().qx_create(self._blob, C.c_size_t(len(blob)), C.c_int32(self.B),
+                                  C.c_int32(self.dev.index), C.byref(h)), "qx_create")
+        self.h = h
+        self.x = self._buffer(0, 0, (self.B, self.D), "<f4")
+        self.err = self._buffer(3, 0, (self.B,), "<u4")
+        self.hash = self._buffer(4, 0, (self.B,), "<u8")
+        self.count = self._buffer(5, 0, (self.B,), "<i8")
+        self.halt_at = self._buffer(6, 0, (self.B,), "<i8")
+        self.state_bytes = self._buffer(7, 0, (1,), "<u8")
+        self.y = torch.zeros(self.B, self.D, device=self.dev)  # Executor2.y (unused here)
+        self.steps, self.hist_dims = [], []
+        hl = 0
+        for lv, kind in zip(self.g.levels, self.g.level_kind):
+            if kind == 0:
+                self.steps.append({"kind": "ffn", "level": int(lv)})
+                continue
+            V = len(self.g.vheads_at(int(lv)))
+            ne = max(1, len(self.plan.lag_dims[int(lv)]))
+            bpad = (self.B + 31) // 32 * 32
+            S = self._buffer(1, hl, (self.B, V, HD, HD), "<f4")
+            H = self._buffer(2, hl, (3, ne, bpad), "<f4").permute(2, 0, 1)[:self.B]
+            self.steps.append({"kind": "head", "level": int(lv), "V": V, "S": S, "hist": H,
+                               "heads": [str(self.g.head_name[h]) for h in self.g.heads_at(int(lv))]})
+            self.hist_dims.append(self.plan.lag_dims[int(lv)])
+            hl += 1
+        self.feat_ids = [int(d) for d in self.g.feat_dims[1:]]
+
+    def _buffer(self, kind: int, i: int, shape, typestr: str):
+        torch = _torch()
+        p, n = C.c_void_p(), C.c_size_t()
+        check(lib().qx_buffer(self.h, C.c_int32(kind), C.c_int32(i), C.byref(p), C.byref(n)),
+              "qx_buffer")
+        return torch.as_tensor(_DevArray(p.value, shape, typestr), device=self.dev)
+
+    def __del__(self):
+        h = getattr(self, "h", None)
+        if h is not None and _lib is not None:
+            _lib.qx_destroy(h)
+            self.h = None
+
+    def _stream(self):
+        torch = _torch()
+        return C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+
+    # ---- Executor2 surface -----------------------------------------------------------------
+    def load_init(self, row: int = 0):
+        """The heads' initial states of the live graph (the snapshot it now holds) into batch
+        row ``row`` (tritonexec.py:246-258).  Needs the executor built from a live graph."""
+        torch = _torch()
+        if self.c is None or isinstance(self.c, (str, Path, graphfile.GraphData)):
+            raise QxError("load_init reads the live graph's Head.init; use load_machines instead")
+        from chipformer.q35.ir import Head
+
+        for st in self.steps:
+            if st["kind"] != "head":
+                continue
+            buf = np.zeros((st["V"], HD, HD), np.float32)
+            j = 0
+            for n in [n for n in self.c.nodes if n.level == st["level"] and isinstance(n, Head)]:
+                init = n.init or []
+                for x in range(len(n.vheads())):
+                    for r, vec in (init[x] if x < len(init) else {}).items():
+                        buf[j, r] = vec
+                    j += 1
+            st["S"][row].copy_(torch.from_numpy(buf))
+
+    def reset(self, rows=None):
+        """Fresh lag histories for the rows (tritonexec.py:260-263)."""
+        if rows is None:
+            check(lib().qx_reset(self.h, 0, self.B, self._stream()), "qx_reset")
+            return
+        for r in ([rows] if isinstance(rows, int) else list(rows)):
+            check(lib().qx_reset(self.h, int(r), 1, self._stream()), "qx_reset")
+
+    def embed(self, toks):
+        """[n, D] fp32 embeddings on the device (tritonexec.py:265-270)."""
+        torch = _torch()
+        return torch.from_numpy(self.g.embed([int(t) for t in toks])).to(self.dev)
+
+    def step(self, x):
+        """One position for every row: x [B, D] fp32 (the embeddings in) becomes the residual
+        after every node, in place (tritonexec.py:272-289)."""
+        assert x.dtype == _torch().float32 and x.is_contiguous() and tuple(x.shape) == (self.B, self.D)
+        check(lib().qx_step(self.h, C.c_void_p(x.data_ptr()), self._stream()), "qx_step")
+        return x
+
+    # ---- machine images / state ------------------------------------------------------------
+    def load_machines(self, row0: int, programs) -> None:
+        """core.snapshot + load_init of fresh program images into rows row0.. (on the device)."""
+        keep: list = []
+        imgs = (Machine * len(programs))(*[program_image(p, keep) for p in programs])
+        check(lib().qx_load_machines(self.h, C.c_int32(row0), C.c_int32(len(programs)), imgs,
+                                     self._stream()), "qx_load_machines")
+
+    def readback(self, row: int) -> State:
+        st = State()
+        check(lib().qx_readback(self.h, C.c_int32(row), C.byref(st), self._stream()), "qx_readback")
+        return st
+
+    def checksums(self):
+        """[B] uint64 (as int64 tensor) FNV-1a 64 state checksums, on the device."""
+        torch = _torch()
+        out = torch.empty(self.B, dtype=torch.int64, device=self.dev)
+        check(lib().qx_checksums(self.h, C.c_void_p(out.data_ptr()), self._stream()), "qx_checksums")
+        return out
+
+    def errors(self) -> int:
+        v = C.c_uint32()
+        check(lib().qx_errors(self.h, C.byref(v), self._stream()), "qx_errors")
+        return int(v.value)
+
+    # ---- free running ----------------------------------------------------------------------
+    def set_tokens(self, row0: int, toks) -> None:
+        t = np.ascontiguousarray(np.asarray(toks, np.int32))
+        check(lib().qx_set_tokens(self.h, C.c_int32(row0), C.c_int32(len(t)),
+                                  t.ctypes.data_as(C.POINTER(C.c_int32)), self._stream()),
+              "qx_set_tokens")
+
+    def run(self, n_tokens: int, tokens=None) -> None:
+        """n_tokens free-running steps of every row (tokens: a [n_tokens, B] int32 CUDA tensor
+        receiving the generated ids, or None)."""
+        p = C.c_void_p(0 if tokens is None else tokens.data_ptr())
+        if tokens is not None:
+            assert tokens.dtype == _torch().int32 and tuple(tokens.shape) == (n_tokens, self.B)
+        check(lib().qx_run(self.h, C.c_int32(n_tokens), p, self._stream()), "qx_run")
+
+
+class FreeRun:
+    """FreeRun's surface (fastexec.py:236-340): every predicted token is the next input; the
+    decode and the next embedding run inside the executor's kernel."""
+
+    def __init__(self, c=None, batch: int = 1, device="cuda"):
+        self.ex = Executor(c, batch, device)
+        self.B = batch
+
+    def load(self, row: int, first_token: int):
+        """Row ``row`` starts from the graph's current snapshot, then ``first_token``."""
+        self.ex.load_init(row)
+        self.ex.reset([row])
+        self.ex.set_tokens(row, [first_token])
+
+    def load_program(self, row: int, prog, first_token: int):
+        self.ex.load_machines(row, [prog])
+        self.ex.reset([row])
+        self.ex.set_tokens(row, [first_token])
+
+    def run(self, n_steps: int) -> np.ndarray:
+        """[B, n_steps] generated tokens."""
+        torch = _torch()
+        out = torch.zeros(n_steps, self.B, dtype=torch.int32, device=self.ex.dev)
+        self.ex.run(n_steps, out)
+        torch.cuda.synchronize(self.ex.dev)
+        return out.cpu().numpy().T.astype(np.int64)
+
+
+def gdn_step(S, q, k, v, alpha, beta, o=None, work=None):
+    """One gated delta-rule decode step on [BH, 128, 128] fp32 states (in place); returns o."""
+    torch = _torch()
+    BH = S.shape[0]
+    for t in (S, q, k, v, alpha, beta):
+        assert t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+    if o is None:
+        o = torch.empty(BH, HD, device=S.device)
+    if work is None:
+        work = torch.empty(int(lib().qx_gdn_work_bytes(BH)), dtype=torch.uint8, device=S.device)
+    stream = C.c_void_p(torch.cuda.current_stream(S.device).cuda_stream)
+    check(lib().qx_gdn_step(C.c_int64(BH), *[C.c_void_p(t.data_ptr()) for t in (S, q, k, v, alpha, beta, o, work)],
+                            stream), "qx_gdn_step")
+    return o

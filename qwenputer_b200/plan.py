@@ -1,0 +1,537 @@
+"""Plan compiler: a compiled graph (graphfile.GraphData) -> the per-token program of the CUDA
+executor (the blob format of include/qx.h).
+
+The reference lowers each sublayer into CSR tables once and launches one Triton kernel per
+sublayer and machine (ERV/chipformer/rv/tritonexec.py:176-244, 272-289).  This compiler instead
+produces one program that a persistent CTA runs for 32 machines at a time (one per lane), with
+the residual stream of those machines resident in shared memory:
+
+* residual slots: every dim gets an X row only over its live range (birth .. last use), so the
+  2,679 dims fit in ~1,000 rows; rows are 33 floats (32 lanes + 1 pad: conflict-free whether a
+  warp walks machines or rows);
+* linear forms: the non-constant part of every projection is deduplicated per phase group and
+  evaluated once into a scratch row; the constant part (the ONE dim's coefficient) is applied
+  where the form is used (``F + c * x0``), so units that differ only in their threshold share
+  a form (FFN nonzeros 227k -> 57k per machine-token);
+* lag history: only (lag, dim) pairs the heads read are kept, staged into scratch rows at the
+  start of their head sublayer (the ``_lag_load`` of tritonexec.py:74-79);
+* dims both written and read inside one sublayer (``into`` outputs) are accumulated into a
+  temporary row and added at the sublayer's end, so every read sees the sublayer's input, as
+  the reference's separate output buffer guarantees (tritonexec.py:151-170).
+
+Work lists are balanced over the CTA's warps at compile time (longest-first).
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import heapq
+import struct
+from collections import defaultdict
+
+import numpy as np
+
+from .graphfile import HD, ONE, GraphData
+
+NONE = 0xFFFF
+ROW_PAD = 33
+MAGIC = 0x314E414C50585151
+VERSION = 1
+PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
+          DECODE=10, END=11)
+SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "FORMS", "NNZ", "WARP_PTR", "NODES", "UNITS",
+       "STAGES", "KHEADS", "KQ_ROW", "KQ_C", "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W",
+       "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW", "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0",
+       "EMB_BASE", "EMB_BITS", "EMB_TABLE", "TABLES", "REG_COLS"]
+TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
+               + [f"quo{i}" for i in range(4)] + [f"rom{i}" for i in range(32)]
+               + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
+               + [f"bn2.{i}" for i in range(4)] + [f"ram{i}" for i in range(32)])
+
+DT = {
+    "phase": np.dtype([("kind", "<u4"), ("a", "<u4"), ("b", "<u4"), ("c", "<u4")]),
+    "form": np.dtype([("nnz0", "<u4"), ("nnz4", "<u2"), ("dst", "<u2")]),
+    "node": np.dtype([("u0", "<u4"), ("nu", "<u2"), ("out", "<u2")]),
+    "unit": np.dtype([("coef", "<f4"), ("ca", "<f4"), ("cb", "<f4"), ("a", "<u2"), ("b", "<u2")]),
+    "stage": np.dtype([("e", "<u4"), ("x_row", "<u2"), ("ml", "<u2"), ("s0", "<u2"),
+                       ("s1", "<u2"), ("s2", "<u2"), ("pad", "<u2")]),
+    "khead": np.dtype([("chan", "<u4"), ("qhot", "<u2"), ("slot", "<u2")]),
+    "vhead": np.dtype([("hl", "<u4"), ("vh", "<u4"), ("col", "<u4"), ("slot", "<u2"),
+                       ("nrows", "<u2"), ("a_row", "<u2"), ("b_row", "<u2"), ("ca", "<f4"),
+                       ("cb", "<f4"), ("bconst", "<f4")]),
+    "colform": np.dtype([("nnz0", "<u4"), ("nnz4", "<u2"), ("live", "<u2"), ("c", "<f4")]),
+}
+HEADER = struct.Struct("<QII" + "I" * 14 + "32Q32Q")
+
+
+def _bf16_bits(w: float) -> int:
+    u = int(np.float32(w).view(np.uint32))
+    if u & 0xFFFF:
+        raise ValueError(f"weight {w!r} is not exact in bf16; the packed form format needs it")
+    return u >> 16
+
+
+@dataclasses.dataclass
+class Form:
+    """The non-constant part of a linear form: sorted ((lag, dim), weight) terms."""
+
+    terms: tuple
+
+    @property
+    def nnz(self) -> int:
+        return len(self.terms)
+
+
+def split_form(forms, i: int, D: int) -> tuple[tuple, float]:
+    """(non-constant terms, constant) of form i: the constant is the coefficient of ONE at
+    lag 0 (x0 = 1 on every chip token); lagged ONE terms stay terms."""
+    idx, w = forms.row(i)
+    const = 0.0
+    terms = []
+    for k, v in zip(idx.tolist(), w.tolist()):
+        lag, d = divmod(k, D)
+        if lag == 0 and d == ONE:
+            const += v
+        else:
+            terms.append(((lag, d), v))
+    return tuple(sorted(terms)), float(np.float32(const))
+
+
+class Plan:
+    """The compiled program (numpy arrays per section) and its statistics."""
+
+    def __init__(self):
+        self.sec: dict[str, np.ndarray] = {}
+        self.hdr: dict[str, int] = {}
+        self.stats: dict[str, float] = {}
+
+    def blob(self) -> bytes:
+        offs, cnts, parts = [0] * 32, [0] * 32, []
+        pos = HEADER.size
+        pos = (pos + 255) // 256 * 256
+        for i, name in enumerate(SEC):
+            a = np.ascontiguousarray(self.sec[name])
+            offs[i], cnts[i] = pos, len(a)
+            b = a.tobytes()
+            parts.append((pos, b))
+            pos = (pos + len(b) + 255) // 256 * 256
+        h = self.hdr
+        head = HEADER.pack(MAGIC, VERSION, h["D"], h["n_slots"], h["n_scratch"], h["nw"],
+                           h["n_head_levels"], h["one_row"], h["n_ksel_slots"], h["qhot_max"],
+                           h["n_fam"], h["n_pay"], h["n_feat"], h["n_emb_rows"], h["n_families"],
+                           h["vocab"], h["n_born0"], *offs, *cnts)
+        out = bytearray(pos)
+        out[:len(head)] = head
+        for p, b in parts:
+            out[p:p + len(b)] = b
+        return bytes(out)
+
+
+SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
+
+
+def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
+                 ksel_slots: int = 16) -> Plan:
+    qhot = int(g.head_qhot.max())
+    if smem_rows is None:  # rows of 33 floats left after the key-select and decode areas
+        smem_rows = (SMEM_MAX - ksel_slots * 32 * (1 + qhot) * 4 - 32 * 18 * 4 - 64) // (ROW_PAD * 4)
+    D = g.D
+    levels = [int(x) for x in g.levels]
+    kinds = [int(k) for k in g.level_kind]
+    head_levels = [lv for lv, k in zip(levels, kinds) if k == 1]
+    hl_index = {lv: i for i, lv in enumerate(head_levels)}
+    INF = 10 ** 9
+
+    # ---- per level: forms (non-constant parts + constants), reads, writes ---------------------
+    ffn_nodes = defaultdict(list)
+    for n in range(len(g.ffn_level)):
+        ffn_nodes[int(g.ffn_level[n])].append(n)
+    unit_a = [split_form(g.unit_a, u, D) for u in range(g.unit_a.n)]
+    unit_b = [split_form(g.unit_b, u, D) for u in range(g.unit_b.n)]
+    qf = [split_form(g.q_forms, i, D) for i in range(g.q_forms.n)]
+    kf = [split_form(g.k_forms, i, D) for i in range(g.k_forms.n)]
+    vf = [split_form(g.v_forms, i, D) for i in range(g.v_forms.n)]
+    zf = [split_form(g.z_forms, i, D) for i in range(g.z_forms.n)]
+    af = [split_form(g.vh_a, i, D) for i in range(g.vh_a.n)]
+    bf = [split_form(g.vh_beta, i, D) for i in range(g.vh_beta.n)]
+
+    reads = defaultdict(set)  # level -> {(lag, dim)}
+    writes = defaultdict(set)  # level -> {dim}
+    for lv in levels:
+        for n in ffn_nodes.get(lv, []):
+            writes[lv].add(int(g.ffn_out[n]))
+            for u in range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1])):
+                for t, _ in unit_a[u][0] + unit_b[u][0]:
+                    reads[lv].add(t)
+        for h in g.heads_at(lv):
+            for c in range(HD):
+                for tab, fs in ((g.head_q, qf), (g.head_k, kf)):
+                    if tab[h, c] >= 0:
+                        for t, _ in fs[tab[h, c]][0]:
+                            reads[lv].add(t)
+            for j in g.vheads_of(h):
+                for c in range(HD):
+                    for tab, fs in ((g.vh_v, vf), (g.vh_z, zf)):
+                        if tab[j, c] >= 0:
+                            for t, _ in fs[tab[j, c]][0]:
+                                reads[lv].add(t)
+                for t, _ in af[j][0] + bf[j][0]:
+                    reads[lv].add(t)
+                for e in range(int(g.vh_out_ptr[j]), int(g.vh_out_ptr[j + 1])):
+                    writes[lv].add(int(g.out_dim[e]))
+
+    # ---- liveness and residual slots ----------------------------------------------------------
+    feat = [int(d) for d in g.feat_dims]
+    birth, last = {}, {}
+    for d in feat:
+        birth[d] = 0
+        last[d] = 0
+    for lv in levels:
+        for d in writes[lv]:
+            birth[d] = min(birth.get(d, INF), lv)
+            last[d] = max(last.get(d, 0), lv)
+    for lv in levels:
+        for lag, d in reads[lv]:
+            # a dim read before its first write holds its input value (0) until then
+            birth[d] = min(birth.get(d, INF), lv)
+            last[d] = max(last.get(d, 0), lv)
+    for d in list(g.fam_dims) + list(g.pay_dims) + [ONE]:
+        birth.setdefault(int(d), 0)
+        last[int(d)] = INF
+    last_write = {}
+    for lv in levels:
+        for d in writes[lv]:
+            last_write[d] = lv
+    # dims written and read (lag 0) in the same sublayer accumulate into a temporary row
+    temps = {}  # (level, dim) -> pseudo id
+    for lv in levels:
+        for d in sorted(writes[lv] & {dd for lag, dd in reads[lv] if lag == 0}):
+            key = ("T", lv, d)
+            temps[(lv, d)] = key
+            birth[key] = lv
+            last[key] = lv
+    items = sorted(birth, key=lambda k: (birth[k], str(k)))
+    slot = {}
+    free: list[int] = []
+    active: list[tuple[int, int]] = []
+    n_slots = 0
+    for k in items:
+        b = birth[k]
+        while active and active[0][0] < b:
+            _, s = heapq.heappop(active)
+            heapq.heappush(free, s)
+        if free:
+            s = heapq.heappop(free)
+        else:
+            s, n_slots = n_slots, n_slots + 1
+        slot[k] = s
+        heapq.heappush(active, (last[k], s))
+    n_scratch = smem_rows - n_slots
+    assert n_scratch >= 64, f"{n_slots} residual slots leave too little scratch"
+    # scratch rows of a sublayer: every row no live dim occupies there
+    occupied = defaultdict(set)
+    for k in items:
+        for lv in levels:
+            if birth[k] <= lv <= last[k]:
+                occupied[lv].add(slot[k])
+    free_rows = {lv: [r for r in range(smem_rows) if r not in occupied[lv]] for lv in levels}
+
+    # ---- builders -----------------------------------------------------------------------------
+    rows_l: list[int] = []
+    pairs_l: list[tuple[int, int]] = []
+    forms_l, nnz_l, warp_ptr_l = [], [], []
+    nodes_l, units_l, stages_l, kheads_l, kq_row_l, kq_c_l = [], [], [], [], [], []
+    vheads_l, vform_l, zform_l, out_row_l, out_w_l = [], [], [], [], []
+    stats = defaultdict(float)
+
+    def pack_terms(terms, rowmap) -> tuple[int, int]:
+        """Append the packed entries of a term list (padded to a multiple of 4)."""
+        start = len(nnz_l)
+        for t, w in terms:
+            nnz_l.append(rowmap(t) | _bf16_bits(w) << 16)
+        while (len(nnz_l) - start) % 4:
+            nnz_l.append(0)  # row 0, weight +0
+        return start, (len(nnz_l) - start) // 4
+
+    def balance(costs: list[float]) -> tuple[list[int], list[int]]:
+        """Longest-first assignment of items to nw warps: (item order, warp_ptr offsets)."""
+        loads = [(0.0, w) for w in range(nw)]
+        heapq.heapify(loads)
+        per = [[] for _ in range(nw)]
+        for i in sorted(range(len(costs)), key=lambda i: -costs[i]):
+            ld, w = heapq.heappop(loads)
+            per[w].append(i)
+            heapq.heappush(loads, (ld + costs[i], w))
+        order, ptr = [], [0]
+        for w in range(nw):
+            order += per[w]
+            ptr.append(len(order))
+        stats["imbalance_max"] = max(stats["imbalance_max"], max(l for l, _ in loads)
+                                     / max(1e-9, sum(costs) / nw))
+        return order, ptr
+
+    def forms_phase(form_list: list[Form], dst_rows: list[int], rowmap, prog):
+        costs = [4 * ((f.nnz + 3) // 4) + 6 for f in form_list]
+        order, ptr = balance(costs)
+        f0 = len(forms_l)
+        for i in order:
+            s, n4 = pack_terms(form_list[i].terms, rowmap)
+            forms_l.append((s, n4, dst_rows[i]))
+            stats["form_nnz"] += form_list[i].nnz
+        wp = len(warp_ptr_l)
+        warp_ptr_l.extend(f0 + p for p in ptr)
+        prog.append((PH["FORMS"], f0, len(forms_l), wp))
+
+    def xrow(lv, d):
+        return slot[temps[(lv, d)]] if (lv, d) in temps else slot[d]
+
+    run_prog: list[tuple] = []
+    step_prog: list[tuple] = []
+    hl_ne = []
+    group_stats = []
+
+    # prologue / epilogue of run mode: the birth-0 dims (features and ONE from x; the rest 0)
+    born0 = sorted(k for k in birth if birth[k] == 0 and not isinstance(k, tuple))
+    never_written_0 = [d for d in born0 if d not in set(feat) and d not in last_write]
+    r0 = len(rows_l)
+    rows_l.extend(slot[d] for d in never_written_0)
+    if never_written_0:
+        run_prog.append((PH["ZERO"], r0, len(never_written_0), 0))
+    assert not pairs_l  # the run-mode prologue / epilogue are PAIRS[0 : n_born0]
+    pairs_l.extend((slot[d], d) for d in born0)
+    step_prog.append((PH["LOADX"], 0, len(born0), 0))
+
+    for lv, kind in zip(levels, kinds):
+        born = sorted(d for d in birth if not isinstance(d, tuple) and birth[d] == lv and lv > 0)
+        tmp = sorted(slot[k] for (l2, d), k in temps.items() if l2 == lv)
+        r0 = len(rows_l)
+        rows_l.extend(slot[d] for d in born)
+        rows_l.extend(tmp)
+        if born or tmp:
+            run_prog.append((PH["ZERO"], r0, len(born) + len(tmp), 0))
+        if tmp:
+            r1 = r0 + len(born)
+            step_prog.append((PH["ZERO"], r1, len(tmp), 0))
+        if born:
+            p0 = len(pairs_l)
+            pairs_l.extend((slot[d], d) for d in born)
+            step_prog.append((PH["LOADX"], p0, len(born), 0))
+        body: list[tuple] = []
+        free = free_rows[lv]
+        if kind == 0:
+            # ---------- FFN sublayer: groups of nodes whose distinct forms fit the scratch ----
+            nodes = ffn_nodes[lv]
+            groups, cur, cur_forms = [], [], {}
+            for n in nodes:
+                nf = {}
+                for u in range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1])):
+                    for fm in (unit_a[u][0], unit_b[u][0]):
+                        if fm:
+                            nf[fm] = 1
+                new = [f for f in nf if f not in cur_forms]
+                if cur and len(cur_forms) + len(new) > len(free):
+                    groups.append((cur, cur_forms))
+                    cur, cur_forms = [], {}
+                    new = list(nf)
+                cur.append(n)
+                for f in new:
+                    cur_forms[f] = len(cur_forms)
+            if cur:
+                groups.append((cur, cur_forms))
+            for gnodes, gforms in groups:
+                assert len(gforms) <= len(free), f"sublayer {lv}: a node needs too many forms"
+                flist = [Form(f) for f in gforms]
+                dst = [free[i] for i in range(len(flist))]
+                forms_phase(flist, dst, lambda t: slot[t[1]], body)
+                frow = {f: free[i] for f, i in gforms.items()}
+                costs, nd = [], []
+                for n in gnodes:
+                    us = range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1]))
+                    costs.append(3 * len(us) + 4)
+                    nd.append(n)
+                order, ptr = balance(costs)
+                n0 = len(nodes_l)
+                for i in order:
+                    n = nd[i]
+                    u0 = len(units_l)
+                    for u in range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1])):
+                        (ta, ca), (tb, cb) = unit_a[u], unit_b[u]
+                        units_l.append((float(g.unit_coef[u]), ca, cb,
+                                        frow[ta] if ta else NONE, frow[tb] if tb else NONE))
+                    nodes_l.append((u0, len(units_l) - u0, xrow(lv, int(g.ffn_out[n]))))
+                    stats["units"] += len(units_l) - u0
+                wp = len(warp_ptr_l)
+                warp_ptr_l.extend(n0 + p for p in ptr)
+                body.append((PH["UNITS"], n0, len(nodes_l), wp))
+            group_stats.append((lv, "ffn", len(groups)))
+        else:
+            # ---------- head sublayer ---------------------------------------------------------
+            hi = hl_index[lv]
+            lag_pairs = sorted({t for t in reads[lv] if t[0] > 0})
+            lag_dims = sorted({d for _, d in lag_pairs})
+            stage_row = {t: free[i] for i, t in enumerate(lag_pairs)}
+            hl_ne.append(len(lag_dims))
+            if lag_dims:
+                s0 = len(stages_l)
+                for e, d in enumerate(lag_dims):
+                    ml = max(lag for lag, dd in lag_pairs if dd == d)
+                    st = [stage_row.get((lag, d), NONE) for lag in (1, 2, 3)]
+                    stages_l.append((e, slot[d], ml, *st, 0))
+                body.append((PH["STAGE"], s0, len(lag_dims), hi))
+            ffree = free[len(lag_pairs):]
+            cap = len(ffree)
+
+            def rowmap(t, lv=lv):
+                return slot[t[1]] if t[0] == 0 else stage_row[t]
+
+            heads = g.heads_at(lv)
+            vhs_level = g.vheads_at(lv)
+            groups, cur, cur_forms = [], [], {}
+            for h in heads:
+                nf = {}
+                for c in range(HD):
+                    for tab, fs in ((g.head_k, kf), (g.head_q, qf)):
+                        if tab[h, c] >= 0 and fs[tab[h, c]][0]:
+                            nf[fs[tab[h, c]][0]] = 1
+                for j in g.vheads_of(h):
+                    for fs in (af, bf):
+                        if fs[j][0]:
+                            nf[fs[j][0]] = 1
+                new = [f for f in nf if f not in cur_forms]
+                if cur and (len(cur_forms) + len(new) > cap or len(cur) >= ksel_slots):
+                    groups.append((cur, cur_forms))
+                    cur, cur_forms = [], {}
+                    new = list(nf)
+                cur.append(h)
+                for f in new:
+                    cur_forms[f] = len(cur_forms)
+            if cur:
+                groups.append((cur, cur_forms))
+            for gheads, gforms in groups:
+                assert len(gforms) <= cap, f"sublayer {lv}: a key head needs too many forms"
+                flist = [Form(f) for f in gforms]
+                frow = {f: ffree[i] for f, i in gforms.items()}
+                if flist:
+                    forms_phase(flist, [ffree[i] for i in range(len(flist))], rowmap, body)
+                k0 = len(kheads_l)
+                for sl, h in enumerate(gheads):
+                    kheads_l.append((len(kq_row_l), int(g.head_qhot[h]), sl))
+                    for tab, fs in ((g.head_k, kf), (g.head_q, qf)):
+                        for c in range(HD):
+                            if tab[h, c] >= 0:
+                                t, cc = fs[tab[h, c]]
+                                kq_row_l.append(frow[t] if t else NONE)
+                                kq_c_l.append(cc)
+                            else:
+                                kq_row_l.append(NONE)
+                                kq_c_l.append(0.0)
+                body.append((PH["KSEL"], k0, len(kheads_l), 0))
+                v0 = len(vheads_l)
+                for sl, h in enumerate(gheads):
+                    for j in g.vheads_of(h):
+                        col = len(out_row_l)
+                        for c in range(HD):
+                            for tab, fs, dstl in ((g.vh_v, vf, vform_l), (g.vh_z, zf, zform_l)):
+                                if tab[j, c] >= 0:
+                                    t, cc = fs[tab[j, c]]
+                                    s, n4 = pack_terms(t, rowmap) if t else (0, 0)
+                                    dstl.append((s, n4, 1, cc))
+                                else:
+                                    dstl.append((0, 0, 0, 0.0))
+                        orow = [NONE] * HD
+                        ow = [0.0] * HD
+                        for e in range(int(g.vh_out_ptr[j]), int(g.vh_out_ptr[j + 1])):
+                            c = int(g.out_col[e])
+                            if float(g.out_w[e]) != 0.0:
+                                orow[c] = xrow(lv, int(g.out_dim[e]))
+                                ow[c] = float(g.out_w[e])
+                        out_row_l.extend(orow)
+                        out_w_l.extend(ow)
+                        ta, ca = af[j]
+                        tb, cb = bf[j]
+                        vheads_l.append((hi, vhs_level.index(j), col, sl, int(g.vh_nrows[j]),
+                                         frow[ta] if ta else NONE, frow[tb] if tb else NONE,
+                                         ca, cb, 0.0 if g.vh_has_beta[j] else 1.0))
+                body.append((PH["VH"], v0, len(vheads_l), 0))
+            group_stats.append((lv, "head", len(groups)))
+        apply_pairs = [(slot[d], slot[k]) for (l2, d), k in temps.items() if l2 == lv]
+        tail = []
+        if apply_pairs:
+            p0 = len(pairs_l)
+            pairs_l.extend(apply_pairs)
+            tail.append((PH["APPLY"], p0, len(apply_pairs), 0))
+        run_prog += body + tail
+        step_prog += body + tail
+        wo = sorted(d for d, l2 in last_write.items() if l2 == lv)
+        if wo:
+            p0 = len(pairs_l)
+            pairs_l.extend((slot[d], d) for d in wo)
+            step_prog.append((PH["WRITEOUT"], p0, len(wo), 0))
+    run_prog.append((PH["DECODE"], 0, 0, 0))
+    run_prog.append((PH["END"], 0, 0, 0))
+    step_prog.append((PH["END"], 0, 0, 0))
+
+    # ---- sections -----------------------------------------------------------------------------
+    def arr(lst, dt):
+        if isinstance(dt, str):
+            dt = DT[dt]
+        a = np.zeros(len(lst), dt)
+        for i, v in enumerate(lst):
+            a[i] = v
+        return a
+
+    P = Plan()
+    s = P.sec
+    s["RUN_PROG"] = arr(run_prog, "phase")
+    s["STEP_PROG"] = arr(step_prog, "phase")
+    s["ROWS"] = np.asarray(rows_l or [0], np.uint16)
+    s["PAIRS"] = np.asarray(pairs_l or [(0, 0)], np.uint32).reshape(-1, 2)
+    s["FORMS"] = arr(forms_l, "form") if forms_l else np.zeros(1, DT["form"])
+    s["NNZ"] = np.asarray(nnz_l or [0], np.uint32)
+    s["WARP_PTR"] = np.asarray(warp_ptr_l or [0], np.uint32)
+    s["NODES"] = arr(nodes_l, "node") if nodes_l else np.zeros(1, DT["node"])
+    s["UNITS"] = arr(units_l, "unit") if units_l else np.zeros(1, DT["unit"])
+    s["STAGES"] = arr(stages_l, "stage") if stages_l else np.zeros(1, DT["stage"])
+    s["KHEADS"] = arr(kheads_l, "khead")
+    s["KQ_ROW"] = np.asarray(kq_row_l, np.uint16)
+    s["KQ_C"] = np.asarray(kq_c_l, np.float32)
+    s["VHEADS"] = arr(vheads_l, "vhead")
+    s["VFORM"] = arr(vform_l, "colform")
+    s["ZFORM"] = arr(zform_l, "colform")
+    s["OUT_ROW"] = np.asarray(out_row_l, np.uint16)
+    s["OUT_W"] = np.asarray(out_w_l, np.float32)
+    s["HL_V"] = np.asarray([len(g.vheads_at(lv)) for lv in head_levels], np.uint32)
+    s["HL_NE"] = np.asarray([max(1, n) for n in hl_ne], np.uint32)
+    s["FAM_ROW"] = np.asarray([slot[int(d)] for d in g.fam_dims], np.uint16)
+    s["PAY_ROW"] = np.asarray([slot[int(d)] for d in g.pay_dims], np.uint16)
+    s["FEAT_ROW"] = np.asarray([slot[d] for d in feat], np.uint16)
+    s["FAM_IDS"] = np.asarray(g.fam_ids, np.int32)
+    s["FAM_SIZE"] = np.asarray(g.fam_size, np.int32)
+    s["FAM_ROW0"] = np.asarray([int(r) if sm else -1 for r, sm in zip(g.fam_row0, g.fam_small)],
+                               np.int32)
+    s["EMB_BASE"] = np.ascontiguousarray(g.emb_base, np.float32).reshape(-1)
+    s["EMB_BITS"] = np.ascontiguousarray(g.emb_bits, np.float32).reshape(-1)
+    s["EMB_TABLE"] = np.ascontiguousarray(g.emb_table, np.float32).reshape(-1)
+    tabs = []
+    for name in TABLE_ORDER:
+        lv, vh0, _ = g.table_position(name)
+        tabs.append((hl_index[lv], vh0))
+    s["TABLES"] = np.asarray(tabs, np.uint32).reshape(-1)
+    s["REG_COLS"] = np.asarray(g.reg_cols, np.int32).reshape(-1)
+    P.hdr = dict(D=D, n_slots=n_slots, n_scratch=n_scratch, nw=nw, n_head_levels=len(head_levels),
+                 one_row=slot[ONE], n_ksel_slots=ksel_slots, qhot_max=int(g.head_qhot.max()),
+                 n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
+                 n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
+                 vocab=int(g.vocab), n_born0=len(born0))
+    stats["n_slots"] = n_slots
+    stats["n_scratch"] = n_scratch
+    stats["phases_run"] = len(run_prog)
+    stats["vform_nnz"] = sum(n4 * 4 for _, n4, _, _ in vform_l)
+    stats["zform_nnz"] = sum(n4 * 4 for _, n4, _, _ in zform_l)
+    stats["weight_bytes"] = sum(a.nbytes for k, a in s.items() if not k.startswith("EMB"))
+    stats["groups"] = group_stats
+    P.stats = dict(stats)
+    P.slot = slot
+    P.head_levels = head_levels
+    P.lag_dims = {lv: sorted({d for lag, d in reads[lv] if lag > 0}) for lv in head_levels}
+    return P

@@ -222,7 +222,11 @@ def gen_program(seed: int, n_instr: int = 512, iters: int = 50, data_bytes: int 
                             rng.choice(OPERANDS)))
             body += 1 + n_skip
     emit(addi(S0, S0, -1))
-    emit(bne(S0, X0, 4 * (loop - len(text))))
+    if -4096 <= 4 * (loop - len(text)):
+        emit(bne(S0, X0, 4 * (loop - len(text))))
+    else:  # a body longer than a branch reaches: skip a backward JAL on exit
+        emit(beq(S0, X0, 8))
+        emit(jal(X0, 4 * (loop - len(text))))
     emit(li(A0, 0))
     emit(li(A7, 93))
     emit(ecall())

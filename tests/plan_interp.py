@@ -1,0 +1,140 @@
+"""A numpy interpreter of the executor's phase program (test infrastructure): runs a compiled
+plan exactly as the CUDA kernel's phases describe it, on the CPU, so the plan compiler can be
+checked against the oracle without a GPU."""
+
+import numpy as np
+
+from qwenputer_b200.plan import PH
+
+NONE = 0xFFFF
+
+
+def _f32(x):
+    return np.float32(x)
+
+
+class PlanInterp:
+    def __init__(self, P, B: int):
+        self.P, self.B = P, B
+        s = P.sec
+        self.s = s
+        h = P.hdr
+        self.rows = h["n_slots"] + h["n_scratch"]
+        self.X = np.zeros((self.rows, B), np.float32)
+        self.hl_v = s["HL_V"]
+        self.S = [np.zeros((B, int(v), 128, 128), np.float32) for v in s["HL_V"]]
+        self.H = [np.zeros((3, int(ne), B), np.float32) for ne in s["HL_NE"]]
+        self.one = h["one_row"]
+
+    def form(self, nnz0, nnz4, m=slice(None)):
+        e = self.s["NNZ"][nnz0:nnz0 + 4 * nnz4]
+        rows = (e & 0xFFFF).astype(np.int64)
+        w = (e & 0xFFFF0000).view(np.float32)
+        acc = np.zeros(self.X[0, m].shape, np.float32)
+        for r, ww in zip(rows, w):
+            acc = acc + ww * self.X[r, m]
+        return acc
+
+    def row(self, r, m=slice(None)):
+        return np.zeros(self.X[0, m].shape, np.float32) if r == NONE else self.X[r, m]
+
+    def step(self, x: np.ndarray) -> np.ndarray:
+        """Step mode on x [B, D] (in place)."""
+        s = self.s
+        for ph in s["STEP_PROG"]:
+            k, a, b, c = (int(ph[f]) for f in ("kind", "a", "b", "c"))
+            if k == PH["END"]:
+                break
+            if k == PH["ZERO"]:
+                for i in range(b):
+                    self.X[s["ROWS"][a + i]] = 0
+            elif k == PH["LOADX"]:
+                for r, d in s["PAIRS"][a:a + b]:
+                    self.X[r] = x[:, d]
+            elif k == PH["WRITEOUT"]:
+                for r, d in s["PAIRS"][a:a + b]:
+                    x[:, d] = self.X[r]
+            elif k == PH["APPLY"]:
+                for dst, src in s["PAIRS"][a:a + b]:
+                    self.X[dst] = self.X[dst] + self.X[src]
+            elif k == PH["STAGE"]:
+                H = self.H[c]
+                for st in s["STAGES"][a:a + b]:
+                    e, xr, ml = int(st["e"]), int(st["x_row"]), int(st["ml"])
+                    h = H[:, e].copy()
+                    for lag, key in enumerate(("s0", "s1", "s2")):
+                        if st[key] != NONE:
+                            self.X[st[key]] = h[lag]
+                    H[0, e] = self.X[xr]
+                    if ml >= 2:
+                        H[1, e] = h[0]
+                    if ml >= 3:
+                        H[2, e] = h[1]
+            elif k == PH["FORMS"]:
+                for f in s["FORMS"][a:b]:
+                    self.X[f["dst"]] = self.form(int(f["nnz0"]), int(f["nnz4"]))
+            elif k == PH["UNITS"]:
+                x0 = self.X[self.one]
+                for nd in s["NODES"][a:b]:
+                    acc = np.zeros(self.B, np.float32)
+                    for u in s["UNITS"][nd["u0"]:nd["u0"] + nd["nu"]]:
+                        av = self.row(u["a"]) + u["ca"] * x0
+                        bv = self.row(u["b"]) + u["cb"] * x0
+                        acc = acc + (u["coef"] * av) * np.maximum(bv, 0)
+                    self.X[nd["out"]] = self.X[nd["out"]] + acc
+            elif k == PH["KSEL"]:
+                self.ksel, self.qsel = {}, {}
+                x0 = self.X[self.one]
+                for kh in s["KHEADS"][a:b]:
+                    ch = int(kh["chan"])
+                    kr, qr = s["KQ_ROW"][ch:ch + 128], s["KQ_ROW"][ch + 128:ch + 256]
+                    kc, qc = s["KQ_C"][ch:ch + 128], s["KQ_C"][ch + 128:ch + 256]
+                    kv = np.stack([np.maximum(self.row(int(r)) + cc * x0, 0) for r, cc in zip(kr, kc)])
+                    qv = np.stack([np.maximum(self.row(int(r)) + cc * x0, 0) for r, cc in zip(qr, qc)])
+                    km, ka = kv.max(0), kv.argmax(0)
+                    self.ksel[int(kh["slot"])] = np.where(km > 0, ka, -1)
+                    sel = []
+                    for j in range(int(kh["qhot"])):
+                        qm, qa = qv.max(0), qv.argmax(0)
+                        sel.append(np.where(qm > 0, qa, -1))
+                        qv[qa, np.arange(self.B)] = 0
+                    self.qsel[int(kh["slot"])] = sel
+            elif k == PH["VH"]:
+                x0 = self.X[self.one]
+                for vh in s["VHEADS"][a:b]:
+                    hl, j, col, sl = int(vh["hl"]), int(vh["vh"]), int(vh["col"]), int(vh["slot"])
+                    for m in range(self.B):
+                        Sb = self.S[hl][m, j]
+                        if vh["nrows"]:
+                            av = self.row(int(vh["a_row"]), m) + vh["ca"] * x0[m]
+                            fac = 1.0 if av == 0 else (0.5 if av == 110 else 0.0)
+                            if fac != 1.0:
+                                Sb[:vh["nrows"]] *= np.float32(fac)
+                        bv = (self.row(int(vh["b_row"]), m) + vh["cb"] * x0[m]) + vh["bconst"]
+                        kr = self.ksel[sl][m]
+                        if kr >= 0 and bv == 1.0:
+                            vals = np.zeros(128, np.float32)
+                            for cc in range(128):
+                                cf = s["VFORM"][col + cc]
+                                if cf["live"]:
+                                    vals[cc] = max(self.form(int(cf["nnz0"]), int(cf["nnz4"]), m) + cf["c"] * x0[m], 0)
+                            Sb[kr] = vals
+                        o = np.zeros(128, np.float32)
+                        anyr = False
+                        for sel in self.qsel[sl]:
+                            if sel[m] >= 0:
+                                o = o + Sb[sel[m]]
+                                anyr = True
+                        if not anyr:
+                            continue
+                        ref = np.float32(o[0] * o[0]) + np.float32(o[1] * o[1])
+                        norm = np.sqrt(np.float32(ref / np.float32(128)))
+                        for cc in range(128):
+                            orow = int(s["OUT_ROW"][col + cc])
+                            if orow == NONE:
+                                continue
+                            zf = s["ZFORM"][col + cc]
+                            z = max(self.form(int(zf["nnz0"]), int(zf["nnz4"]), m) + zf["c"] * x0[m], 0) if zf["live"] else 0
+                            out = o[cc] / norm if ref > 0 else np.float32(0)
+                            self.X[orow, m] += np.float32(out * np.float32(z)) * s["OUT_W"][col + cc]
+        return x

@@ -1,0 +1,162 @@
+"""The CUDA executor against the CPU oracle (bit-exact tokens and states; residuals equal on every
+dim, as the reference's own check compares them: tritonexec.py:292-305)."""
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def qx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from qwenputer_b200 import build
+
+    build.build()
+    from qwenputer_b200 import executor
+
+    return executor
+
+
+def _oracle_state(o, progs):
+    st = o.new_state(len(progs))
+    for r, p in enumerate(progs):
+        o.snapshot(st, r, oracle.Machine.from_program(p))
+    return st
+
+
+def test_load_machines_matches_snapshot(qx, oracle_, programs):
+    names = ["gen_base_0", "digit_file", "zba_rodata", "gen_bignum_5", "fault_ecall"]
+    progs = [programs[n]["prog"] for n in names]
+    ex = qx.Executor(None, batch=len(progs))
+    ex.load_machines(0, progs)
+    want = _oracle_state(oracle_, progs)
+    heads = [s for s in ex.steps if s["kind"] == "head"]
+    for i, st in enumerate(heads):
+        got = st["S"].cpu().numpy()
+        assert np.array_equal(got, want["S"][i]), f"head sublayer {i}"
+
+
+@pytest.mark.parametrize("batch", [1, 5, 37])
+def test_step_matches_oracle(qx, oracle_, graph, programs, batch):
+    """Teacher-forced steps: every dim of every row equals the oracle's Executor2 step."""
+    pool = ["gen_small_7", "div_fuzz_0", "mul_fuzz_1", "digit_file", "gen_base_1", "refresh_70",
+            "zba_rodata", "gen_many_11", "csr_putchar"]
+    names = [pool[i % len(pool)] for i in range(batch)]
+    progs = [programs[n]["prog"] for n in names]
+    traces = [programs[n]["trace"] for n in names]
+    ex = qx.Executor(None, batch=batch)
+    ex.load_machines(0, progs)
+    ost = _oracle_state(oracle_, progs)
+    T = 60 if batch > 8 else 120
+    for t in range(T):
+        toks = [int(tr[min(t, len(tr) - 1)]) for tr in traces]
+        emb = graph.embed(toks)
+        x = torch.from_numpy(emb).cuda()
+        ex.step(x)
+        oracle_.step(ost, emb)
+        got = x.cpu().numpy()
+        bad = np.argwhere(got != emb)
+        assert not len(bad), (t, bad[:5], got[tuple(bad[0])], emb[tuple(bad[0])])
+    for i, st in enumerate([s for s in ex.steps if s["kind"] == "head"]):
+        assert np.array_equal(st["S"].cpu().numpy(), ost["S"][i])
+    assert ex.errors() == 0
+
+
+@pytest.mark.parametrize("batch,n", [(1, 3000), (40, 1500)])
+def test_free_run_matches_machine(qx, programs, batch, n):
+    """Free-running generation: every token equals the traced machine's, and the machine state
+    read back from the heads equals the traced state after the last complete record."""
+    from qwenputer_b200 import workload
+
+    progs = [programs[k]["prog"] for k in sorted(programs)]
+    progs += workload.workload_programs("many", max(0, batch - len(progs)), 500)
+    progs = progs[:batch]
+    ex = qx.Executor(None, batch=batch)
+    ex.load_machines(0, progs)
+    ex.reset()
+    go = int(oracle.lib().qxo_tok_family(18, 0))  # GO: the seventh control after 12 families
+    ex.set_tokens(0, [go] * batch)
+    out = torch.zeros(n, batch, dtype=torch.int32, device="cuda")
+    ex.run(n, out)
+    got = out.cpu().numpy().T
+    sums = ex.checksums().cpu().numpy().view(np.uint64)
+    for r, p in enumerate(progs):
+        toks, st = oracle.Machine.from_program(p).trace_and_state(n)
+        want = toks[1:]
+        assert np.array_equal(got[r, :len(want)], want), (r, np.argmax(got[r, :len(want)] != want))
+        if len(toks) < n + 1:
+            continue  # halted: the reference machine stops there, the circuit does not
+        rb = ex.readback(r)
+        assert list(rb.x)[1:] == list(st.x)[1:], r
+        assert (rb.anchor, rb.n) == (st.anchor, st.n), r
+        assert np.array_equal(np.ctypeslib.as_array(rb.ram), np.ctypeslib.as_array(st.ram)), r
+        assert int(sums[r]) == st.checksum(), r
+    assert ex.errors() == 0
+
+
+def test_free_run_in_chunks_equals_one_run(qx, programs):
+    """Two launches of n/2 tokens generate what one launch of n does (x, lag history and head
+    states carry over between launches)."""
+    p = [programs["gen_base_2"]["prog"], programs["div_fuzz_1"]["prog"]]
+    outs = []
+    for chunks in ([800], [300, 500]):
+        ex = qx.Executor(None, batch=2)
+        ex.load_machines(0, p)
+        ex.set_tokens(0, [int(programs["gen_base_2"]["trace"][0])] * 2)
+        parts = []
+        for c in chunks:
+            o = torch.zeros(c, 2, dtype=torch.int32, device="cuda")
+            ex.run(c, o)
+            parts.append(o.cpu().numpy())
+        outs.append(np.concatenate(parts))
+    assert np.array_equal(outs[0], outs[1])
+
+
+def _gdn_case(BH, seed, general=0.05):
+    g = torch.Generator().manual_seed(seed)
+    S = torch.randint(0, 2, (BH, 128, 128), generator=g).float()
+    k = torch.zeros(BH, 128)
+    k[torch.arange(BH), torch.randint(0, 128, (BH,), generator=g)] = 1.0
+    gen = torch.rand(BH, generator=g) < general
+    kg = torch.randn(int(gen.sum()), 128, generator=g)
+    k[gen] = kg / kg.norm(dim=1, keepdim=True)
+    q = torch.zeros(BH, 128)
+    q[torch.arange(BH), torch.randint(0, 128, (BH,), generator=g)] = 1.0
+    v = torch.randint(0, 2, (BH, 128), generator=g).float()
+    u = torch.rand(BH, generator=g)
+    alpha = torch.where(u < 0.9, 1.0, torch.where(u < 0.95, 0.5, 0.0))
+    beta = torch.ones(BH)
+    return S, q, k, v, alpha, beta
+
+
+@pytest.mark.parametrize("BH,seed,general", [(512, 1, 0.05), (3000, 2, 0.05), (256, 3, 1.0), (777, 4, 0.0)])
+def test_gdn_step_matches_oracle(qx, BH, seed, general):
+    S, q, k, v, alpha, beta = _gdn_case(BH, seed, general)
+    So = S.numpy().copy()
+    o_want = oracle.gdn_step(So, q.numpy(), k.numpy(), v.numpy(), alpha.numpy(), beta.numpy())
+    Sd = S.cuda()
+    o = qx.gdn_step(Sd, q.cuda(), k.cuda(), v.cuda(), alpha.cuda(), beta.cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(Sd.cpu().numpy(), So)
+    assert np.array_equal(o.cpu().numpy(), o_want)
+
+
+def test_gdn_two_steps_and_beta(qx):
+    """Two consecutive steps with beta in {0, 1/2, 1} and a second, denser write pattern."""
+    S, q, k, v, alpha, beta = _gdn_case(1024, 9)
+    beta = torch.tensor([0.0, 0.5, 1.0])[torch.randint(0, 3, (1024,), generator=torch.Generator().manual_seed(5))]
+    So = S.numpy().copy()
+    Sd = S.cuda()
+    for step in range(2):
+        ow = oracle.gdn_step(So, q.numpy(), k.numpy(), v.numpy(), alpha.numpy(), beta.numpy())
+        od = qx.gdn_step(Sd, q.cuda(), k.cuda(), v.cuda(), alpha.cuda(), beta.cuda())
+        torch.cuda.synchronize()
+        assert np.array_equal(od.cpu().numpy(), ow), step
+        assert np.array_equal(Sd.cpu().numpy(), So), step
+        q = q.roll(1, 0)
