@@ -49,36 +49,30 @@ enum { /* phase kinds of the per-token program */
     QX_PH_ZERO = 1,     /* X rows [a, a + b) of the row list: set to 0 */
     QX_PH_LOADX = 2,    /* step mode: X[row] = x[machine][dim] for pairs [a, a + b) */
     QX_PH_STAGE = 3,    /* lag history of head sublayer c: entries [a, a + b) */
-    QX_PH_FORMS = 4,    /* forms [a, b); warp ranges warp_ptr[c .. c + NW] */
-    QX_PH_UNITS = 5,    /* FFN nodes [a, b); warp ranges warp_ptr[c .. c + NW] */
-    QX_PH_KSEL = 6,     /* key heads [a, b): key argmax and query top-k, per machine */
+    QX_PH_FORMS = 4,    /* form records of the stream; warp w reads quads warp_ptr[c + w ..] */
+    QX_PH_UNITS = 5,    /* FFN node records of the stream; warp ranges at warp_ptr[c] */
+    QX_PH_KSEL = 6,     /* key-head records of the stream: key argmax, query top-k per machine */
     QX_PH_VH = 7,       /* value heads [a, b): decay, write, read, output, per machine */
     QX_PH_APPLY = 8,    /* X[dst] += X[src] for pairs [a, a + b) */
     QX_PH_WRITEOUT = 9, /* step mode: x[machine][dim] = X[row] for pairs [a, a + b) */
     QX_PH_DECODE = 10,  /* run mode: output code -> token; next embedding into X */
-    QX_PH_END = 11
+    QX_PH_END = 11,
+    QX_PH_NOSYNC = 0x100 /* flag on a phase kind: no barrier after the phase */
 };
 
 typedef struct {
-    uint32_t kind, a, b, c;
+    uint32_t kind, a, b, c;  /* kind: QX_PH_* (low 8 bits) | QX_PH_NOSYNC */
 } qx_phase;
 
-typedef struct {        /* a linear form over smem rows: sum of w * row, packed entries */
-    uint32_t nnz0;      /* first packed entry (a multiple of 4) */
-    uint16_t nnz4;      /* entries / 4 (zero-weight padded) */
-    uint16_t dst;       /* destination row (scratch) */
-} qx_form;
-
-typedef struct {        /* FFN node: X[out] += sum of its units */
-    uint32_t u0;
-    uint16_t nu;
-    uint16_t out;
-} qx_node;
-
-typedef struct {        /* coef * (F[a] + ca x0) * relu(F[b] + cb x0); QX_NONE rows read 0 */
-    float coef, ca, cb;
-    uint16_t a, b;
-} qx_unit;
+/* Stream records (uint4 quads), consumed per warp in order.  Every row field is a shared-memory
+ * word offset (row * 33); the row after the last one is kept at zero and stands for "no form".
+ *   form      [dst, n entry quads, 0, 0] + entry quads of 4 entries (row | bf16 w << 16)
+ *   FFN node  [out, n units, 0, 0] + units [coef, ca, cb, a | b << 16]:
+ *             X[out] += sum coef * (F[a] + ca x0) * relu(F[b] + cb x0)
+ *   key head  [slot | qhot << 16, k common | q common << 16, nk | nq << 16, k lag-ONE | q lag-ONE
+ *             << 16] + (if nk) a quad of the key channels' existence mask and 64 key quads, then
+ *             (if nq) the same for the queries; two channels a quad [row | bf16 c1 << 16, c0, ..]:
+ *             channel = relu(F[row] + (exists ? F[common] : 0) + c0 x0 + c1 x0(t - lag)) */
 
 typedef struct {        /* lag history entry of a head sublayer */
     uint32_t e;         /* index into that sublayer's history rows */
@@ -87,12 +81,6 @@ typedef struct {        /* lag history entry of a head sublayer */
     uint16_t stage[3];  /* scratch row receiving lag 1, 2, 3 (QX_NONE: not read) */
     uint16_t pad;
 } qx_stage;
-
-typedef struct {        /* key head: channel -> scratch row and constant, for k and q */
-    uint32_t chan;      /* offset into kq_row / kq_c: [2][128] (k then q) */
-    uint16_t qhot;      /* query rows read (QHOT) */
-    uint16_t slot;      /* its KSEL slot within the phase group */
-} qx_khead;
 
 typedef struct {        /* value head task */
     uint32_t hl;        /* head sublayer (which S buffer) */
@@ -105,8 +93,8 @@ typedef struct {        /* value head task */
 } qx_vhead;
 
 typedef struct {        /* a per-column lazily evaluated form (v or z): relu(sum + c x0) */
-    uint32_t nnz0;
-    uint16_t nnz4;
+    uint32_t nnz0;      /* first packed entry in NNZ (a multiple of 4) */
+    uint16_t nnz4;      /* entries / 4 */
     uint16_t live;      /* 0: the column has no form (reads 0) */
     float c;
 } qx_colform;
@@ -134,15 +122,10 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_STEP_PROG,      /* qx_phase: the step-mode program */
     QX_S_ROWS,           /* uint16: row lists */
     QX_S_PAIRS,          /* uint32 pairs (row, dim) / (dst, src) */
-    QX_S_FORMS,          /* qx_form */
-    QX_S_NNZ,            /* uint32: row | bf16 weight << 16 */
-    QX_S_WARP_PTR,       /* uint32 */
-    QX_S_NODES,          /* qx_node */
-    QX_S_UNITS,          /* qx_unit */
+    QX_S_STREAM,         /* uint4 quads: form, FFN node and key-head records */
+    QX_S_NNZ,            /* uint32: packed entries of the lazily evaluated v / z forms */
+    QX_S_WARP_PTR,       /* uint32: per phase, nw + 1 quad offsets into STREAM */
     QX_S_STAGES,         /* qx_stage */
-    QX_S_KHEADS,         /* qx_khead */
-    QX_S_KQ_ROW,         /* uint16 [kheads][2][128] */
-    QX_S_KQ_C,           /* float  [kheads][2][128] */
     QX_S_VHEADS,         /* qx_vhead */
     QX_S_VFORM,          /* qx_colform [vheads][128] */
     QX_S_ZFORM,          /* qx_colform [vheads][128] */
@@ -163,6 +146,9 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_REG_COLS,       /* int32 [32][8] */
     QX_S_COUNT
 };
+
+#define QX_PLAN_VERSION 3
+#define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */
 

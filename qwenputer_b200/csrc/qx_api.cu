@@ -90,16 +90,17 @@ struct SecSpec {
 qx_status validate(const qx_plan_header &h, size_t bytes) {
     if (bytes < sizeof(qx_plan_header)) return fail(QX_ERR_INVALID_PLAN, "plan shorter than its header");
     if (h.magic != QX_PLAN_MAGIC) return fail(QX_ERR_INVALID_PLAN, "bad plan magic");
-    if (h.version != 1) return fail(QX_ERR_INVALID_PLAN, "plan version %u, expected 1", h.version);
+    if (h.version != QX_PLAN_VERSION)
+        return fail(QX_ERR_INVALID_PLAN, "plan version %u, expected %d", h.version, QX_PLAN_VERSION);
+    if (h.qhot_max > 4) return fail(QX_ERR_INVALID_PLAN, "queries read at most 4 rows");
     if (h.nw != QX_NW) return fail(QX_ERR_INVALID_PLAN, "plan balanced for %u warps, kernel has %d", h.nw, QX_NW);
     if (h.n_head_levels > QX_MAX_HL) return fail(QX_ERR_INVALID_PLAN, "too many head sublayers");
     if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
     if (h.n_born0 != h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
     const SecSpec specs[] = {
         {QX_S_RUN_PROG, sizeof(qx_phase)}, {QX_S_STEP_PROG, sizeof(qx_phase)}, {QX_S_ROWS, 2},
-        {QX_S_PAIRS, 8}, {QX_S_FORMS, sizeof(qx_form)}, {QX_S_NNZ, 4}, {QX_S_WARP_PTR, 4},
-        {QX_S_NODES, sizeof(qx_node)}, {QX_S_UNITS, sizeof(qx_unit)}, {QX_S_STAGES, sizeof(qx_stage)},
-        {QX_S_KHEADS, sizeof(qx_khead)}, {QX_S_KQ_ROW, 2}, {QX_S_KQ_C, 4}, {QX_S_VHEADS, sizeof(qx_vhead)},
+        {QX_S_PAIRS, 8}, {QX_S_STREAM, 16}, {QX_S_NNZ, 4}, {QX_S_WARP_PTR, 4},
+        {QX_S_STAGES, sizeof(qx_stage)}, {QX_S_VHEADS, sizeof(qx_vhead)},
         {QX_S_VFORM, sizeof(qx_colform)}, {QX_S_ZFORM, sizeof(qx_colform)}, {QX_S_OUT_ROW, 2}, {QX_S_OUT_W, 4},
         {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 2}, {QX_S_PAY_ROW, 2}, {QX_S_FEAT_ROW, 2},
         {QX_S_FAM_IDS, 4}, {QX_S_FAM_SIZE, 4}, {QX_S_FAM_ROW0, 4}, {QX_S_EMB_BASE, 4}, {QX_S_EMB_BITS, 4},
@@ -154,15 +155,10 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.step_prog = sec<qx_phase>(ex, QX_S_STEP_PROG);
     d.rows = sec<uint16_t>(ex, QX_S_ROWS);
     d.pairs = sec<uint2>(ex, QX_S_PAIRS);
-    d.forms = sec<qx_form>(ex, QX_S_FORMS);
+    d.stream = sec<uint4>(ex, QX_S_STREAM);
     d.nnz = sec<uint32_t>(ex, QX_S_NNZ);
     d.warp_ptr = sec<uint32_t>(ex, QX_S_WARP_PTR);
-    d.nodes = sec<qx_node>(ex, QX_S_NODES);
-    d.units = sec<qx_unit>(ex, QX_S_UNITS);
     d.stages = sec<qx_stage>(ex, QX_S_STAGES);
-    d.kheads = sec<qx_khead>(ex, QX_S_KHEADS);
-    d.kq_row = sec<uint16_t>(ex, QX_S_KQ_ROW);
-    d.kq_c = sec<float>(ex, QX_S_KQ_C);
     d.vheads = sec<qx_vhead>(ex, QX_S_VHEADS);
     d.vform = sec<qx_colform>(ex, QX_S_VFORM);
     d.zform = sec<qx_colform>(ex, QX_S_ZFORM);

@@ -6,6 +6,10 @@
 // query reads are touched.  A phase ends with __syncthreads(); no grid-wide synchronisation is
 // ever needed because machines never exchange data.
 //
+// The plan's form / unit / key-head records reach each warp as a stream of 16-byte quads that
+// the warp copies from L2 into its own two-half ring in shared memory with cp.async, one half
+// ahead of the half it reads; all 32 lanes then read each quad with one broadcast load.
+//
 // Semantics follow the reference executor (ERV = experimental/riscv):
 //   FFN units    coef * a * relu(b) into the node's dim          ERV/chipformer/rv/tritonexec.py:47-71
 //   heads        q/k/v/z relu projections over the lagged input,
@@ -22,55 +26,22 @@ namespace {
 
 __device__ __forceinline__ float relu(float v) { return v > 0.0f ? v : 0.0f; }
 
-__device__ __forceinline__ float sm_row(const float *sm, uint32_t row, int lane) {
-    return row == QX_NONE ? 0.0f : sm[row * QX_RP + lane];
-}
+__device__ __forceinline__ float wbits(uint32_t e) { return __uint_as_float(e & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t obits(uint32_t e) { return e & 0xFFFFu; }
 
-// sum of w * sm[row][lane] over packed entries (row | bf16 weight << 16), 4 per uint4
-__device__ __forceinline__ float form_sum(const float *sm, const uint32_t *nnz, uint32_t nnz0,
-                                          uint32_t nnz4, int lane) {
+// sum of w * sml[off] over packed entries read from global memory (lazy v / z forms); sml is
+// the shared memory of one machine's column (sm + machine), offsets are row * 33
+__device__ __forceinline__ float form_sum_g(const float *sml, const uint32_t *nnz, uint32_t nnz0, uint32_t nnz4) {
     const uint4 *q = reinterpret_cast<const uint4 *>(nnz + nnz0);
-    float acc0 = 0.0f, acc1 = 0.0f;
-    uint32_t k = 0;
-    for (; k + 1 < nnz4; k += 2) {
-        uint4 e = __ldg(q + k), f = __ldg(q + k + 1);
-        acc0 = fmaf(__uint_as_float(e.x & 0xFFFF0000u), sm[(e.x & 0xFFFFu) * QX_RP + lane], acc0);
-        acc1 = fmaf(__uint_as_float(e.y & 0xFFFF0000u), sm[(e.y & 0xFFFFu) * QX_RP + lane], acc1);
-        acc0 = fmaf(__uint_as_float(e.z & 0xFFFF0000u), sm[(e.z & 0xFFFFu) * QX_RP + lane], acc0);
-        acc1 = fmaf(__uint_as_float(e.w & 0xFFFF0000u), sm[(e.w & 0xFFFFu) * QX_RP + lane], acc1);
-        acc0 = fmaf(__uint_as_float(f.x & 0xFFFF0000u), sm[(f.x & 0xFFFFu) * QX_RP + lane], acc0);
-        acc1 = fmaf(__uint_as_float(f.y & 0xFFFF0000u), sm[(f.y & 0xFFFFu) * QX_RP + lane], acc1);
-        acc0 = fmaf(__uint_as_float(f.z & 0xFFFF0000u), sm[(f.z & 0xFFFFu) * QX_RP + lane], acc0);
-        acc1 = fmaf(__uint_as_float(f.w & 0xFFFF0000u), sm[(f.w & 0xFFFFu) * QX_RP + lane], acc1);
+    float a0 = 0.0f, a1 = 0.0f;
+    for (uint32_t k = 0; k < nnz4; k++) {
+        const uint4 e = __ldg(q + k);
+        a0 = fmaf(wbits(e.x), sml[obits(e.x)], a0);
+        a1 = fmaf(wbits(e.y), sml[obits(e.y)], a1);
+        a0 = fmaf(wbits(e.z), sml[obits(e.z)], a0);
+        a1 = fmaf(wbits(e.w), sml[obits(e.w)], a1);
     }
-    if (k < nnz4) {
-        uint4 e = __ldg(q + k);
-        acc0 = fmaf(__uint_as_float(e.x & 0xFFFF0000u), sm[(e.x & 0xFFFFu) * QX_RP + lane], acc0);
-        acc1 = fmaf(__uint_as_float(e.y & 0xFFFF0000u), sm[(e.y & 0xFFFFu) * QX_RP + lane], acc1);
-        acc0 = fmaf(__uint_as_float(e.z & 0xFFFF0000u), sm[(e.z & 0xFFFFu) * QX_RP + lane], acc0);
-        acc1 = fmaf(__uint_as_float(e.w & 0xFFFF0000u), sm[(e.w & 0xFFFFu) * QX_RP + lane], acc1);
-    }
-    return acc0 + acc1;
-}
-
-// argmax over 128 channel values held 4 per lane (channel = lane + 32 i): the first maximum
-__device__ __forceinline__ void warp_argmax(float v, int idx, float &bv, int &bi) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xFFFFFFFFu, v, o);
-        int oi = __shfl_xor_sync(0xFFFFFFFFu, idx, o);
-        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
-    }
-    bv = v;
-    bi = idx;
-}
-
-__device__ __forceinline__ void lane_best(const float c[4], int lane, float &v, int &idx) {
-    v = c[0];
-    idx = lane;
-#pragma unroll
-    for (int i = 1; i < 4; i++)
-        if (c[i] > v) { v = c[i]; idx = lane + 32 * i; }
+    return a0 + a1;
 }
 
 __device__ __forceinline__ uint64_t fnv_word(uint64_t h, uint32_t w) {
@@ -82,20 +53,79 @@ __device__ __forceinline__ uint64_t fnv_word(uint64_t h, uint32_t w) {
     return h;
 }
 
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// A warp's view of its range [begin, end) of the plan stream, read through a ring of two halves
+// of QX_RING_QUADS quads: while the warp reads one half, the next half is in flight.
+struct Stream {
+    const uint4 *g;
+    uint4 *ring;        // this warp's 2 * QX_RING_QUADS quads
+    const uint4 *rp;    // next quad to read (in the ring)
+    uint32_t begin, end, chunk;
+    int left, lane;     // quads left in the current half
+
+    __device__ __forceinline__ void issue(uint32_t c) {
+        const uint32_t q = begin + c * QX_RING_QUADS + lane;
+        if (q < end) cp_async16(ring + (c & 1) * QX_RING_QUADS + lane, g + q);
+        cp_commit();
+    }
+    __device__ __forceinline__ void settle() {
+        rp = ring + (chunk & 1) * QX_RING_QUADS;
+        const uint32_t rest = end - (begin + chunk * QX_RING_QUADS);
+        left = rest < QX_RING_QUADS ? (int)rest : QX_RING_QUADS;
+    }
+    __device__ __forceinline__ void start(const uint4 *g_, uint4 *ring_, uint32_t b, uint32_t e, int l) {
+        g = g_; ring = ring_; begin = b; end = e; lane = l; chunk = 0;
+        issue(0);
+        issue(1);
+        cp_wait<1>();
+        __syncwarp();
+        settle();
+    }
+    // the next half: once every lane is done with the current one, refill it two halves ahead
+    __device__ __forceinline__ void advance() {
+        chunk++;
+        __syncwarp();
+        issue(chunk + 1);
+        cp_wait<1>();
+        __syncwarp();
+        settle();
+    }
+    __device__ __forceinline__ bool more() const { return left > 0 || begin + (chunk + 1) * QX_RING_QUADS < end; }
+    __device__ __forceinline__ uint4 next() {
+        if (left == 0) advance();
+        left--;
+        return *rp++;
+    }
+    __device__ __forceinline__ void finish() {
+        cp_wait<0>();
+        __syncwarp();
+    }
+};
+
 }  // namespace
 
 template <int RUN>
 __global__ void __launch_bounds__(QX_NT, 1)
     qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens) {
     extern __shared__ __align__(16) float sm[];
-    int *ksel = reinterpret_cast<int *>(sm + (size_t)d.smem_rows * QX_RP);  // [slots][32]
+    int *ksel = reinterpret_cast<int *>(sm + (size_t)(d.smem_rows + 1) * QX_RP);  // [slots][32]
     int *qsel = ksel + d.ksel_slots * 32;                                    // [slots][qhot][32]
     int *dec_i = qsel + d.ksel_slots * d.qhot_max * 32;                      // [2][32]
     float *dec_pay = reinterpret_cast<float *>(dec_i + 64);                  // [16][32]
     unsigned int *touched = reinterpret_cast<unsigned int *>(dec_pay + 16 * 32);  // state rows
-    if (threadIdx.x == 0) *touched = 0;
-    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint4 *ring = reinterpret_cast<uint4 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d)) +
+                  warp * 2 * QX_RING_QUADS;
+    float *sml = sm + lane;  // this lane's machine column: row r at sml[r * 33]
+    if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
+    if (threadIdx.x == 0) *touched = 0;
     const int m = blockIdx.x * 32 + lane;  // this lane's machine
     const bool act = m < d.B;
     const int mbase = blockIdx.x * 32;
@@ -106,41 +136,42 @@ __global__ void __launch_bounds__(QX_NT, 1)
     if (RUN) {
         for (int i = warp; i < d.n_born0; i += QX_NW) {
             uint2 p = d.pairs[i];
-            sm[p.x * QX_RP + lane] = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
+            sml[p.x] = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
         }
         if (warp == 0 && act) {
             hash = d.hash[m];
             count = d.count[m];
             halt_at = d.halt_at[m];
         }
-        __syncthreads();
     }
+    __syncthreads();
     const qx_phase *prog = RUN ? d.run_prog : d.step_prog;
     for (int32_t t = 0; t < n_tokens; t++) {
         for (int pc = 0;; pc++) {
             const qx_phase ph = prog[pc];
-            if (ph.kind == QX_PH_END) break;
-            switch (ph.kind) {
+            const uint32_t kind = ph.kind & 0xFFu;
+            if (kind == QX_PH_END) break;
+            switch (kind) {
             case QX_PH_ZERO:
-                for (uint32_t i = warp; i < ph.b; i += QX_NW) sm[d.rows[ph.a + i] * QX_RP + lane] = 0.0f;
+                for (uint32_t i = warp; i < ph.b; i += QX_NW) sml[d.rows[ph.a + i]] = 0.0f;
                 break;
             case QX_PH_LOADX:
                 for (uint32_t i = warp; i < ph.b; i += QX_NW) {
                     uint2 p = d.pairs[ph.a + i];
-                    sm[p.x * QX_RP + lane] = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
+                    sml[p.x] = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
                 }
                 break;
             case QX_PH_WRITEOUT:
                 if (act)
                     for (uint32_t i = warp; i < ph.b; i += QX_NW) {
                         uint2 p = d.pairs[ph.a + i];
-                        d.x[(size_t)m * d.D + p.y] = sm[p.x * QX_RP + lane];
+                        d.x[(size_t)m * d.D + p.y] = sml[p.x];
                     }
                 break;
             case QX_PH_APPLY:
                 for (uint32_t i = warp; i < ph.b; i += QX_NW) {
                     uint2 p = d.pairs[ph.a + i];
-                    sm[p.x * QX_RP + lane] += sm[p.y * QX_RP + lane];
+                    sml[p.x] += sml[p.y];
                 }
                 break;
             case QX_PH_STAGE: {
@@ -154,146 +185,218 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     float h0 = h[0];
                     float h1 = s.ml >= 2 ? h[ne * bp] : 0.0f;
                     float h2 = s.ml >= 3 ? h[2 * ne * bp] : 0.0f;
-                    if (s.stage[0] != QX_NONE) sm[s.stage[0] * QX_RP + lane] = h0;
-                    if (s.stage[1] != QX_NONE) sm[s.stage[1] * QX_RP + lane] = h1;
-                    if (s.stage[2] != QX_NONE) sm[s.stage[2] * QX_RP + lane] = h2;
-                    h[0] = sm[s.x_row * QX_RP + lane];
+                    if (s.stage[0] != QX_NONE) sml[s.stage[0]] = h0;
+                    if (s.stage[1] != QX_NONE) sml[s.stage[1]] = h1;
+                    if (s.stage[2] != QX_NONE) sml[s.stage[2]] = h2;
+                    h[0] = sml[s.x_row];
                     if (s.ml >= 2) h[ne * bp] = h0;
                     if (s.ml >= 3) h[2 * ne * bp] = h1;
                 }
                 break;
             }
             case QX_PH_FORMS: {
-                const uint32_t f1 = d.warp_ptr[ph.c + warp + 1];
-                for (uint32_t f = d.warp_ptr[ph.c + warp]; f < f1; f++) {
-                    const qx_form fm = d.forms[f];
-                    sm[fm.dst * QX_RP + lane] = form_sum(sm, d.nnz, fm.nnz0, fm.nnz4, lane);
+                const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
+                if (b0 == b1) break;
+                Stream st;
+                st.start(d.stream, ring, b0, b1, lane);
+                while (st.more()) {
+                    const uint4 h = st.next();
+                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                    int nq = (int)h.y;
+                    while (nq > 0) {
+                        if (st.left == 0) st.advance();
+                        const int n = nq < st.left ? nq : st.left;
+                        const uint4 *rp = st.rp;
+                        for (int j = 0; j < n; j++) {
+                            const uint4 e = rp[j];
+                            a0 = fmaf(wbits(e.x), sml[obits(e.x)], a0);
+                            a1 = fmaf(wbits(e.y), sml[obits(e.y)], a1);
+                            a2 = fmaf(wbits(e.z), sml[obits(e.z)], a2);
+                            a3 = fmaf(wbits(e.w), sml[obits(e.w)], a3);
+                        }
+                        st.rp += n;
+                        st.left -= n;
+                        nq -= n;
+                    }
+                    sml[h.x] = (a0 + a1) + (a2 + a3);
                 }
+                st.finish();
                 break;
             }
             case QX_PH_UNITS: {
-                const float x0 = sm[d.one_row * QX_RP + lane];
-                const uint32_t n1 = d.warp_ptr[ph.c + warp + 1];
-                for (uint32_t n = d.warp_ptr[ph.c + warp]; n < n1; n++) {
-                    const qx_node nd = d.nodes[n];
+                const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
+                if (b0 == b1) break;
+                const float x0 = sml[d.one_row];
+                Stream st;
+                st.start(d.stream, ring, b0, b1, lane);
+                while (st.more()) {
+                    const uint4 h = st.next();
                     float acc = 0.0f;
-                    for (uint32_t u = nd.u0; u < nd.u0 + nd.nu; u++) {
-                        const qx_unit un = d.units[u];
-                        float av = sm_row(sm, un.a, lane) + un.ca * x0;
-                        float bv = sm_row(sm, un.b, lane) + un.cb * x0;
-                        acc += __fmul_rn(__fmul_rn(un.coef, av), relu(bv));
+                    for (uint32_t u = 0; u < h.y; u++) {
+                        const uint4 un = st.next();
+                        const float av = fmaf(__uint_as_float(un.y), x0, sml[un.w & 0xFFFFu]);
+                        const float bv = fmaf(__uint_as_float(un.z), x0, sml[un.w >> 16]);
+                        acc += __fmul_rn(__fmul_rn(__uint_as_float(un.x), av), relu(bv));
                     }
-                    atomicAdd(&sm[nd.out * QX_RP + lane], acc);
+                    atomicAdd(&sml[h.x], acc);  // records into one row may meet
                 }
+                st.finish();
                 break;
             }
             case QX_PH_KSEL: {
-                // per (key head, machine): lanes walk the 128 channels
-                const uint32_t n = ph.b - ph.a;
-                for (uint32_t task = warp; task < n * 32; task += QX_NW) {
-                    const qx_khead kh = d.kheads[ph.a + task / 32];
-                    const int mm = task % 32;
-                    const float x0 = sm[d.one_row * QX_RP + mm];
-                    float kc[4], qc[4];
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int c = lane + 32 * i;
-                        uint16_t kr = d.kq_row[kh.chan + c], qr = d.kq_row[kh.chan + 128 + c];
-                        kc[i] = relu(sm_row(sm, kr, mm) + d.kq_c[kh.chan + c] * x0);
-                        qc[i] = relu(sm_row(sm, qr, mm) + d.kq_c[kh.chan + 128 + c] * x0);
-                    }
-                    float bv;
-                    int bi, lv;
-                    float lvv;
-                    lane_best(kc, lane, lvv, lv);
-                    warp_argmax(lvv, lv, bv, bi);
-                    int npos = 0;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) npos += __popc(__ballot_sync(0xFFFFFFFFu, kc[i] > 0.0f));
-                    const int gm = mbase + mm;
-                    if (lane == 0) {
-                        ksel[kh.slot * 32 + mm] = bv > 0.0f ? bi : -1;
-                        if (npos > 1 && gm < d.B) atomicOr(&d.err[gm], QX_E_KEY);
-                    }
-                    int qpos = 0;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) qpos += __popc(__ballot_sync(0xFFFFFFFFu, qc[i] > 0.0f));
-                    for (int j = 0; j < d.qhot_max; j++) {
-                        int sel = -1;
-                        if (j < kh.qhot) {
-                            lane_best(qc, lane, lvv, lv);
-                            warp_argmax(lvv, lv, bv, bi);
-                            sel = bv > 0.0f ? bi : -1;
-                            if ((bi & 31) == lane) qc[bi >> 5] = 0.0f;
+                // per key head, lanes walk machines: the key's first maximal channel (a write
+                // when it is positive) and the query's top-qhot positive channels
+                const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
+                if (b0 == b1) break;
+                const float x0 = sml[d.one_row];
+                Stream st;
+                st.start(d.stream, ring, b0, b1, lane);
+                while (st.more()) {
+                    const uint4 h = st.next();
+                    const uint32_t slot = h.x & 0xFFFFu, qhot = h.x >> 16;
+                    const uint32_t nk = h.z & 0xFFFFu, nq = h.z >> 16;
+                    int ik = -1, npos = 0;
+                    if (nk) {
+                        const float com = sml[h.y & 0xFFFFu], x1 = sml[h.w & 0xFFFFu];
+                        const uint4 mk = st.next();
+                        float bk = 0.0f;
+                        for (uint32_t i = 0; i + 1 < nk; i++) {
+                            const uint4 c = st.next();
+                            const uint32_t word = i < 16 ? mk.x : (i < 32 ? mk.y : (i < 48 ? mk.z : mk.w));
+                            const uint32_t bits = word >> ((2 * i) & 31);
+                            const float v0 = relu(fmaf(wbits(c.x), x1, fmaf(__uint_as_float(c.y), x0,
+                                                  sml[obits(c.x)] + ((bits & 1u) ? com : 0.0f))));
+                            const float v1 = relu(fmaf(wbits(c.z), x1, fmaf(__uint_as_float(c.w), x0,
+                                                  sml[obits(c.z)] + ((bits & 2u) ? com : 0.0f))));
+                            npos += (v0 > 0.0f) + (v1 > 0.0f);
+                            if (v0 > bk) { bk = v0; ik = 2 * i; }
+                            if (v1 > bk) { bk = v1; ik = 2 * i + 1; }
                         }
-                        if (lane == 0) qsel[(kh.slot * d.qhot_max + j) * 32 + mm] = sel;
                     }
-                    if (lane == 0 && qpos > kh.qhot && gm < d.B) atomicOr(&d.err[gm], QX_E_QUERY);
+                    ksel[slot * 32 + lane] = ik;
+                    if (npos > 1 && act) atomicOr(&d.err[m], QX_E_KEY);
+                    float qb0 = 0.f, qb1 = 0.f, qb2 = 0.f, qb3 = 0.f;
+                    int qi0 = -1, qi1 = -1, qi2 = -1, qi3 = -1, qpos = 0;
+                    if (nq) {
+                        const float com = sml[h.y >> 16], x1 = sml[h.w >> 16];
+                        const uint4 mq = st.next();
+                        for (uint32_t i = 0; i + 1 < nq; i++) {
+                            const uint4 c = st.next();
+                            const uint32_t word = i < 16 ? mq.x : (i < 32 ? mq.y : (i < 48 ? mq.z : mq.w));
+                            const uint32_t bits = word >> ((2 * i) & 31);
+#pragma unroll
+                            for (int half = 0; half < 2; half++) {
+                                const uint32_t e = half ? c.z : c.x;
+                                const float c0 = __uint_as_float(half ? c.w : c.y);
+                                float v = relu(fmaf(wbits(e), x1, fmaf(c0, x0, sml[obits(e)] +
+                                                    ((bits >> half) & 1u ? com : 0.0f))));
+                                int vi = (int)(2 * i + half);
+                                qpos += v > 0.0f;
+                                // insertion into the descending top list: a value displaces only
+                                // a strictly smaller one, so ties keep the lower channel first
+                                if (v > qb0) { float tv = qb0; int ti = qi0; qb0 = v; qi0 = vi; v = tv; vi = ti; }
+                                if (qhot > 1 && v > qb1) { float tv = qb1; int ti = qi1; qb1 = v; qi1 = vi; v = tv; vi = ti; }
+                                if (qhot > 2 && v > qb2) { float tv = qb2; int ti = qi2; qb2 = v; qi2 = vi; v = tv; vi = ti; }
+                                if (qhot > 3 && v > qb3) { qb3 = v; qi3 = vi; }
+                            }
+                        }
+                    }
+                    const int qs[4] = {qi0, qi1, qi2, qi3};
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if (j < d.qhot_max) qsel[(slot * d.qhot_max + j) * 32 + lane] = j < (int)qhot ? qs[j] : -1;
+                    if (qpos > (int)qhot && act) atomicOr(&d.err[m], QX_E_QUERY);
                 }
+                st.finish();
                 break;
             }
             case QX_PH_VH: {
-                // per (value head, machine): lanes own 4 columns each
+                // per value head and quarter of the CTA's machines: lanes evaluate each
+                // machine's decay / write / read conditions, then serve the machines that touch
+                // a row one at a time with lanes over columns (4 each)
                 const uint32_t n = ph.b - ph.a;
-                for (uint32_t task = warp; task < n * 32; task += QX_NW) {
-                    const int mm = task % 32, gm = mbase + mm;
-                    if (gm >= d.B) continue;
-                    const qx_vhead vh = d.vheads[ph.a + task / 32];
-                    const float x0 = sm[d.one_row * QX_RP + mm];
-                    float *Sb = d.S[vh.hl] + ((size_t)gm * d.V[vh.hl] + vh.vh) * (QX_HD * QX_HD) + lane * 4;
-                    unsigned int rows = 0;  // 512-byte row transfers of this task
+                for (uint32_t task = warp; task < n * 4; task += QX_NW) {
+                    const qx_vhead vh = d.vheads[ph.a + task / 4];
+                    const int quarter = task & 3;
+                    const float x0 = sml[d.one_row];
+                    float fac = 1.0f;
                     if (vh.nrows > 0) {
-                        float av = sm_row(sm, vh.a_row, mm) + vh.ca * x0;
-                        float fac = av == 0.0f ? 1.0f : (av == 110.0f ? 0.5f : 0.0f);
-                        if (fac != 1.0f) rows += 2 * vh.nrows;
-                        if (fac != 1.0f)
+                        const float av = fmaf(vh.ca, x0, sml[vh.a_row]);
+                        fac = av == 0.0f ? 1.0f : (av == 110.0f ? 0.5f : 0.0f);
+                    }
+                    const float bv = fmaf(vh.cb, x0, sml[vh.b_row]) + vh.bconst;
+                    const int kr = ksel[vh.slot * 32 + lane];
+                    const int wrow = (kr >= 0 && bv == 1.0f) ? kr : -1;
+                    int q[4];
+                    bool anyq = false;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        q[j] = j < d.qhot_max ? qsel[(vh.slot * d.qhot_max + j) * 32 + lane] : -1;
+                        anyq |= q[j] >= 0;
+                    }
+                    const bool need = act && (lane >> 3) == quarter && (fac != 1.0f || wrow >= 0 || anyq);
+                    unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
+                    while (mask) {
+                        const int mm = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const int gm = mbase + mm;
+                        const float f = __shfl_sync(0xFFFFFFFFu, fac, mm);
+                        const int wr = __shfl_sync(0xFFFFFFFFu, wrow, mm);
+                        int qr[4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) qr[j] = __shfl_sync(0xFFFFFFFFu, q[j], mm);
+                        const float x0m = __shfl_sync(0xFFFFFFFFu, x0, mm);
+                        const float *smm = sm + mm;  // machine mm's column
+                        float *Sb = d.S[vh.hl] + ((size_t)gm * d.V[vh.hl] + vh.vh) * (QX_HD * QX_HD) + lane * 4;
+                        unsigned int rows = 0;  // 512-byte row transfers
+                        if (f != 1.0f) {
+                            rows += 2 * vh.nrows;
                             for (int r = 0; r < vh.nrows; r++) {
                                 float4 *p = reinterpret_cast<float4 *>(Sb + r * QX_HD);
                                 float4 s = *p;
-                                s.x = __fmul_rn(s.x, fac); s.y = __fmul_rn(s.y, fac);
-                                s.z = __fmul_rn(s.z, fac); s.w = __fmul_rn(s.w, fac);
+                                s.x = __fmul_rn(s.x, f); s.y = __fmul_rn(s.y, f);
+                                s.z = __fmul_rn(s.z, f); s.w = __fmul_rn(s.w, f);
                                 *p = s;
                             }
-                    }
-                    const float bv = (sm_row(sm, vh.b_row, mm) + vh.cb * x0) + vh.bconst;
-                    const int krow = ksel[vh.slot * 32 + mm];
-                    if (krow >= 0 && bv == 1.0f) {
-                        float v[4];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const qx_colform cf = d.vform[vh.col + lane * 4 + i];
-                            v[i] = cf.live ? relu(form_sum(sm, d.nnz, cf.nnz0, cf.nnz4, mm) + cf.c * x0) : 0.0f;
                         }
-                        *reinterpret_cast<float4 *>(Sb + krow * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
-                        rows++;
-                    }
-                    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                    bool any = false;
-                    for (int j = 0; j < d.qhot_max; j++) {
-                        const int qi = qsel[(vh.slot * d.qhot_max + j) * 32 + mm];
-                        if (qi >= 0) {
-                            float4 s = *reinterpret_cast<const float4 *>(Sb + qi * QX_HD);
-                            o.x = __fadd_rn(o.x, s.x); o.y = __fadd_rn(o.y, s.y);
-                            o.z = __fadd_rn(o.z, s.z); o.w = __fadd_rn(o.w, s.w);
-                            any = true;
+                        if (wr >= 0) {
+                            float v[4];
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                const qx_colform cf = d.vform[vh.col + lane * 4 + i];
+                                v[i] = cf.live ? relu(fmaf(cf.c, x0m, form_sum_g(smm, d.nnz, cf.nnz0, cf.nnz4))) : 0.0f;
+                            }
+                            *reinterpret_cast<float4 *>(Sb + wr * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
                             rows++;
                         }
-                    }
-                    if (lane == 0 && rows) atomicAdd(touched, rows);
-                    if (!any) continue;
-                    float ref = __fadd_rn(__fmul_rn(o.x, o.x), __fmul_rn(o.y, o.y));
-                    ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
-                    const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
-                    const float oc[4] = {o.x, o.y, o.z, o.w};
+                        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                        bool any = false;
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int c = lane * 4 + i;
-                        const uint16_t orow = d.out_row[vh.col + c];
-                        if (orow == QX_NONE) continue;
-                        const qx_colform zf = d.zform[vh.col + c];
-                        const float z = zf.live ? relu(form_sum(sm, d.nnz, zf.nnz0, zf.nnz4, mm) + zf.c * x0) : 0.0f;
-                        const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
-                        atomicAdd(&sm[orow * QX_RP + mm], __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
+                        for (int j = 0; j < 4; j++) {
+                            if (qr[j] >= 0) {
+                                const float4 s = *reinterpret_cast<const float4 *>(Sb + qr[j] * QX_HD);
+                                o.x = __fadd_rn(o.x, s.x); o.y = __fadd_rn(o.y, s.y);
+                                o.z = __fadd_rn(o.z, s.z); o.w = __fadd_rn(o.w, s.w);
+                                any = true;
+                                rows++;
+                            }
+                        }
+                        if (lane == 0) atomicAdd(touched, rows);
+                        if (!any) continue;
+                        float ref = __fadd_rn(__fmul_rn(o.x, o.x), __fmul_rn(o.y, o.y));
+                        ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
+                        const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
+                        const float oc[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int c = lane * 4 + i;
+                            const uint16_t orow = d.out_row[vh.col + c];
+                            if (orow == QX_NONE) continue;
+                            const qx_colform zf = d.zform[vh.col + c];
+                            const float z = zf.live ? relu(fmaf(zf.c, x0m, form_sum_g(smm, d.nnz, zf.nnz0, zf.nnz4))) : 0.0f;
+                            const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
+                            atomicAdd(&sm[orow + mm], __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
+                        }
                     }
                 }
                 break;
@@ -302,9 +405,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 if (warp == 0) {
                     float fam = 0.0f, psum = 0.0f;
                     for (int i = 0; i < d.n_fam; i++)
-                        fam = __fadd_rn(fam, __fmul_rn(rintf(sm[d.fam_row[i] * QX_RP + lane]), ldexpf(1.0f, i)));
+                        fam = __fadd_rn(fam, __fmul_rn(rintf(sml[d.fam_row[i]]), ldexpf(1.0f, i)));
                     for (int i = 0; i < d.n_pay; i++) {
-                        const float p = rintf(sm[d.pay_row[i] * QX_RP + lane]);
+                        const float p = rintf(sml[d.pay_row[i]]);
                         dec_pay[i * 32 + lane] = p;
                         psum = __fadd_rn(psum, __fmul_rn(p, ldexpf(1.0f, i)));
                     }
@@ -327,18 +430,19 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 for (int mm = warp; mm < 32; mm += QX_NW) {
                     const int fid = dec_i[mm], p = dec_i[32 + mm];
                     const int row0 = d.fam_row0[fid];
+                    float *smm = sm + mm;
                     if (row0 >= 0) {
                         int r = row0 + p;
                         r = r < 0 ? 0 : (r > d.n_emb_rows - 1 ? d.n_emb_rows - 1 : r);
                         for (int f = lane; f < d.n_feat; f += 32)
-                            sm[d.feat_row[f] * QX_RP + mm] = __ldg(d.emb_table + (size_t)r * d.n_feat + f);
+                            smm[d.feat_row[f]] = __ldg(d.emb_table + (size_t)r * d.n_feat + f);
                     } else {
                         const float *bits = d.emb_bits + (size_t)fid * d.n_pay * d.n_feat;
                         for (int f = lane; f < d.n_feat; f += 32) {
                             float acc = 0.0f;
                             for (int i = 0; i < d.n_pay; i++)
                                 acc = __fadd_rn(acc, __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
-                            sm[d.feat_row[f] * QX_RP + mm] = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), acc);
+                            smm[d.feat_row[f]] = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), acc);
                         }
                     }
                 }
@@ -347,14 +451,14 @@ __global__ void __launch_bounds__(QX_NT, 1)
             default:
                 break;
             }
-            __syncthreads();
+            if (!(ph.kind & QX_PH_NOSYNC)) __syncthreads();
         }
     }
     if (threadIdx.x == 0 && d.state_bytes) atomicAdd(d.state_bytes, 512ull * *touched);
     if (RUN) {
         for (int i = warp; i < d.n_born0; i += QX_NW) {
             uint2 p = d.pairs[i];
-            if (act) d.x[(size_t)m * d.D + p.y] = sm[p.x * QX_RP + lane];
+            if (act) d.x[(size_t)m * d.D + p.y] = sml[p.x];
         }
         if (warp == 0 && act) {
             d.hash[m] = hash;

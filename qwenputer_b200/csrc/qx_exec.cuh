@@ -15,15 +15,10 @@ struct QxDev {
     const qx_phase *run_prog, *step_prog;
     const uint16_t *rows;
     const uint2 *pairs;
-    const qx_form *forms;
+    const uint4 *stream;
     const uint32_t *nnz;
     const uint32_t *warp_ptr;
-    const qx_node *nodes;
-    const qx_unit *units;
     const qx_stage *stages;
-    const qx_khead *kheads;
-    const uint16_t *kq_row;
-    const float *kq_c;
     const qx_vhead *vheads;
     const qx_colform *vform, *zform;
     const uint16_t *out_row;
@@ -61,9 +56,15 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
     uint32_t anchor, n;
 };
 
-// shared memory after the rows: key-select slots, the decode area ([2][32] ints, [16][32]
-// payload floats) and a 64-byte counter block
-static inline size_t qx_smem_bytes(const QxDev &d) {
-    return (size_t)d.smem_rows * QX_RP * 4 + (size_t)d.ksel_slots * 32 * (1 + d.qhot_max) * 4 +
-           (size_t)32 * (2 + 16) * 4 + 64;
+// shared memory: the rows (word offsets row * 33; row smem_rows is kept at zero), then the
+// key-select slots, the decode area ([2][32] ints, [16][32] payload floats), a 64-byte counter
+// block and the per-warp stream rings ([NW][2][32] quads)
+__host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
+    // rows (plus the zero row), key-select slots, decode area, counters
+    size_t o = (size_t)(d.smem_rows + 1) * QX_RP * 4 + (size_t)d.ksel_slots * 32 * (1 + d.qhot_max) * 4 +
+               (size_t)32 * (2 + 16) * 4 + 64;
+    return (o + 15) & ~(size_t)15;
+}
+__host__ __device__ inline size_t qx_smem_bytes(const QxDev &d) {
+    return qx_ring_offset(d) + (size_t)QX_NW * 2 * QX_RING_QUADS * 16;
 }

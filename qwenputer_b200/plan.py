@@ -7,24 +7,40 @@ produces one program that a persistent CTA runs for 32 machines at a time (one p
 the residual stream of those machines resident in shared memory:
 
 * residual slots: every dim gets an X row only over its live range (birth .. last use), so the
-  2,679 dims fit in ~1,000 rows; rows are 33 floats (32 lanes + 1 pad: conflict-free whether a
+  2,679 dims fit in ~1,400 rows; rows are 33 floats (32 lanes + 1 pad: conflict-free whether a
   warp walks machines or rows);
 * linear forms: the non-constant part of every projection is deduplicated per phase group and
   evaluated once into a scratch row; the constant part (the ONE dim's coefficient) is applied
   where the form is used (``F + c * x0``), so units that differ only in their threshold share
-  a form (FFN nonzeros 227k -> 57k per machine-token);
+  a form;
+* key heads: the terms every channel of a key head shares (its head-select literals) form one
+  "common" form per head; the per-channel remainders are shared across heads (the row-address
+  literals of the RAM, ROM and DROM heads), cutting the head projections ~6x;
 * lag history: only (lag, dim) pairs the heads read are kept, staged into scratch rows at the
   start of their head sublayer (the ``_lag_load`` of tritonexec.py:74-79);
 * dims both written and read inside one sublayer (``into`` outputs) are accumulated into a
   temporary row and added at the sublayer's end, so every read sees the sublayer's input, as
   the reference's separate output buffer guarantees (tritonexec.py:151-170).
 
-Work lists are balanced over the CTA's warps at compile time (longest-first).
+Form, unit and key-head work is serialised into one stream of 16-byte quads, split into
+contiguous per-warp ranges balanced at compile time (longest first); the kernel streams each
+warp's range through shared memory with asynchronous copies.
+
+Stream records (all fields little-endian uint32; "row" fields are shared-memory word offsets,
+row * 33, so the kernel adds them to its lane's base without a multiply):
+  form      [dst, n entry quads, 0, 0] + entry quads (4 entries: row | bf16 weight << 16;
+            padding entries read the zero row with weight +0)
+  FFN node  [out, n units, 0, 0] + unit quads [coef, ca, cb, a | b << 16] (a node may be split
+            into several records that add into the same row)
+  key head  [slot | qhot << 16, k common | q common << 16, nk | nq << 16,
+             k lag-ONE row | q lag-ONE row << 16] + a quad of the 128-bit existence mask of the
+            key channels and one of the query channels (when nk / nq > 0), then nk key quads and
+            nq query quads, two channels each [row | bf16 c1 << 16, c0, row | bf16 c1 << 16, c0]:
+            channel = relu(F[row] + (exists ? F[common] : 0) + c0 x0 + c1 x0(t - lag))
 """
 
 from __future__ import annotations
 
-import dataclasses
 import heapq
 import struct
 from collections import defaultdict
@@ -36,32 +52,40 @@ from .graphfile import HD, ONE, GraphData
 NONE = 0xFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 1
+VERSION = 3
+NW_DEFAULT = 16
+RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
           DECODE=10, END=11)
-SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "FORMS", "NNZ", "WARP_PTR", "NODES", "UNITS",
-       "STAGES", "KHEADS", "KQ_ROW", "KQ_C", "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W",
-       "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW", "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0",
-       "EMB_BASE", "EMB_BITS", "EMB_TABLE", "TABLES", "REG_COLS"]
+NOSYNC = 0x100  # phase kind flag: no barrier after the phase
+UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most this many
+SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "NNZ", "WARP_PTR", "STAGES",
+       "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
+       "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
+       "TABLES", "REG_COLS"]
 TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
                + [f"quo{i}" for i in range(4)] + [f"rom{i}" for i in range(32)]
                + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
                + [f"bn2.{i}" for i in range(4)] + [f"ram{i}" for i in range(32)])
+SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
 
 DT = {
     "phase": np.dtype([("kind", "<u4"), ("a", "<u4"), ("b", "<u4"), ("c", "<u4")]),
-    "form": np.dtype([("nnz0", "<u4"), ("nnz4", "<u2"), ("dst", "<u2")]),
-    "node": np.dtype([("u0", "<u4"), ("nu", "<u2"), ("out", "<u2")]),
-    "unit": np.dtype([("coef", "<f4"), ("ca", "<f4"), ("cb", "<f4"), ("a", "<u2"), ("b", "<u2")]),
     "stage": np.dtype([("e", "<u4"), ("x_row", "<u2"), ("ml", "<u2"), ("s0", "<u2"),
                        ("s1", "<u2"), ("s2", "<u2"), ("pad", "<u2")]),
-    "khead": np.dtype([("chan", "<u4"), ("qhot", "<u2"), ("slot", "<u2")]),
     "vhead": np.dtype([("hl", "<u4"), ("vh", "<u4"), ("col", "<u4"), ("slot", "<u2"),
                        ("nrows", "<u2"), ("a_row", "<u2"), ("b_row", "<u2"), ("ca", "<f4"),
                        ("cb", "<f4"), ("bconst", "<f4")]),
     "colform": np.dtype([("nnz0", "<u4"), ("nnz4", "<u2"), ("live", "<u2"), ("c", "<f4")]),
 }
 HEADER = struct.Struct("<QII" + "I" * 14 + "32Q32Q")
+
+
+def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int) -> int:
+    """Shared memory after the rows: key-select slots, the decode area, a counter block and the
+    per-warp stream rings (two halves of RING_QUADS quads)."""
+    return (ROW_PAD * 4 + ksel_slots * 32 * (1 + qhot) * 4 + 32 * 18 * 4 + 64 + 16
+            + nw * 2 * RING_QUADS * 16)
 
 
 def _bf16_bits(w: float) -> int:
@@ -71,15 +95,8 @@ def _bf16_bits(w: float) -> int:
     return u >> 16
 
 
-@dataclasses.dataclass
-class Form:
-    """The non-constant part of a linear form: sorted ((lag, dim), weight) terms."""
-
-    terms: tuple
-
-    @property
-    def nnz(self) -> int:
-        return len(self.terms)
+def _fbits(x: float) -> int:
+    return int(np.float32(x).view(np.uint32))
 
 
 def split_form(forms, i: int, D: int) -> tuple[tuple, float]:
@@ -103,12 +120,11 @@ class Plan:
     def __init__(self):
         self.sec: dict[str, np.ndarray] = {}
         self.hdr: dict[str, int] = {}
-        self.stats: dict[str, float] = {}
+        self.stats: dict = {}
 
     def blob(self) -> bytes:
         offs, cnts, parts = [0] * 32, [0] * 32, []
-        pos = HEADER.size
-        pos = (pos + 255) // 256 * 256
+        pos = (HEADER.size + 255) // 256 * 256
         for i, name in enumerate(SEC):
             a = np.ascontiguousarray(self.sec[name])
             offs[i], cnts[i] = pos, len(a)
@@ -127,20 +143,19 @@ class Plan:
         return bytes(out)
 
 
-SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
-
-
-def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
+def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAULT,
                  ksel_slots: int = 16) -> Plan:
     qhot = int(g.head_qhot.max())
-    if smem_rows is None:  # rows of 33 floats left after the key-select and decode areas
-        smem_rows = (SMEM_MAX - ksel_slots * 32 * (1 + qhot) * 4 - 32 * 18 * 4 - 64) // (ROW_PAD * 4)
+    assert qhot <= 4, "queries may read at most 4 rows"
+    if smem_rows is None:
+        smem_rows = (SMEM_MAX - smem_extra_bytes(ksel_slots, qhot, nw)) // (ROW_PAD * 4)
     D = g.D
     levels = [int(x) for x in g.levels]
     kinds = [int(k) for k in g.level_kind]
     head_levels = [lv for lv, k in zip(levels, kinds) if k == 1]
     hl_index = {lv: i for i, lv in enumerate(head_levels)}
     INF = 10 ** 9
+    stats = defaultdict(float)
 
     # ---- per level: forms (non-constant parts + constants), reads, writes ---------------------
     ffn_nodes = defaultdict(list)
@@ -202,8 +217,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
     for lv in levels:
         for d in writes[lv]:
             last_write[d] = lv
-    # dims written and read (lag 0) in the same sublayer accumulate into a temporary row
-    temps = {}  # (level, dim) -> pseudo id
+    temps = {}  # (level, dim) -> pseudo id of its temporary row
     for lv in levels:
         for d in sorted(writes[lv] & {dd for lag, dd in reads[lv] if lag == 0}):
             key = ("T", lv, d)
@@ -228,33 +242,45 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
         heapq.heappush(active, (last[k], s))
     n_scratch = smem_rows - n_slots
     assert n_scratch >= 64, f"{n_slots} residual slots leave too little scratch"
-    # scratch rows of a sublayer: every row no live dim occupies there
     occupied = defaultdict(set)
     for k in items:
         for lv in levels:
             if birth[k] <= lv <= last[k]:
                 occupied[lv].add(slot[k])
     free_rows = {lv: [r for r in range(smem_rows) if r not in occupied[lv]] for lv in levels}
+    zero_row = smem_rows  # an extra row the kernel keeps at zero (reads of "no form")
+
+    def W(r: int) -> int:
+        """Shared-memory word offset of a row (rows are ROW_PAD floats apart)."""
+        return r * ROW_PAD
+
+    ZW = W(zero_row)
+    one_w = W(slot[ONE])
+    assert W(zero_row) < NONE
 
     # ---- builders -----------------------------------------------------------------------------
     rows_l: list[int] = []
     pairs_l: list[tuple[int, int]] = []
-    forms_l, nnz_l, warp_ptr_l = [], [], []
-    nodes_l, units_l, stages_l, kheads_l, kq_row_l, kq_c_l = [], [], [], [], [], []
-    vheads_l, vform_l, zform_l, out_row_l, out_w_l = [], [], [], [], []
-    stats = defaultdict(float)
+    stream: list[tuple[int, int, int, int]] = []
+    warp_ptr_l: list[int] = []
+    nnz_l: list[int] = []
+    stages_l, vheads_l, vform_l, zform_l, out_row_l, out_w_l = [], [], [], [], [], []
+
+    def entry_quads(terms, rowmap) -> list[tuple]:
+        ents = [W(rowmap(t)) | _bf16_bits(w) << 16 for t, w in terms]
+        while len(ents) % 4:
+            ents.append(ZW)  # the zero row times +0
+        return [tuple(ents[i:i + 4]) for i in range(0, len(ents), 4)]
 
     def pack_terms(terms, rowmap) -> tuple[int, int]:
-        """Append the packed entries of a term list (padded to a multiple of 4)."""
+        """Packed entries of a lazily evaluated column form (NNZ array, 4-aligned)."""
         start = len(nnz_l)
-        for t, w in terms:
-            nnz_l.append(rowmap(t) | _bf16_bits(w) << 16)
-        while (len(nnz_l) - start) % 4:
-            nnz_l.append(0)  # row 0, weight +0
+        for q in entry_quads(terms, rowmap):
+            nnz_l.extend(q)
         return start, (len(nnz_l) - start) // 4
 
-    def balance(costs: list[float]) -> tuple[list[int], list[int]]:
-        """Longest-first assignment of items to nw warps: (item order, warp_ptr offsets)."""
+    def balance(costs: list[float]) -> list[list[int]]:
+        """Longest-first assignment of items to the nw warps."""
         loads = [(0.0, w) for w in range(nw)]
         heapq.heapify(loads)
         per = [[] for _ in range(nw)]
@@ -262,25 +288,31 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
             ld, w = heapq.heappop(loads)
             per[w].append(i)
             heapq.heappush(loads, (ld + costs[i], w))
-        order, ptr = [], [0]
-        for w in range(nw):
-            order += per[w]
-            ptr.append(len(order))
-        stats["imbalance_max"] = max(stats["imbalance_max"], max(l for l, _ in loads)
-                                     / max(1e-9, sum(costs) / nw))
-        return order, ptr
+        tot = sum(costs)
+        if tot:
+            stats["imbalance_sum"] += max(l for l, _ in loads) - tot / nw
+            stats["balanced_sum"] += tot / nw
+        return per
 
-    def forms_phase(form_list: list[Form], dst_rows: list[int], rowmap, prog):
-        costs = [4 * ((f.nnz + 3) // 4) + 6 for f in form_list]
-        order, ptr = balance(costs)
-        f0 = len(forms_l)
-        for i in order:
-            s, n4 = pack_terms(form_list[i].terms, rowmap)
-            forms_l.append((s, n4, dst_rows[i]))
-            stats["form_nnz"] += form_list[i].nnz
+    def stream_phase(kind: int, records: list[list[tuple]], costs: list[float], prog, a=0, b=0):
+        """Emit per-warp quad ranges of the records (each a list of quads) as one phase."""
+        per = balance(costs)
         wp = len(warp_ptr_l)
-        warp_ptr_l.extend(f0 + p for p in ptr)
-        prog.append((PH["FORMS"], f0, len(forms_l), wp))
+        warp_ptr_l.append(len(stream))
+        for w in range(nw):
+            for i in per[w]:
+                stream.extend(records[i])
+            warp_ptr_l.append(len(stream))
+        prog.append((kind, a, b, wp))
+
+    def forms_phase(form_list: list[tuple], dst_rows: list[int], rowmap, prog):
+        recs, costs = [], []
+        for terms, dst in zip(form_list, dst_rows):
+            qs = entry_quads(terms, rowmap)
+            recs.append([(W(dst), len(qs), 0, 0)] + qs)
+            costs.append(22 * len(qs) + 12)
+            stats["form_nnz"] += len(terms)
+        stream_phase(PH["FORMS"], recs, costs, prog)
 
     def xrow(lv, d):
         return slot[temps[(lv, d)]] if (lv, d) in temps else slot[d]
@@ -290,32 +322,27 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
     hl_ne = []
     group_stats = []
 
-    # prologue / epilogue of run mode: the birth-0 dims (features and ONE from x; the rest 0)
     born0 = sorted(k for k in birth if birth[k] == 0 and not isinstance(k, tuple))
-    never_written_0 = [d for d in born0 if d not in set(feat) and d not in last_write]
-    r0 = len(rows_l)
-    rows_l.extend(slot[d] for d in never_written_0)
-    if never_written_0:
-        run_prog.append((PH["ZERO"], r0, len(never_written_0), 0))
     assert not pairs_l  # the run-mode prologue / epilogue are PAIRS[0 : n_born0]
-    pairs_l.extend((slot[d], d) for d in born0)
+    pairs_l.extend((W(slot[d]), d) for d in born0)
     step_prog.append((PH["LOADX"], 0, len(born0), 0))
 
     for lv, kind in zip(levels, kinds):
         born = sorted(d for d in birth if not isinstance(d, tuple) and birth[d] == lv and lv > 0)
         tmp = sorted(slot[k] for (l2, d), k in temps.items() if l2 == lv)
         r0 = len(rows_l)
-        rows_l.extend(slot[d] for d in born)
-        rows_l.extend(tmp)
+        rows_l.extend(W(slot[d]) for d in born)
+        rows_l.extend(W(t) for t in tmp)
+        # newborn and temporary rows are neither read nor written by the sublayer's first phase
+        # (a stage or form phase): their zeroing needs no barrier of its own
         if born or tmp:
-            run_prog.append((PH["ZERO"], r0, len(born) + len(tmp), 0))
+            run_prog.append((PH["ZERO"] | NOSYNC, r0, len(born) + len(tmp), 0))
         if tmp:
-            r1 = r0 + len(born)
-            step_prog.append((PH["ZERO"], r1, len(tmp), 0))
+            step_prog.append((PH["ZERO"] | NOSYNC, r0 + len(born), len(tmp), 0))
         if born:
             p0 = len(pairs_l)
-            pairs_l.extend((slot[d], d) for d in born)
-            step_prog.append((PH["LOADX"], p0, len(born), 0))
+            pairs_l.extend((W(slot[d]), d) for d in born)
+            step_prog.append((PH["LOADX"] | NOSYNC, p0, len(born), 0))
         body: list[tuple] = []
         free = free_rows[lv]
         if kind == 0:
@@ -340,34 +367,39 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
                 groups.append((cur, cur_forms))
             for gnodes, gforms in groups:
                 assert len(gforms) <= len(free), f"sublayer {lv}: a node needs too many forms"
-                flist = [Form(f) for f in gforms]
-                dst = [free[i] for i in range(len(flist))]
-                forms_phase(flist, dst, lambda t: slot[t[1]], body)
-                frow = {f: free[i] for f, i in gforms.items()}
-                costs, nd = [], []
+                flist = list(gforms)
+                forms_phase(flist, [free[i] for i in range(len(flist))], lambda t: slot[t[1]], body)
+                frow = {f: W(free[i]) for f, i in gforms.items()}
+                recs, costs = [], []
                 for n in gnodes:
-                    us = range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1]))
-                    costs.append(3 * len(us) + 4)
-                    nd.append(n)
-                order, ptr = balance(costs)
-                n0 = len(nodes_l)
-                for i in order:
-                    n = nd[i]
-                    u0 = len(units_l)
+                    q = []
                     for u in range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1])):
                         (ta, ca), (tb, cb) = unit_a[u], unit_b[u]
-                        units_l.append((float(g.unit_coef[u]), ca, cb,
-                                        frow[ta] if ta else NONE, frow[tb] if tb else NONE))
-                    nodes_l.append((u0, len(units_l) - u0, xrow(lv, int(g.ffn_out[n]))))
-                    stats["units"] += len(units_l) - u0
-                wp = len(warp_ptr_l)
-                warp_ptr_l.extend(n0 + p for p in ptr)
-                body.append((PH["UNITS"], n0, len(nodes_l), wp))
+                        ra = frow[ta] if ta else ZW
+                        rb = frow[tb] if tb else ZW
+                        q.append((_fbits(g.unit_coef[u]), _fbits(ca), _fbits(cb), ra | rb << 16))
+                    out = W(xrow(lv, int(g.ffn_out[n])))
+                    for c0 in range(0, len(q), UNIT_CHUNK):
+                        part = q[c0:c0 + UNIT_CHUNK]
+                        recs.append([(out, len(part), 0, 0)] + part)
+                        costs.append(16 * len(part) + 14)
+                    stats["units"] += len(q)
+                stream_phase(PH["UNITS"], recs, costs, body)
             group_stats.append((lv, "ffn", len(groups)))
         else:
             # ---------- head sublayer ---------------------------------------------------------
             hi = hl_index[lv]
             lag_pairs = sorted({t for t in reads[lv] if t[0] > 0})
+            # lagged ONE terms of key / query channels become per-channel constants times the
+            # staged ONE: make sure those stage rows exist
+            for h in g.heads_at(lv):
+                for tab, fs in ((g.head_k, kf), (g.head_q, qf)):
+                    for c in range(HD):
+                        if tab[h, c] >= 0:
+                            for (lag, d), _ in fs[tab[h, c]][0]:
+                                if d == ONE and lag > 0 and (lag, ONE) not in lag_pairs:
+                                    lag_pairs.append((lag, ONE))
+            lag_pairs = sorted(set(lag_pairs))
             lag_dims = sorted({d for _, d in lag_pairs})
             stage_row = {t: free[i] for i, t in enumerate(lag_pairs)}
             hl_ne.append(len(lag_dims))
@@ -375,8 +407,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
                 s0 = len(stages_l)
                 for e, d in enumerate(lag_dims):
                     ml = max(lag for lag, dd in lag_pairs if dd == d)
-                    st = [stage_row.get((lag, d), NONE) for lag in (1, 2, 3)]
-                    stages_l.append((e, slot[d], ml, *st, 0))
+                    st = [W(stage_row[(lag, d)]) if (lag, d) in stage_row else NONE for lag in (1, 2, 3)]
+                    stages_l.append((e, W(slot[d]), ml, *st, 0))
                 body.append((PH["STAGE"], s0, len(lag_dims), hi))
             ffree = free[len(lag_pairs):]
             cap = len(ffree)
@@ -384,15 +416,48 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
             def rowmap(t, lv=lv):
                 return slot[t[1]] if t[0] == 0 else stage_row[t]
 
+            def head_forms(h):
+                """Per key / query: (common terms, lag of the lagged-ONE constant,
+                {channel: (resid terms, c0, c1)}).  The common terms are those all (>= 4)
+                channels of the head share; a lagged ONE term becomes the constant c1."""
+                out = {}
+                for nm, tab, fs in (("k", g.head_k, kf), ("q", g.head_q, qf)):
+                    chans = {}
+                    lags = set()
+                    for c in range(HD):
+                        if tab[h, c] < 0:
+                            continue
+                        t, c0 = fs[tab[h, c]]
+                        ones = [(lag, w) for (lag, d), w in t if d == ONE and lag > 0]
+                        assert len(ones) <= 1
+                        c1 = ones[0][1] if ones else 0.0
+                        if ones:
+                            lags.add(ones[0][0])
+                        chans[c] = (tuple(x for x in t if not (x[0][1] == ONE and x[0][0] > 0)), c0, c1)
+                    assert len(lags) <= 1, "one lag of the ONE dim per head"
+                    common = set()
+                    if len(chans) >= 4:
+                        common = set(next(iter(chans.values()))[0])
+                        for t, _, _ in chans.values():
+                            common &= set(t)
+                    res = {c: (tuple(x for x in t if x not in common), c0, c1)
+                           for c, (t, c0, c1) in chans.items()}
+                    out[nm] = (tuple(sorted(common)), lags.pop() if lags else 0, res)
+                return out
+
             heads = g.heads_at(lv)
             vhs_level = g.vheads_at(lv)
+            hf = {h: head_forms(h) for h in heads}
             groups, cur, cur_forms = [], [], {}
             for h in heads:
                 nf = {}
-                for c in range(HD):
-                    for tab, fs in ((g.head_k, kf), (g.head_q, qf)):
-                        if tab[h, c] >= 0 and fs[tab[h, c]][0]:
-                            nf[fs[tab[h, c]][0]] = 1
+                for nm in ("k", "q"):
+                    com, _, res = hf[h][nm]
+                    if com:
+                        nf[com] = 1
+                    for t, _, _ in res.values():
+                        if t:
+                            nf[t] = 1
                 for j in g.vheads_of(h):
                     for fs in (af, bf):
                         if fs[j][0]:
@@ -409,23 +474,39 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
                 groups.append((cur, cur_forms))
             for gheads, gforms in groups:
                 assert len(gforms) <= cap, f"sublayer {lv}: a key head needs too many forms"
-                flist = [Form(f) for f in gforms]
-                frow = {f: ffree[i] for f, i in gforms.items()}
+                flist = list(gforms)
+                frow = {f: W(ffree[i]) for f, i in gforms.items()}
                 if flist:
                     forms_phase(flist, [ffree[i] for i in range(len(flist))], rowmap, body)
-                k0 = len(kheads_l)
+                recs, costs = [], []
                 for sl, h in enumerate(gheads):
-                    kheads_l.append((len(kq_row_l), int(g.head_qhot[h]), sl))
-                    for tab, fs in ((g.head_k, kf), (g.head_q, qf)):
+                    quads, com_rows, one_rows, masks = {}, {}, {}, {}
+                    for nm in ("k", "q"):
+                        com, lag, res = hf[h][nm]
+                        com_rows[nm] = frow[com] if com else ZW
+                        one_rows[nm] = W(stage_row[(lag, ONE)]) if lag else ZW
+                        mask = [0, 0, 0, 0]
+                        chans = []
                         for c in range(HD):
-                            if tab[h, c] >= 0:
-                                t, cc = fs[tab[h, c]]
-                                kq_row_l.append(frow[t] if t else NONE)
-                                kq_c_l.append(cc)
+                            if c in res:
+                                t, c0, c1 = res[c]
+                                if com:
+                                    mask[c // 32] |= 1 << (c % 32)
+                                chans.append(((frow[t] if t else ZW) | _bf16_bits(c1) << 16, _fbits(c0)))
                             else:
-                                kq_row_l.append(NONE)
-                                kq_c_l.append(0.0)
-                body.append((PH["KSEL"], k0, len(kheads_l), 0))
+                                chans.append((ZW, 0))
+                        masks[nm] = tuple(mask)
+                        quads[nm] = [] if not res else [masks[nm]] + [
+                            (chans[2 * i][0], chans[2 * i][1], chans[2 * i + 1][0], chans[2 * i + 1][1])
+                            for i in range(HD // 2)]
+                    nk, nq = len(quads["k"]), len(quads["q"])
+                    rec = [(sl | int(g.head_qhot[h]) << 16, com_rows["k"] | com_rows["q"] << 16,
+                            nk | nq << 16, one_rows["k"] | one_rows["q"] << 16)]
+                    rec += quads["k"] + quads["q"]
+                    recs.append(rec)
+                    costs.append(26 * (nk + nq) + 40)
+                    stats["kq_channels"] += 2 * (nk + nq)
+                stream_phase(PH["KSEL"], recs, costs, body)
                 v0 = len(vheads_l)
                 for sl, h in enumerate(gheads):
                     for j in g.vheads_of(h):
@@ -434,8 +515,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
                             for tab, fs, dstl in ((g.vh_v, vf, vform_l), (g.vh_z, zf, zform_l)):
                                 if tab[j, c] >= 0:
                                     t, cc = fs[tab[j, c]]
-                                    s, n4 = pack_terms(t, rowmap) if t else (0, 0)
-                                    dstl.append((s, n4, 1, cc))
+                                    s_, n4 = pack_terms(t, rowmap) if t else (0, 0)
+                                    dstl.append((s_, n4, 1, cc))
                                 else:
                                     dstl.append((0, 0, 0, 0.0))
                         orow = [NONE] * HD
@@ -443,18 +524,18 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
                         for e in range(int(g.vh_out_ptr[j]), int(g.vh_out_ptr[j + 1])):
                             c = int(g.out_col[e])
                             if float(g.out_w[e]) != 0.0:
-                                orow[c] = xrow(lv, int(g.out_dim[e]))
+                                orow[c] = W(xrow(lv, int(g.out_dim[e])))
                                 ow[c] = float(g.out_w[e])
                         out_row_l.extend(orow)
                         out_w_l.extend(ow)
                         ta, ca = af[j]
                         tb, cb = bf[j]
                         vheads_l.append((hi, vhs_level.index(j), col, sl, int(g.vh_nrows[j]),
-                                         frow[ta] if ta else NONE, frow[tb] if tb else NONE,
+                                         frow[ta] if ta else ZW, frow[tb] if tb else ZW,
                                          ca, cb, 0.0 if g.vh_has_beta[j] else 1.0))
                 body.append((PH["VH"], v0, len(vheads_l), 0))
             group_stats.append((lv, "head", len(groups)))
-        apply_pairs = [(slot[d], slot[k]) for (l2, d), k in temps.items() if l2 == lv]
+        apply_pairs = [(W(slot[d]), W(slot[k])) for (l2, d), k in temps.items() if l2 == lv]
         tail = []
         if apply_pairs:
             p0 = len(pairs_l)
@@ -465,7 +546,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
         wo = sorted(d for d, l2 in last_write.items() if l2 == lv)
         if wo:
             p0 = len(pairs_l)
-            pairs_l.extend((slot[d], d) for d in wo)
+            pairs_l.extend((W(slot[d]), d) for d in wo)
             step_prog.append((PH["WRITEOUT"], p0, len(wo), 0))
     run_prog.append((PH["DECODE"], 0, 0, 0))
     run_prog.append((PH["END"], 0, 0, 0))
@@ -473,9 +554,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
 
     # ---- sections -----------------------------------------------------------------------------
     def arr(lst, dt):
-        if isinstance(dt, str):
-            dt = DT[dt]
-        a = np.zeros(len(lst), dt)
+        dt = DT[dt]
+        a = np.zeros(max(1, len(lst)), dt)
         for i, v in enumerate(lst):
             a[i] = v
         return a
@@ -486,15 +566,10 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
     s["STEP_PROG"] = arr(step_prog, "phase")
     s["ROWS"] = np.asarray(rows_l or [0], np.uint16)
     s["PAIRS"] = np.asarray(pairs_l or [(0, 0)], np.uint32).reshape(-1, 2)
-    s["FORMS"] = arr(forms_l, "form") if forms_l else np.zeros(1, DT["form"])
-    s["NNZ"] = np.asarray(nnz_l or [0], np.uint32)
+    s["STREAM"] = np.asarray(stream or [(0, 0, 0, 0)], np.uint32).reshape(-1, 4)
+    s["NNZ"] = np.asarray(nnz_l or [0, 0, 0, 0], np.uint32)
     s["WARP_PTR"] = np.asarray(warp_ptr_l or [0], np.uint32)
-    s["NODES"] = arr(nodes_l, "node") if nodes_l else np.zeros(1, DT["node"])
-    s["UNITS"] = arr(units_l, "unit") if units_l else np.zeros(1, DT["unit"])
-    s["STAGES"] = arr(stages_l, "stage") if stages_l else np.zeros(1, DT["stage"])
-    s["KHEADS"] = arr(kheads_l, "khead")
-    s["KQ_ROW"] = np.asarray(kq_row_l, np.uint16)
-    s["KQ_C"] = np.asarray(kq_c_l, np.float32)
+    s["STAGES"] = arr(stages_l, "stage")
     s["VHEADS"] = arr(vheads_l, "vhead")
     s["VFORM"] = arr(vform_l, "colform")
     s["ZFORM"] = arr(zform_l, "colform")
@@ -502,9 +577,9 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
     s["OUT_W"] = np.asarray(out_w_l, np.float32)
     s["HL_V"] = np.asarray([len(g.vheads_at(lv)) for lv in head_levels], np.uint32)
     s["HL_NE"] = np.asarray([max(1, n) for n in hl_ne], np.uint32)
-    s["FAM_ROW"] = np.asarray([slot[int(d)] for d in g.fam_dims], np.uint16)
-    s["PAY_ROW"] = np.asarray([slot[int(d)] for d in g.pay_dims], np.uint16)
-    s["FEAT_ROW"] = np.asarray([slot[d] for d in feat], np.uint16)
+    s["FAM_ROW"] = np.asarray([W(slot[int(d)]) for d in g.fam_dims], np.uint16)
+    s["PAY_ROW"] = np.asarray([W(slot[int(d)]) for d in g.pay_dims], np.uint16)
+    s["FEAT_ROW"] = np.asarray([W(slot[d]) for d in feat], np.uint16)
     s["FAM_IDS"] = np.asarray(g.fam_ids, np.int32)
     s["FAM_SIZE"] = np.asarray(g.fam_size, np.int32)
     s["FAM_ROW0"] = np.asarray([int(r) if sm else -1 for r, sm in zip(g.fam_row0, g.fam_small)],
@@ -519,16 +594,20 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = 16,
     s["TABLES"] = np.asarray(tabs, np.uint32).reshape(-1)
     s["REG_COLS"] = np.asarray(g.reg_cols, np.int32).reshape(-1)
     P.hdr = dict(D=D, n_slots=n_slots, n_scratch=n_scratch, nw=nw, n_head_levels=len(head_levels),
-                 one_row=slot[ONE], n_ksel_slots=ksel_slots, qhot_max=int(g.head_qhot.max()),
+                 one_row=one_w, n_ksel_slots=ksel_slots, qhot_max=qhot,
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
                  n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
                  vocab=int(g.vocab), n_born0=len(born0))
     stats["n_slots"] = n_slots
     stats["n_scratch"] = n_scratch
     stats["phases_run"] = len(run_prog)
+    stats["barriers_run"] = sum(1 for k, *_ in run_prog if not k & NOSYNC and k != PH["END"])
+    stats["stream_quads"] = len(stream)
     stats["vform_nnz"] = sum(n4 * 4 for _, n4, _, _ in vform_l)
     stats["zform_nnz"] = sum(n4 * 4 for _, n4, _, _ in zform_l)
-    stats["weight_bytes"] = sum(a.nbytes for k, a in s.items() if not k.startswith("EMB"))
+    stats["weight_bytes"] = int(s["STREAM"].nbytes + s["STAGES"].nbytes + s["VHEADS"].nbytes
+                                + s["RUN_PROG"].nbytes + s["WARP_PTR"].nbytes)
+    stats["imbalance"] = (stats["imbalance_sum"] / stats["balanced_sum"]) if stats["balanced_sum"] else 0
     stats["groups"] = group_stats
     P.stats = dict(stats)
     P.slot = slot

@@ -20,11 +20,13 @@ class PlanInterp:
         self.s = s
         h = P.hdr
         self.rows = h["n_slots"] + h["n_scratch"]
-        self.X = np.zeros((self.rows, B), np.float32)
+        # indexed by shared-memory word offset (row * 33); the row after the last is zero
+        self.X = np.zeros(((self.rows + 1) * 33, B), np.float32)
         self.hl_v = s["HL_V"]
         self.S = [np.zeros((B, int(v), 128, 128), np.float32) for v in s["HL_V"]]
         self.H = [np.zeros((3, int(ne), B), np.float32) for ne in s["HL_NE"]]
         self.one = h["one_row"]
+        self.ksel, self.qsel = {}, {}
 
     def form(self, nnz0, nnz4, m=slice(None)):
         e = self.s["NNZ"][nnz0:nnz0 + 4 * nnz4]
@@ -35,14 +37,40 @@ class PlanInterp:
             acc = acc + ww * self.X[r, m]
         return acc
 
+    def warp_records(self, c, k):
+        """Per warp, the (header, body quads) records of a stream phase."""
+        st = self.s["STREAM"].astype(np.int64)
+        wp = self.s["WARP_PTR"].astype(np.int64)
+        nw = self.P.hdr["nw"]
+        out = []
+        for w in range(nw):
+            i, end = wp[c + w], wp[c + w + 1]
+            recs = []
+            while i < end:
+                h = st[i]
+                n = h[1] if k != PH["KSEL"] else (h[2] & 0xFFFF) + (h[2] >> 16)
+                recs.append((h, st[i + 1:i + 1 + n]))
+                i += 1 + n
+            out.append(recs)
+        return out
+
+    def entries(self, ent):
+        rows = (ent & 0xFFFF).astype(np.int64)
+        w = (ent.astype(np.uint32) & 0xFFFF0000).view(np.float32)
+        acc = np.zeros(self.B, np.float32)
+        for r, ww in zip(rows, w):
+            acc = acc + ww * self.X[r]
+        return acc
+
     def row(self, r, m=slice(None)):
-        return np.zeros(self.X[0, m].shape, np.float32) if r == NONE else self.X[r, m]
+        return self.X[r, m]
 
     def step(self, x: np.ndarray) -> np.ndarray:
         """Step mode on x [B, D] (in place)."""
         s = self.s
         for ph in s["STEP_PROG"]:
             k, a, b, c = (int(ph[f]) for f in ("kind", "a", "b", "c"))
+            k &= 0xFF
             if k == PH["END"]:
                 break
             if k == PH["ZERO"]:
@@ -71,34 +99,53 @@ class PlanInterp:
                     if ml >= 3:
                         H[2, e] = h[1]
             elif k == PH["FORMS"]:
-                for f in s["FORMS"][a:b]:
-                    self.X[f["dst"]] = self.form(int(f["nnz0"]), int(f["nnz4"]))
+                for recs in self.warp_records(c, k):
+                    for h, q in recs:
+                        ent = q.reshape(-1)
+                        self.X[h[0]] = self.entries(ent)
             elif k == PH["UNITS"]:
                 x0 = self.X[self.one]
-                for nd in s["NODES"][a:b]:
-                    acc = np.zeros(self.B, np.float32)
-                    for u in s["UNITS"][nd["u0"]:nd["u0"] + nd["nu"]]:
-                        av = self.row(u["a"]) + u["ca"] * x0
-                        bv = self.row(u["b"]) + u["cb"] * x0
-                        acc = acc + (u["coef"] * av) * np.maximum(bv, 0)
-                    self.X[nd["out"]] = self.X[nd["out"]] + acc
+                for recs in self.warp_records(c, k):
+                    for h, q in recs:
+                        acc = np.zeros(self.B, np.float32)
+                        for un in q:
+                            coef, ca, cb = (np.uint32(v).view(np.float32) for v in un[:3])
+                            av = self.row(int(un[3]) & 0xFFFF) + ca * x0
+                            bv = self.row(int(un[3]) >> 16) + cb * x0
+                            acc = acc + (coef * av) * np.maximum(bv, 0)
+                        self.X[h[0]] = self.X[h[0]] + acc
             elif k == PH["KSEL"]:
-                self.ksel, self.qsel = {}, {}
                 x0 = self.X[self.one]
-                for kh in s["KHEADS"][a:b]:
-                    ch = int(kh["chan"])
-                    kr, qr = s["KQ_ROW"][ch:ch + 128], s["KQ_ROW"][ch + 128:ch + 256]
-                    kc, qc = s["KQ_C"][ch:ch + 128], s["KQ_C"][ch + 128:ch + 256]
-                    kv = np.stack([np.maximum(self.row(int(r)) + cc * x0, 0) for r, cc in zip(kr, kc)])
-                    qv = np.stack([np.maximum(self.row(int(r)) + cc * x0, 0) for r, cc in zip(qr, qc)])
-                    km, ka = kv.max(0), kv.argmax(0)
-                    self.ksel[int(kh["slot"])] = np.where(km > 0, ka, -1)
-                    sel = []
-                    for j in range(int(kh["qhot"])):
-                        qm, qa = qv.max(0), qv.argmax(0)
-                        sel.append(np.where(qm > 0, qa, -1))
-                        qv[qa, np.arange(self.B)] = 0
-                    self.qsel[int(kh["slot"])] = sel
+                for recs in self.warp_records(c, k):
+                    for h, q in recs:
+                        slot, qhot = int(h[0]) & 0xFFFF, int(h[0]) >> 16
+                        nk, nq = int(h[2]) & 0xFFFF, int(h[2]) >> 16
+
+                        def chans(quads, com, x1):
+                            if not len(quads):
+                                return np.zeros((128, self.B), np.float32)
+                            mask = [int(w) for w in quads[0]]
+                            vals = []
+                            for i, qq in enumerate(quads[1:]):
+                                for half, (e, cc) in enumerate(((qq[0], qq[1]), (qq[2], qq[3]))):
+                                    ch = 2 * i + half
+                                    e = int(e)
+                                    c1 = np.uint32(e & 0xFFFF0000).view(np.float32)
+                                    ex = (mask[ch // 32] >> (ch % 32)) & 1
+                                    v = (self.X[e & 0xFFFF] + (com if ex else 0)) + np.uint32(cc).view(np.float32) * x0 + c1 * x1
+                                    vals.append(np.maximum(v, 0))
+                            return np.stack(vals)
+
+                        kv = chans(q[:nk], self.X[int(h[1]) & 0xFFFF], self.X[int(h[3]) & 0xFFFF])
+                        qv = chans(q[nk:nk + nq], self.X[int(h[1]) >> 16], self.X[int(h[3]) >> 16])
+                        km, ka = kv.max(0), kv.argmax(0)
+                        self.ksel[slot] = np.where(km > 0, ka, -1)
+                        sel = []
+                        for j in range(qhot):
+                            qm, qa = qv.max(0), qv.argmax(0)
+                            sel.append(np.where(qm > 0, qa, -1))
+                            qv[qa, np.arange(self.B)] = 0
+                        self.qsel[slot] = sel
             elif k == PH["VH"]:
                 x0 = self.X[self.one]
                 for vh in s["VHEADS"][a:b]:

@@ -59,31 +59,50 @@ def test_bad_plans_are_rejected():
 
 
 def test_plan_is_consistent(graph):
-    from qwenputer_b200.plan import PH, compile_plan
+    from qwenputer_b200.plan import PH, RING_QUADS, SMEM_MAX, compile_plan, smem_extra_bytes
 
     P = compile_plan(graph)
     s = P.sec
-    rows = P.hdr["n_slots"] + P.hdr["n_scratch"]
-    # every packed entry and destination addresses a shared-memory row
-    assert int((s["NNZ"] & 0xFFFF).max()) < rows
-    assert int(s["FORMS"]["dst"].max()) < rows
-    assert int(s["NODES"]["out"].max()) < rows
-    assert all(r < rows or r == 0xFFFF for r in s["UNITS"]["a"]) and all(r < rows or r == 0xFFFF for r in s["UNITS"]["b"])
-    # forms' entries lie inside the packed array and are 16-byte aligned
-    assert np.all(s["FORMS"]["nnz0"] % 4 == 0)
-    assert np.all(s["FORMS"]["nnz0"] + 4 * s["FORMS"]["nnz4"].astype(np.int64) <= len(s["NNZ"]))
-    # each run program ends with the decode and END, warp ranges are monotone
-    kinds = list(s["RUN_PROG"]["kind"])
-    assert kinds[-2:] == [PH["DECODE"], PH["END"]] and kinds.count(PH["END"]) == 1
+    rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * 33  # word offsets, zero row included
+    nw = P.hdr["nw"]
+    st = s["STREAM"].astype(np.int64)
     wp = s["WARP_PTR"].astype(np.int64)
+    # walk every stream record of every phase: rows in range, records end on their warp's range
     for ph in s["RUN_PROG"]:
-        if ph["kind"] in (PH["FORMS"], PH["UNITS"]):
-            seg = wp[ph["c"]:ph["c"] + P.hdr["nw"] + 1]
-            assert np.all(np.diff(seg) >= 0) and seg[0] == ph["a"] and seg[-1] == ph["b"]
-    # 99 snapshot tables, the plan fits the shared memory of one CTA
+        k = int(ph["kind"]) & 0xFF
+        if k not in (PH["FORMS"], PH["UNITS"], PH["KSEL"]):
+            continue
+        seg = wp[ph["c"]:ph["c"] + nw + 1]
+        assert np.all(np.diff(seg) >= 0)
+        for w in range(nw):
+            i, end = seg[w], seg[w + 1]
+            while i < end:
+                h = st[i]
+                if k == PH["FORMS"]:
+                    assert h[0] < rows
+                    ent = st[i + 1:i + 1 + h[1]].reshape(-1)
+                    assert np.all((ent & 0xFFFF) < rows)
+                    i += 1 + h[1]
+                elif k == PH["UNITS"]:
+                    assert h[0] < rows
+                    u = st[i + 1:i + 1 + h[1]]
+                    for r in np.concatenate([u[:, 3] & 0xFFFF, u[:, 3] >> 16]):
+                        assert r < rows or r == 0xFFFF
+                    i += 1 + h[1]
+                else:
+                    nk, nq = h[2] & 0xFFFF, h[2] >> 16
+                    assert nk in (0, 65) and nq in (0, 65) and (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"]
+                    c = np.concatenate([st[i + 2:i + 1 + nk], st[i + 2 + nk:i + 1 + nk + nq]])
+                    for r in np.concatenate([c[:, 0] & 0xFFFF, c[:, 2] & 0xFFFF]):
+                        assert r < rows or r == 0xFFFF
+                    i += 1 + nk + nq
+            assert i == end
+    kinds = [int(k) & 0xFF for k in s["RUN_PROG"]["kind"]]
+    assert kinds[-2:] == [PH["DECODE"], PH["END"]] and kinds.count(PH["END"]) == 1
     assert len(s["TABLES"]) == 198
-    smem = rows * 33 * 4 + P.hdr["n_ksel_slots"] * 32 * (1 + P.hdr["qhot_max"]) * 4 + 32 * 18 * 4 + 64
-    assert smem <= 232448, smem
+    smem = (P.hdr["n_slots"] + P.hdr["n_scratch"]) * 33 * 4 + smem_extra_bytes(P.hdr["n_ksel_slots"], P.hdr["qhot_max"], nw)
+    assert smem <= SMEM_MAX, smem
+    assert RING_QUADS == 32
     assert P.hdr["n_born0"] == P.hdr["n_feat"]
     assert list(s["PAIRS"][:P.hdr["n_born0"], 1]) == [int(d) for d in graph.feat_dims]
 
@@ -94,4 +113,4 @@ def test_plan_residual_slots_never_collide(graph):
 
     P = compile_plan(graph)
     assert P.hdr["n_slots"] < 1500
-    assert P.stats["form_nnz"] < 400_000
+    assert P.stats["form_nnz"] < 150_000
