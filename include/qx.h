@@ -67,8 +67,11 @@ typedef struct {
 /* Stream records (uint4 quads), consumed per warp in order.  Every row field is a shared-memory
  * word offset (row * 33); the row after the last one is kept at zero and stands for "no form".
  *   form      [dst, n entry quads, 0, 0] + entry quads of 4 entries (row | bf16 w << 16)
- *   FFN node  [out, n units, 0, 0] + units [coef, ca, cb, a | b << 16]:
- *             X[out] += sum coef * (F[a] + ca x0) * relu(F[b] + cb x0)
+ *   FFN node  [out, n groups, n quads, 0] + groups of units sharing their forms (a, b):
+ *             constant a: [a | b << 16, n, k, cb] + (n - 1) / 2 quads [k, cb, k, cb]: each unit
+ *                         k x0 relu(F[b] + cb x0), k = coef * ca (pad units have k = 0)
+ *             a form:     [a | b << 16, n | 1 << 16, 0, 0] + n quads [coef, ca, cb, 0]: each
+ *                         unit coef (F[a] + ca x0) relu(F[b] + cb x0); X[out] += the sum
  *   key head  [slot | qhot << 16, k common | q common << 16, nk | nq << 16, k lag-ONE | q lag-ONE
  *             << 16] + (if nk) a quad of the key channels' existence mask and 64 key quads, then
  *             (if nq) the same for the queries; two channels a quad [row | bf16 c1 << 16, c0, ..]:
@@ -147,7 +150,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 3
+#define QX_PLAN_VERSION 4
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

@@ -230,13 +230,32 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
                 while (st.more()) {
-                    const uint4 h = st.next();
+                    const uint4 h = st.next();  // [out, groups, quads, 0]
                     float acc = 0.0f;
-                    for (uint32_t u = 0; u < h.y; u++) {
-                        const uint4 un = st.next();
-                        const float av = fmaf(__uint_as_float(un.y), x0, sml[un.w & 0xFFFFu]);
-                        const float bv = fmaf(__uint_as_float(un.z), x0, sml[un.w >> 16]);
-                        acc += __fmul_rn(__fmul_rn(__uint_as_float(un.x), av), relu(bv));
+                    for (uint32_t gi = 0; gi < h.y; gi++) {
+                        const uint4 gq = st.next();
+                        const uint32_t n = gq.y & 0xFFFFu;
+                        const float fb = sml[gq.x >> 16];
+                        if (!(gq.y >> 16)) {
+                            // constant a: k x0 relu(F[b] + cb x0), the first unit in the header
+                            acc += __fmul_rn(__fmul_rn(__uint_as_float(gq.z), x0),
+                                             relu(fmaf(__uint_as_float(gq.w), x0, fb)));
+                            for (uint32_t u = 1; u < n; u += 2) {
+                                const uint4 q = st.next();
+                                acc += __fmul_rn(__fmul_rn(__uint_as_float(q.x), x0),
+                                                 relu(fmaf(__uint_as_float(q.y), x0, fb)));
+                                acc += __fmul_rn(__fmul_rn(__uint_as_float(q.z), x0),
+                                                 relu(fmaf(__uint_as_float(q.w), x0, fb)));
+                            }
+                        } else {
+                            const float fa = sml[gq.x & 0xFFFFu];
+                            for (uint32_t u = 0; u < n; u++) {
+                                const uint4 q = st.next();
+                                const float av = fmaf(__uint_as_float(q.y), x0, fa);
+                                const float bv = fmaf(__uint_as_float(q.z), x0, fb);
+                                acc += __fmul_rn(__fmul_rn(__uint_as_float(q.x), av), relu(bv));
+                            }
+                        }
                     }
                     atomicAdd(&sml[h.x], acc);  // records into one row may meet
                 }

@@ -28,7 +28,9 @@ import numpy as np
 from . import graphfile
 from .plan import compile_plan
 
-LIB_PATH = Path(__file__).resolve().parent / "libqx.so"
+import os
+
+LIB_PATH = Path(os.environ.get("QX_LIBRARY") or Path(__file__).resolve().parent / "libqx.so")
 HD = 128
 _lib = None
 _plans: dict = {}

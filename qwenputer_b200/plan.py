@@ -30,8 +30,12 @@ Stream records (all fields little-endian uint32; "row" fields are shared-memory 
 row * 33, so the kernel adds them to its lane's base without a multiply):
   form      [dst, n entry quads, 0, 0] + entry quads (4 entries: row | bf16 weight << 16;
             padding entries read the zero row with weight +0)
-  FFN node  [out, n units, 0, 0] + unit quads [coef, ca, cb, a | b << 16] (a node may be split
-            into several records that add into the same row)
+  FFN node  [out, n groups, n quads, 0] + per group of units sharing their (a, b) forms:
+              constant a: [a | b << 16, n, k, cb] + (n - 1) / 2 quads [k, cb, k, cb], where
+                          k = coef * ca and the unit is k x0 relu(F[b] + cb x0)
+              a form:     [a | b << 16, n | 1 << 16, 0, 0] + n quads [coef, ca, cb, 0], the unit
+                          coef (F[a] + ca x0) relu(F[b] + cb x0)
+            (a node may be split into several records that add into the same row)
   key head  [slot | qhot << 16, k common | q common << 16, nk | nq << 16,
              k lag-ONE row | q lag-ONE row << 16] + a quad of the 128-bit existence mask of the
             key channels and one of the query channels (when nk / nq > 0), then nk key quads and
@@ -52,7 +56,7 @@ from .graphfile import HD, ONE, GraphData
 NONE = 0xFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 3
+VERSION = 4
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -372,18 +376,46 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 frow = {f: W(free[i]) for f, i in gforms.items()}
                 recs, costs = [], []
                 for n in gnodes:
-                    q = []
+                    # units grouped by their (a, b) forms; a constant-a unit is (k, cb) with
+                    # k = coef * ca rounded as the reference rounds coef * a when a = ca * 1
+                    grp: dict = {}
                     for u in range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1])):
                         (ta, ca), (tb, cb) = unit_a[u], unit_b[u]
+                        grp.setdefault((ta, tb), []).append((float(g.unit_coef[u]), ca, cb))
+                    out = W(xrow(lv, int(g.ffn_out[n])))
+                    chunks, cur_q, cur_g, cur_u = [], [], 0, 0
+
+                    def flush():
+                        nonlocal cur_q, cur_g, cur_u
+                        if cur_g:
+                            chunks.append(([(out, cur_g, len(cur_q), 0)] + cur_q, cur_u, cur_g))
+                        cur_q, cur_g, cur_u = [], 0, 0
+
+                    for (ta, tb), us in grp.items():
                         ra = frow[ta] if ta else ZW
                         rb = frow[tb] if tb else ZW
-                        q.append((_fbits(g.unit_coef[u]), _fbits(ca), _fbits(cb), ra | rb << 16))
-                    out = W(xrow(lv, int(g.ffn_out[n])))
-                    for c0 in range(0, len(q), UNIT_CHUNK):
-                        part = q[c0:c0 + UNIT_CHUNK]
-                        recs.append([(out, len(part), 0, 0)] + part)
-                        costs.append(16 * len(part) + 14)
-                    stats["units"] += len(q)
+                        for c0 in range(0, len(us), UNIT_CHUNK):
+                            part = us[c0:c0 + UNIT_CHUNK]
+                            if cur_u + len(part) > UNIT_CHUNK:
+                                flush()
+                            if ta:
+                                qs = [(ra | rb << 16, len(part) | 1 << 16, 0, 0)]
+                                qs += [(_fbits(cf), _fbits(ca), _fbits(cb), 0) for cf, ca, cb in part]
+                            else:
+                                ks = [(_fbits(np.float32(cf) * np.float32(ca)), _fbits(cb)) for cf, ca, cb in part]
+                                qs = [(ra | rb << 16, len(part), ks[0][0], ks[0][1])]
+                                rest = ks[1:] + ([(0, 0)] if len(ks[1:]) % 2 else [])
+                                qs += [(rest[i][0], rest[i][1], rest[i + 1][0], rest[i + 1][1])
+                                       for i in range(0, len(rest), 2)]
+                            cur_q += qs
+                            cur_g += 1
+                            cur_u += len(part)
+                    flush()
+                    for rec, nu, ng in chunks:
+                        recs.append(rec)
+                        costs.append(6 * nu + 10 * ng + 14)
+                    stats["units"] += int(g.ffn_uptr[n + 1] - g.ffn_uptr[n])
+                    stats["unit_groups"] += len(grp)
                 stream_phase(PH["UNITS"], recs, costs, body)
             group_stats.append((lv, "ffn", len(groups)))
         else:

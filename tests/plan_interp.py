@@ -48,7 +48,7 @@ class PlanInterp:
             recs = []
             while i < end:
                 h = st[i]
-                n = h[1] if k != PH["KSEL"] else (h[2] & 0xFFFF) + (h[2] >> 16)
+                n = h[1] if k == PH["FORMS"] else (h[2] if k == PH["UNITS"] else (h[2] & 0xFFFF) + (h[2] >> 16))
                 recs.append((h, st[i + 1:i + 1 + n]))
                 i += 1 + n
             out.append(recs)
@@ -105,14 +105,30 @@ class PlanInterp:
                         self.X[h[0]] = self.entries(ent)
             elif k == PH["UNITS"]:
                 x0 = self.X[self.one]
+                f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
                     for h, q in recs:
                         acc = np.zeros(self.B, np.float32)
-                        for un in q:
-                            coef, ca, cb = (np.uint32(v).view(np.float32) for v in un[:3])
-                            av = self.row(int(un[3]) & 0xFFFF) + ca * x0
-                            bv = self.row(int(un[3]) >> 16) + cb * x0
-                            acc = acc + (coef * av) * np.maximum(bv, 0)
+                        i = 0
+                        for _ in range(int(h[1])):
+                            gq = q[i]
+                            i += 1
+                            ra, rb = int(gq[0]) & 0xFFFF, int(gq[0]) >> 16
+                            n, has_a = int(gq[1]) & 0xFFFF, int(gq[1]) >> 16
+                            fb = self.X[rb]
+                            if not has_a:
+                                ks = [(gq[2], gq[3])]
+                                for _ in range((n - 1 + 1) // 2):
+                                    ks += [(q[i][0], q[i][1]), (q[i][2], q[i][3])]
+                                    i += 1
+                                for kk, cb in ks[:n]:
+                                    acc = acc + (f32(kk) * x0) * np.maximum(fb + f32(cb) * x0, 0)
+                            else:
+                                fa = self.X[ra]
+                                for _ in range(n):
+                                    coef, ca, cb = (f32(v) for v in q[i][:3])
+                                    i += 1
+                                    acc = acc + (coef * (fa + ca * x0)) * np.maximum(fb + cb * x0, 0)
                         self.X[h[0]] = self.X[h[0]] + acc
             elif k == PH["KSEL"]:
                 x0 = self.X[self.one]

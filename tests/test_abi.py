@@ -85,10 +85,16 @@ def test_plan_is_consistent(graph):
                     i += 1 + h[1]
                 elif k == PH["UNITS"]:
                     assert h[0] < rows
-                    u = st[i + 1:i + 1 + h[1]]
-                    for r in np.concatenate([u[:, 3] & 0xFFFF, u[:, 3] >> 16]):
-                        assert r < rows or r == 0xFFFF
-                    i += 1 + h[1]
+                    j, n_g = i + 1, 0
+                    while j < i + 1 + h[2]:
+                        gq = st[j]
+                        for r in (gq[0] & 0xFFFF, gq[0] >> 16):
+                            assert r < rows
+                        n, has_a = gq[1] & 0xFFFF, gq[1] >> 16
+                        j += 1 + (n if has_a else n // 2)
+                        n_g += 1
+                    assert j == i + 1 + h[2] and n_g == h[1]
+                    i += 1 + h[2]
                 else:
                     nk, nq = h[2] & 0xFFFF, h[2] >> 16
                     assert nk in (0, 65) and nq in (0, 65) and (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"]
