@@ -95,9 +95,9 @@ typedef struct {        /* value head task */
     float ca, cb, bconst;
 } qx_vhead;
 
-typedef struct {        /* a per-column lazily evaluated form (v or z): relu(sum + c x0) */
-    uint32_t nnz0;      /* first packed entry in NNZ (a multiple of 4) */
-    uint16_t nnz4;      /* entries / 4 */
+typedef struct {        /* a value head column's v or z: relu(F[row] + c x0) (F from the FORMS phase) */
+    uint32_t row;       /* shared-memory word offset of the form's row (the zero row if none) */
+    uint16_t pad;
     uint16_t live;      /* 0: the column has no form (reads 0) */
     float c;
 } qx_colform;
@@ -126,7 +126,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_ROWS,           /* uint16: row lists */
     QX_S_PAIRS,          /* uint32 pairs (row, dim) / (dst, src) */
     QX_S_STREAM,         /* uint4 quads: form, FFN node and key-head records */
-    QX_S_NNZ,            /* uint32: packed entries of the lazily evaluated v / z forms */
+    QX_S_NNZ,            /* uint32: unused (kept for the section numbering) */
     QX_S_WARP_PTR,       /* uint32: per phase, nw + 1 quad offsets into STREAM */
     QX_S_STAGES,         /* qx_stage */
     QX_S_VHEADS,         /* qx_vhead */
@@ -150,7 +150,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 4
+#define QX_PLAN_VERSION 5
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

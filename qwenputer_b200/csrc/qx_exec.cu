@@ -29,21 +29,6 @@ __device__ __forceinline__ float relu(float v) { return v > 0.0f ? v : 0.0f; }
 __device__ __forceinline__ float wbits(uint32_t e) { return __uint_as_float(e & 0xFFFF0000u); }
 __device__ __forceinline__ uint32_t obits(uint32_t e) { return e & 0xFFFFu; }
 
-// sum of w * sml[off] over packed entries read from global memory (lazy v / z forms); sml is
-// the shared memory of one machine's column (sm + machine), offsets are row * 33
-__device__ __forceinline__ float form_sum_g(const float *sml, const uint32_t *nnz, uint32_t nnz0, uint32_t nnz4) {
-    const uint4 *q = reinterpret_cast<const uint4 *>(nnz + nnz0);
-    float a0 = 0.0f, a1 = 0.0f;
-    for (uint32_t k = 0; k < nnz4; k++) {
-        const uint4 e = __ldg(q + k);
-        a0 = fmaf(wbits(e.x), sml[obits(e.x)], a0);
-        a1 = fmaf(wbits(e.y), sml[obits(e.y)], a1);
-        a0 = fmaf(wbits(e.z), sml[obits(e.z)], a0);
-        a1 = fmaf(wbits(e.w), sml[obits(e.w)], a1);
-    }
-    return a0 + a1;
-}
-
 __device__ __forceinline__ uint64_t fnv_word(uint64_t h, uint32_t w) {
 #pragma unroll
     for (int b = 0; b < 4; b++) {
@@ -331,8 +316,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
             }
             case QX_PH_VH: {
                 // per value head and quarter of the CTA's machines: lanes evaluate each
-                // machine's decay / write / read conditions, then serve the machines that touch
-                // a row one at a time with lanes over columns (4 each)
+                // machine's decay / write / read conditions; the machines that touch a row are
+                // then served four at a time with lanes over columns (4 each): first their decays
+                // and writes, then all their row reads in flight together, then the outputs
                 const uint32_t n = ph.b - ph.a;
                 for (uint32_t task = warp; task < n * 4; task += QX_NW) {
                     const qx_vhead vh = d.vheads[ph.a + task / 4];
@@ -355,66 +341,94 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     }
                     const bool need = act && (lane >> 3) == quarter && (fac != 1.0f || wrow >= 0 || anyq);
                     unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
+                    float *const Sh = d.S[vh.hl] + (size_t)vh.vh * (QX_HD * QX_HD) + lane * 4;
+                    const size_t mstride = (size_t)d.V[vh.hl] * (QX_HD * QX_HD);
                     while (mask) {
-                        const int mm = __ffs(mask) - 1;
-                        mask &= mask - 1;
-                        const int gm = mbase + mm;
-                        const float f = __shfl_sync(0xFFFFFFFFu, fac, mm);
-                        const int wr = __shfl_sync(0xFFFFFFFFu, wrow, mm);
-                        int qr[4];
+                        int mmv[4], wr[4], qr[4][4];
+                        float f[4];
+                        bool valid[4];
 #pragma unroll
-                        for (int j = 0; j < 4; j++) qr[j] = __shfl_sync(0xFFFFFFFFu, q[j], mm);
-                        const float x0m = __shfl_sync(0xFFFFFFFFu, x0, mm);
-                        const float *smm = sm + mm;  // machine mm's column
-                        float *Sb = d.S[vh.hl] + ((size_t)gm * d.V[vh.hl] + vh.vh) * (QX_HD * QX_HD) + lane * 4;
+                        for (int b = 0; b < 4; b++) {
+                            valid[b] = mask != 0;
+                            const int mm = valid[b] ? __ffs(mask) - 1 : 0;
+                            if (valid[b]) mask &= mask - 1;
+                            mmv[b] = mm;
+                            f[b] = __shfl_sync(0xFFFFFFFFu, fac, mm);
+                            wr[b] = valid[b] ? __shfl_sync(0xFFFFFFFFu, wrow, mm) : -1;
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const int v = __shfl_sync(0xFFFFFFFFu, q[j], mm);
+                                qr[b][j] = valid[b] ? v : -1;
+                            }
+                        }
                         unsigned int rows = 0;  // 512-byte row transfers
-                        if (f != 1.0f) {
-                            rows += 2 * vh.nrows;
-                            for (int r = 0; r < vh.nrows; r++) {
-                                float4 *p = reinterpret_cast<float4 *>(Sb + r * QX_HD);
-                                float4 s = *p;
-                                s.x = __fmul_rn(s.x, f); s.y = __fmul_rn(s.y, f);
-                                s.z = __fmul_rn(s.z, f); s.w = __fmul_rn(s.w, f);
-                                *p = s;
-                            }
-                        }
-                        if (wr >= 0) {
-                            float v[4];
+                        // decays and writes (each machine's own rows: program order suffices)
 #pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const qx_colform cf = d.vform[vh.col + lane * 4 + i];
-                                v[i] = cf.live ? relu(fmaf(cf.c, x0m, form_sum_g(smm, d.nnz, cf.nnz0, cf.nnz4))) : 0.0f;
+                        for (int b = 0; b < 4; b++) {
+                            if (!valid[b]) continue;
+                            float *Sb = Sh + (size_t)(mbase + mmv[b]) * mstride;
+                            if (f[b] != 1.0f) {
+                                rows += 2 * vh.nrows;
+                                for (int r = 0; r < vh.nrows; r++) {
+                                    float4 *p = reinterpret_cast<float4 *>(Sb + r * QX_HD);
+                                    float4 s = *p;
+                                    s.x = __fmul_rn(s.x, f[b]); s.y = __fmul_rn(s.y, f[b]);
+                                    s.z = __fmul_rn(s.z, f[b]); s.w = __fmul_rn(s.w, f[b]);
+                                    *p = s;
+                                }
                             }
-                            *reinterpret_cast<float4 *>(Sb + wr * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
-                            rows++;
-                        }
-                        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                        bool any = false;
+                            if (wr[b] >= 0) {
+                                const float *smm = sm + mmv[b];
+                                const float x0m = smm[d.one_row];
+                                float v[4];
 #pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            if (qr[j] >= 0) {
-                                const float4 s = *reinterpret_cast<const float4 *>(Sb + qr[j] * QX_HD);
-                                o.x = __fadd_rn(o.x, s.x); o.y = __fadd_rn(o.y, s.y);
-                                o.z = __fadd_rn(o.z, s.z); o.w = __fadd_rn(o.w, s.w);
-                                any = true;
+                                for (int i = 0; i < 4; i++) {
+                                    const qx_colform cf = d.vform[vh.col + lane * 4 + i];
+                                    v[i] = cf.live ? relu(fmaf(cf.c, x0m, smm[cf.row])) : 0.0f;
+                                }
+                                *reinterpret_cast<float4 *>(Sb + wr[b] * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
                                 rows++;
                             }
                         }
-                        if (lane == 0) atomicAdd(touched, rows);
-                        if (!any) continue;
-                        float ref = __fadd_rn(__fmul_rn(o.x, o.x), __fmul_rn(o.y, o.y));
-                        ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
-                        const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
-                        const float oc[4] = {o.x, o.y, o.z, o.w};
+                        // the reads: every machine's query rows in flight together
+                        float4 o[4];
+                        bool any[4];
 #pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const int c = lane * 4 + i;
-                            const uint16_t orow = d.out_row[vh.col + c];
-                            if (orow == QX_NONE) continue;
-                            const qx_colform zf = d.zform[vh.col + c];
-                            const float z = zf.live ? relu(fmaf(zf.c, x0m, form_sum_g(smm, d.nnz, zf.nnz0, zf.nnz4))) : 0.0f;
-                            const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
-                            atomicAdd(&sm[orow + mm], __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
+                        for (int b = 0; b < 4; b++) {
+                            o[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            any[b] = false;
+                            const float *Sb = Sh + (size_t)(mbase + mmv[b]) * mstride;
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                if (qr[b][j] >= 0) {
+                                    const float4 s = *reinterpret_cast<const float4 *>(Sb + qr[b][j] * QX_HD);
+                                    o[b].x = __fadd_rn(o[b].x, s.x); o[b].y = __fadd_rn(o[b].y, s.y);
+                                    o[b].z = __fadd_rn(o[b].z, s.z); o[b].w = __fadd_rn(o[b].w, s.w);
+                                    any[b] = true;
+                                    rows++;
+                                }
+                            }
+                        }
+                        if (lane == 0) atomicAdd(touched, rows);
+#pragma unroll
+                        for (int b = 0; b < 4; b++) {
+                            if (!any[b]) continue;
+                            const float *smm = sm + mmv[b];
+                            const float x0m = smm[d.one_row];
+                            float ref = __fadd_rn(__fmul_rn(o[b].x, o[b].x), __fmul_rn(o[b].y, o[b].y));
+                            ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
+                            const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
+                            const float oc[4] = {o[b].x, o[b].y, o[b].z, o[b].w};
+#pragma unroll
+                            for (int i = 0; i < 4; i++) {
+                                const int c = lane * 4 + i;
+                                const uint16_t orow = d.out_row[vh.col + c];
+                                if (orow == QX_NONE) continue;
+                                const qx_colform zf = d.zform[vh.col + c];
+                                const float z = zf.live ? relu(fmaf(zf.c, x0m, smm[zf.row])) : 0.0f;
+                                const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
+                                atomicAdd(&sm[orow + mmv[b]], __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
+                            }
                         }
                     }
                 }

@@ -56,7 +56,7 @@ from .graphfile import HD, ONE, GraphData
 NONE = 0xFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 4
+VERSION = 5
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -80,7 +80,7 @@ DT = {
     "vhead": np.dtype([("hl", "<u4"), ("vh", "<u4"), ("col", "<u4"), ("slot", "<u2"),
                        ("nrows", "<u2"), ("a_row", "<u2"), ("b_row", "<u2"), ("ca", "<f4"),
                        ("cb", "<f4"), ("bconst", "<f4")]),
-    "colform": np.dtype([("nnz0", "<u4"), ("nnz4", "<u2"), ("live", "<u2"), ("c", "<f4")]),
+    "colform": np.dtype([("row", "<u4"), ("pad", "<u2"), ("live", "<u2"), ("c", "<f4")]),
 }
 HEADER = struct.Struct("<QII" + "I" * 14 + "32Q32Q")
 
@@ -494,6 +494,10 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                     for fs in (af, bf):
                         if fs[j][0]:
                             nf[fs[j][0]] = 1
+                    for c in range(HD):
+                        for tab, fs in ((g.vh_v, vf), (g.vh_z, zf)):
+                            if tab[j, c] >= 0 and fs[tab[j, c]][0]:
+                                nf[fs[tab[j, c]][0]] = 1
                 new = [f for f in nf if f not in cur_forms]
                 if cur and (len(cur_forms) + len(new) > cap or len(cur) >= ksel_slots):
                     groups.append((cur, cur_forms))
@@ -547,10 +551,9 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                             for tab, fs, dstl in ((g.vh_v, vf, vform_l), (g.vh_z, zf, zform_l)):
                                 if tab[j, c] >= 0:
                                     t, cc = fs[tab[j, c]]
-                                    s_, n4 = pack_terms(t, rowmap) if t else (0, 0)
-                                    dstl.append((s_, n4, 1, cc))
+                                    dstl.append((frow[t] if t else ZW, 0, 1, cc))
                                 else:
-                                    dstl.append((0, 0, 0, 0.0))
+                                    dstl.append((ZW, 0, 0, 0.0))
                         orow = [NONE] * HD
                         ow = [0.0] * HD
                         for e in range(int(g.vh_out_ptr[j]), int(g.vh_out_ptr[j + 1])):
@@ -635,8 +638,6 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     stats["phases_run"] = len(run_prog)
     stats["barriers_run"] = sum(1 for k, *_ in run_prog if not k & NOSYNC and k != PH["END"])
     stats["stream_quads"] = len(stream)
-    stats["vform_nnz"] = sum(n4 * 4 for _, n4, _, _ in vform_l)
-    stats["zform_nnz"] = sum(n4 * 4 for _, n4, _, _ in zform_l)
     stats["weight_bytes"] = int(s["STREAM"].nbytes + s["STAGES"].nbytes + s["VHEADS"].nbytes
                                 + s["RUN_PROG"].nbytes + s["WARP_PTR"].nbytes)
     stats["imbalance"] = (stats["imbalance_sum"] / stats["balanced_sum"]) if stats["balanced_sum"] else 0

@@ -180,7 +180,7 @@ class PlanInterp:
                             for cc in range(128):
                                 cf = s["VFORM"][col + cc]
                                 if cf["live"]:
-                                    vals[cc] = max(self.form(int(cf["nnz0"]), int(cf["nnz4"]), m) + cf["c"] * x0[m], 0)
+                                    vals[cc] = max(self.X[int(cf["row"]), m] + cf["c"] * x0[m], 0)
                             Sb[kr] = vals
                         o = np.zeros(128, np.float32)
                         anyr = False
@@ -197,7 +197,7 @@ class PlanInterp:
                             if orow == NONE:
                                 continue
                             zf = s["ZFORM"][col + cc]
-                            z = max(self.form(int(zf["nnz0"]), int(zf["nnz4"]), m) + zf["c"] * x0[m], 0) if zf["live"] else 0
+                            z = max(self.X[int(zf["row"]), m] + zf["c"] * x0[m], 0) if zf["live"] else 0
                             out = o[cc] / norm if ref > 0 else np.float32(0)
                             self.X[orow, m] += np.float32(out * np.float32(z)) * s["OUT_W"][col + cc]
         return x
