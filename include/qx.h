@@ -43,11 +43,11 @@ typedef struct qx_executor qx_t;
 
 #define QX_PLAN_MAGIC 0x314E414C50585151ull /* "QQXPLAN1" */
 #define QX_MPC 32                          /* machines per CTA: one per lane */
-#define QX_NONE 0xFFFFu                    /* "no row" in 16-bit row fields */
+#define QX_NONE32 0xFFFFFFFFu              /* "no row" in row fields */
 
 enum { /* phase kinds of the per-token program */
-    QX_PH_ZERO = 1,     /* X rows [a, a + b) of the row list: set to 0 */
-    QX_PH_LOADX = 2,    /* step mode: X[row] = x[machine][dim] for pairs [a, a + b) */
+    QX_PH_ZERO = 1,     /* rows [a, a + b) of the row list: set to 0 */
+    QX_PH_LOADX = 2,    /* step mode: X[row] = x[machine][dim] for (row, dim) pairs [a, a + b) */
     QX_PH_STAGE = 3,    /* lag history of head sublayer c: entries [a, a + b) */
     QX_PH_FORMS = 4,    /* form records of the stream; warp w reads quads warp_ptr[c + w ..] */
     QX_PH_UNITS = 5,    /* FFN node records of the stream; warp ranges at warp_ptr[c] */
@@ -65,24 +65,24 @@ typedef struct {
 } qx_phase;
 
 /* Stream records (uint4 quads), consumed per warp in order.  Every row field is a shared-memory
- * word offset (row * 33); the row after the last one is kept at zero and stands for "no form".
- *   form      [dst, n entry quads, 0, 0] + entry quads of 4 entries (row | bf16 w << 16)
+ * byte offset (row * 132); the row after the last one is kept at zero and stands for "no form".
+ *   form      [dst, n entry quads, 0, 0] + quads of two entries [row, w, row, w] (fp32 w):
+ *             F[dst] = sum w X[row]
  *   FFN node  [out, n groups, n quads, 0] + groups of units sharing their forms (a, b):
- *             constant a: [a | b << 16, n, k, cb] + (n - 1) / 2 quads [k, cb, k, cb]: each unit
- *                         k x0 relu(F[b] + cb x0), k = coef * ca (pad units have k = 0)
- *             a form:     [a | b << 16, n | 1 << 16, 0, 0] + n quads [coef, ca, cb, 0]: each
- *                         unit coef (F[a] + ca x0) relu(F[b] + cb x0); X[out] += the sum
- *   key head  [slot | qhot << 16, k common | q common << 16, nk | nq << 16, k lag-ONE | q lag-ONE
- *             << 16] + (if nk) a quad of the key channels' existence mask and 64 key quads, then
- *             (if nq) the same for the queries; two channels a quad [row | bf16 c1 << 16, c0, ..]:
+ *             constant a: [a, b, n, 0] + (n + 1) / 2 quads [k, cb, k, cb]: each unit
+ *                         k x0 relu(F[b] + cb x0), k = coef * ca (a padding unit has k = 0)
+ *             a form:     [a, b, n | 1 << 31, 0] + n quads [coef, ca, cb, 0]: each unit
+ *                         coef (F[a] + ca x0) relu(F[b] + cb x0); X[out] += the sum
+ *   key head  [slot | qhot << 16, k common, q common, nk | nq << 16], [k lag-ONE row, q lag-ONE
+ *             row, 0, 0], then nk key-channel quads and nq query-channel quads
+ *             [row | exists << 31, c0, c1, 0]:
  *             channel = relu(F[row] + (exists ? F[common] : 0) + c0 x0 + c1 x0(t - lag)) */
 
 typedef struct {        /* lag history entry of a head sublayer */
     uint32_t e;         /* index into that sublayer's history rows */
-    uint16_t x_row;     /* X row of the dim (the value that becomes lag 1) */
-    uint16_t ml;        /* deepest lag kept (1..3) */
-    uint16_t stage[3];  /* scratch row receiving lag 1, 2, 3 (QX_NONE: not read) */
-    uint16_t pad;
+    uint32_t x_row;     /* byte offset of the dim's row (the value that becomes lag 1) */
+    uint32_t ml;        /* deepest lag kept (1..3) */
+    uint32_t stage[3];  /* byte offset of the row receiving lag 1, 2, 3 (~0u: not read) */
 } qx_stage;
 
 typedef struct {        /* value head task */
@@ -91,12 +91,12 @@ typedef struct {        /* value head task */
     uint32_t col;       /* offset into the per-column tables ([128] each) */
     uint16_t slot;      /* KSEL slot of its key head */
     uint16_t nrows;     /* decaying rows (0: the head never decays) */
-    uint16_t a_row, b_row;
+    uint32_t a_row, b_row;  /* byte offsets of the decay selector and write gate forms */
     float ca, cb, bconst;
 } qx_vhead;
 
 typedef struct {        /* a value head column's v or z: relu(F[row] + c x0) (F from the FORMS phase) */
-    uint32_t row;       /* shared-memory word offset of the form's row (the zero row if none) */
+    uint32_t row;       /* shared-memory byte offset of the form's row (the zero row if none) */
     uint16_t pad;
     uint16_t live;      /* 0: the column has no form (reads 0) */
     float c;
@@ -108,7 +108,7 @@ typedef struct {
     uint32_t n_slots, n_scratch;   /* X rows, scratch rows (smem rows of 33 floats each) */
     uint32_t nw;                   /* warps per CTA the warp ranges were balanced for */
     uint32_t n_head_levels;
-    uint32_t one_row;              /* X row of the constant-one dim */
+    uint32_t one_row;              /* byte offset of the constant-one dim's row */
     uint32_t n_ksel_slots;         /* key-head slots one KSEL phase may fill */
     uint32_t qhot_max;
     uint32_t n_fam, n_pay, n_feat, n_emb_rows, n_families;
@@ -123,7 +123,7 @@ typedef struct {
 enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_RUN_PROG = 0,   /* qx_phase: the run-mode program of one token */
     QX_S_STEP_PROG,      /* qx_phase: the step-mode program */
-    QX_S_ROWS,           /* uint16: row lists */
+    QX_S_ROWS,           /* uint32: row lists (byte offsets) */
     QX_S_PAIRS,          /* uint32 pairs (row, dim) / (dst, src) */
     QX_S_STREAM,         /* uint4 quads: form, FFN node and key-head records */
     QX_S_NNZ,            /* uint32: unused (kept for the section numbering) */
@@ -132,13 +132,13 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_VHEADS,         /* qx_vhead */
     QX_S_VFORM,          /* qx_colform [vheads][128] */
     QX_S_ZFORM,          /* qx_colform [vheads][128] */
-    QX_S_OUT_ROW,        /* uint16 [vheads][128] (QX_NONE: no output) */
+    QX_S_OUT_ROW,        /* uint32 [vheads][128] byte offsets (~0u: no output) */
     QX_S_OUT_W,          /* float  [vheads][128] */
     QX_S_HL_V,           /* uint32 [head levels]: value heads of each head sublayer */
     QX_S_HL_NE,          /* uint32 [head levels]: lag-history rows of each head sublayer */
-    QX_S_FAM_ROW,        /* uint16 [n_fam]: X rows of the family-id code bits */
-    QX_S_PAY_ROW,        /* uint16 [n_pay]: X rows of the payload code bits */
-    QX_S_FEAT_ROW,       /* uint16 [n_feat]: X rows of ONE and the token features */
+    QX_S_FAM_ROW,        /* uint32 [n_fam]: rows of the family-id code bits */
+    QX_S_PAY_ROW,        /* uint32 [n_pay]: rows of the payload code bits */
+    QX_S_FEAT_ROW,       /* uint32 [n_feat]: rows of ONE and the token features */
     QX_S_FAM_IDS,        /* int32 [n_families]: first token of each family */
     QX_S_FAM_SIZE,       /* int32 [n_families] */
     QX_S_FAM_ROW0,       /* int32 [n_families]: first table row (small families), -1 big */
@@ -150,7 +150,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 5
+#define QX_PLAN_VERSION 6
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

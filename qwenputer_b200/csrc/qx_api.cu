@@ -98,11 +98,11 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
     if (h.n_born0 != h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
     const SecSpec specs[] = {
-        {QX_S_RUN_PROG, sizeof(qx_phase)}, {QX_S_STEP_PROG, sizeof(qx_phase)}, {QX_S_ROWS, 2},
+        {QX_S_RUN_PROG, sizeof(qx_phase)}, {QX_S_STEP_PROG, sizeof(qx_phase)}, {QX_S_ROWS, 4},
         {QX_S_PAIRS, 8}, {QX_S_STREAM, 16}, {QX_S_NNZ, 4}, {QX_S_WARP_PTR, 4},
         {QX_S_STAGES, sizeof(qx_stage)}, {QX_S_VHEADS, sizeof(qx_vhead)},
-        {QX_S_VFORM, sizeof(qx_colform)}, {QX_S_ZFORM, sizeof(qx_colform)}, {QX_S_OUT_ROW, 2}, {QX_S_OUT_W, 4},
-        {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 2}, {QX_S_PAY_ROW, 2}, {QX_S_FEAT_ROW, 2},
+        {QX_S_VFORM, sizeof(qx_colform)}, {QX_S_ZFORM, sizeof(qx_colform)}, {QX_S_OUT_ROW, 4}, {QX_S_OUT_W, 4},
+        {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 4}, {QX_S_PAY_ROW, 4}, {QX_S_FEAT_ROW, 4},
         {QX_S_FAM_IDS, 4}, {QX_S_FAM_SIZE, 4}, {QX_S_FAM_ROW0, 4}, {QX_S_EMB_BASE, 4}, {QX_S_EMB_BITS, 4},
         {QX_S_EMB_TABLE, 4}, {QX_S_TABLES, 4}, {QX_S_REG_COLS, 4}};
     for (const SecSpec &s : specs) {
@@ -153,7 +153,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     QxDev &d = ex->d;
     d.run_prog = sec<qx_phase>(ex, QX_S_RUN_PROG);
     d.step_prog = sec<qx_phase>(ex, QX_S_STEP_PROG);
-    d.rows = sec<uint16_t>(ex, QX_S_ROWS);
+    d.rows = sec<uint32_t>(ex, QX_S_ROWS);
     d.pairs = sec<uint2>(ex, QX_S_PAIRS);
     d.stream = sec<uint4>(ex, QX_S_STREAM);
     d.nnz = sec<uint32_t>(ex, QX_S_NNZ);
@@ -162,11 +162,11 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.vheads = sec<qx_vhead>(ex, QX_S_VHEADS);
     d.vform = sec<qx_colform>(ex, QX_S_VFORM);
     d.zform = sec<qx_colform>(ex, QX_S_ZFORM);
-    d.out_row = sec<uint16_t>(ex, QX_S_OUT_ROW);
+    d.out_row = sec<uint32_t>(ex, QX_S_OUT_ROW);
     d.out_w = sec<float>(ex, QX_S_OUT_W);
-    d.fam_row = sec<uint16_t>(ex, QX_S_FAM_ROW);
-    d.pay_row = sec<uint16_t>(ex, QX_S_PAY_ROW);
-    d.feat_row = sec<uint16_t>(ex, QX_S_FEAT_ROW);
+    d.fam_row = sec<uint32_t>(ex, QX_S_FAM_ROW);
+    d.pay_row = sec<uint32_t>(ex, QX_S_PAY_ROW);
+    d.feat_row = sec<uint32_t>(ex, QX_S_FEAT_ROW);
     d.fam_ids = sec<int32_t>(ex, QX_S_FAM_IDS);
     d.fam_size = sec<int32_t>(ex, QX_S_FAM_SIZE);
     d.fam_row0 = sec<int32_t>(ex, QX_S_FAM_ROW0);

@@ -26,9 +26,6 @@ namespace {
 
 __device__ __forceinline__ float relu(float v) { return v > 0.0f ? v : 0.0f; }
 
-__device__ __forceinline__ float wbits(uint32_t e) { return __uint_as_float(e & 0xFFFF0000u); }
-__device__ __forceinline__ uint32_t obits(uint32_t e) { return e & 0xFFFFu; }
-
 __device__ __forceinline__ uint64_t fnv_word(uint64_t h, uint32_t w) {
 #pragma unroll
     for (int b = 0; b < 4; b++) {
@@ -108,7 +105,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint4 *ring = reinterpret_cast<uint4 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d)) +
                   warp * 2 * QX_RING_QUADS;
-    float *sml = sm + lane;  // this lane's machine column: row r at sml[r * 33]
+    float *sml = sm + lane;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
     if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
     if (threadIdx.x == 0) *touched = 0;
     const int m = blockIdx.x * 32 + lane;  // this lane's machine
@@ -121,7 +118,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
     if (RUN) {
         for (int i = warp; i < d.n_born0; i += QX_NW) {
             uint2 p = d.pairs[i];
-            sml[p.x] = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
+            QX_AT(sml, p.x) = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
         }
         if (warp == 0 && act) {
             hash = d.hash[m];
@@ -138,25 +135,25 @@ __global__ void __launch_bounds__(QX_NT, 1)
             if (kind == QX_PH_END) break;
             switch (kind) {
             case QX_PH_ZERO:
-                for (uint32_t i = warp; i < ph.b; i += QX_NW) sml[d.rows[ph.a + i]] = 0.0f;
+                for (uint32_t i = warp; i < ph.b; i += QX_NW) QX_AT(sml, d.rows[ph.a + i]) = 0.0f;
                 break;
             case QX_PH_LOADX:
                 for (uint32_t i = warp; i < ph.b; i += QX_NW) {
                     uint2 p = d.pairs[ph.a + i];
-                    sml[p.x] = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
+                    QX_AT(sml, p.x) = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
                 }
                 break;
             case QX_PH_WRITEOUT:
                 if (act)
                     for (uint32_t i = warp; i < ph.b; i += QX_NW) {
                         uint2 p = d.pairs[ph.a + i];
-                        d.x[(size_t)m * d.D + p.y] = sml[p.x];
+                        d.x[(size_t)m * d.D + p.y] = QX_AT(sml, p.x);
                     }
                 break;
             case QX_PH_APPLY:
                 for (uint32_t i = warp; i < ph.b; i += QX_NW) {
                     uint2 p = d.pairs[ph.a + i];
-                    sml[p.x] += sml[p.y];
+                    QX_AT(sml, p.x) += QX_AT(sml, p.y);
                 }
                 break;
             case QX_PH_STAGE: {
@@ -170,10 +167,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     float h0 = h[0];
                     float h1 = s.ml >= 2 ? h[ne * bp] : 0.0f;
                     float h2 = s.ml >= 3 ? h[2 * ne * bp] : 0.0f;
-                    if (s.stage[0] != QX_NONE) sml[s.stage[0]] = h0;
-                    if (s.stage[1] != QX_NONE) sml[s.stage[1]] = h1;
-                    if (s.stage[2] != QX_NONE) sml[s.stage[2]] = h2;
-                    h[0] = sml[s.x_row];
+                    if (s.stage[0] != QX_NONE32) QX_AT(sml, s.stage[0]) = h0;
+                    if (s.stage[1] != QX_NONE32) QX_AT(sml, s.stage[1]) = h1;
+                    if (s.stage[2] != QX_NONE32) QX_AT(sml, s.stage[2]) = h2;
+                    h[0] = QX_AT(sml, s.x_row);
                     if (s.ml >= 2) h[ne * bp] = h0;
                     if (s.ml >= 3) h[2 * ne * bp] = h1;
                 }
@@ -186,7 +183,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 st.start(d.stream, ring, b0, b1, lane);
                 while (st.more()) {
                     const uint4 h = st.next();
-                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                    float a0 = 0.0f, a1 = 0.0f;
                     int nq = (int)h.y;
                     while (nq > 0) {
                         if (st.left == 0) st.advance();
@@ -194,16 +191,14 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         const uint4 *rp = st.rp;
                         for (int j = 0; j < n; j++) {
                             const uint4 e = rp[j];
-                            a0 = fmaf(wbits(e.x), sml[obits(e.x)], a0);
-                            a1 = fmaf(wbits(e.y), sml[obits(e.y)], a1);
-                            a2 = fmaf(wbits(e.z), sml[obits(e.z)], a2);
-                            a3 = fmaf(wbits(e.w), sml[obits(e.w)], a3);
+                            a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
+                            a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
                         }
                         st.rp += n;
                         st.left -= n;
                         nq -= n;
                     }
-                    sml[h.x] = (a0 + a1) + (a2 + a3);
+                    QX_AT(sml, h.x) = a0 + a1;
                 }
                 st.finish();
                 break;
@@ -211,21 +206,19 @@ __global__ void __launch_bounds__(QX_NT, 1)
             case QX_PH_UNITS: {
                 const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
                 if (b0 == b1) break;
-                const float x0 = sml[d.one_row];
+                const float x0 = QX_AT(sml, d.one_row);
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
                 while (st.more()) {
                     const uint4 h = st.next();  // [out, groups, quads, 0]
                     float acc = 0.0f;
                     for (uint32_t gi = 0; gi < h.y; gi++) {
-                        const uint4 gq = st.next();
-                        const uint32_t n = gq.y & 0xFFFFu;
-                        const float fb = sml[gq.x >> 16];
-                        if (!(gq.y >> 16)) {
-                            // constant a: k x0 relu(F[b] + cb x0), the first unit in the header
-                            acc += __fmul_rn(__fmul_rn(__uint_as_float(gq.z), x0),
-                                             relu(fmaf(__uint_as_float(gq.w), x0, fb)));
-                            for (uint32_t u = 1; u < n; u += 2) {
+                        const uint4 gq = st.next();  // [a, b, n | has_a << 31, 0]
+                        const uint32_t n = gq.z & 0x7FFFFFFFu;
+                        const float fb = QX_AT(sml, gq.y);
+                        if (!(gq.z >> 31)) {
+                            // constant a: k x0 relu(F[b] + cb x0), two units a quad
+                            for (uint32_t u = 0; u < n; u += 2) {
                                 const uint4 q = st.next();
                                 acc += __fmul_rn(__fmul_rn(__uint_as_float(q.x), x0),
                                                  relu(fmaf(__uint_as_float(q.y), x0, fb)));
@@ -233,7 +226,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                                                  relu(fmaf(__uint_as_float(q.w), x0, fb)));
                             }
                         } else {
-                            const float fa = sml[gq.x & 0xFFFFu];
+                            const float fa = QX_AT(sml, gq.x);
                             for (uint32_t u = 0; u < n; u++) {
                                 const uint4 q = st.next();
                                 const float av = fmaf(__uint_as_float(q.y), x0, fa);
@@ -242,7 +235,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             }
                         }
                     }
-                    atomicAdd(&sml[h.x], acc);  // records into one row may meet
+                    atomicAdd(&QX_AT(sml, h.x), acc);  // records into one row may meet
                 }
                 st.finish();
                 break;
@@ -252,57 +245,44 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // when it is positive) and the query's top-qhot positive channels
                 const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
                 if (b0 == b1) break;
-                const float x0 = sml[d.one_row];
+                const float x0 = QX_AT(sml, d.one_row);
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
                 while (st.more()) {
-                    const uint4 h = st.next();
+                    const uint4 h = st.next();   // [slot | qhot << 16, k common, q common, nk | nq << 16]
+                    const uint4 h2 = st.next();  // [k lag-ONE row, q lag-ONE row, 0, 0]
                     const uint32_t slot = h.x & 0xFFFFu, qhot = h.x >> 16;
-                    const uint32_t nk = h.z & 0xFFFFu, nq = h.z >> 16;
+                    const uint32_t nk = h.w & 0xFFFFu, nq = h.w >> 16;
                     int ik = -1, npos = 0;
-                    if (nk) {
-                        const float com = sml[h.y & 0xFFFFu], x1 = sml[h.w & 0xFFFFu];
-                        const uint4 mk = st.next();
+                    {
+                        const float com = QX_AT(sml, h.y), x1 = QX_AT(sml, h2.x);
                         float bk = 0.0f;
-                        for (uint32_t i = 0; i + 1 < nk; i++) {
+                        for (uint32_t i = 0; i < nk; i++) {
                             const uint4 c = st.next();
-                            const uint32_t word = i < 16 ? mk.x : (i < 32 ? mk.y : (i < 48 ? mk.z : mk.w));
-                            const uint32_t bits = word >> ((2 * i) & 31);
-                            const float v0 = relu(fmaf(wbits(c.x), x1, fmaf(__uint_as_float(c.y), x0,
-                                                  sml[obits(c.x)] + ((bits & 1u) ? com : 0.0f))));
-                            const float v1 = relu(fmaf(wbits(c.z), x1, fmaf(__uint_as_float(c.w), x0,
-                                                  sml[obits(c.z)] + ((bits & 2u) ? com : 0.0f))));
-                            npos += (v0 > 0.0f) + (v1 > 0.0f);
-                            if (v0 > bk) { bk = v0; ik = 2 * i; }
-                            if (v1 > bk) { bk = v1; ik = 2 * i + 1; }
+                            const float v = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
+                                                 QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
+                            npos += v > 0.0f;
+                            if (v > bk) { bk = v; ik = (int)i; }
                         }
                     }
                     ksel[slot * 32 + lane] = ik;
                     if (npos > 1 && act) atomicOr(&d.err[m], QX_E_KEY);
                     float qb0 = 0.f, qb1 = 0.f, qb2 = 0.f, qb3 = 0.f;
                     int qi0 = -1, qi1 = -1, qi2 = -1, qi3 = -1, qpos = 0;
-                    if (nq) {
-                        const float com = sml[h.y >> 16], x1 = sml[h.w >> 16];
-                        const uint4 mq = st.next();
-                        for (uint32_t i = 0; i + 1 < nq; i++) {
+                    {
+                        const float com = QX_AT(sml, h.z), x1 = QX_AT(sml, h2.y);
+                        for (uint32_t i = 0; i < nq; i++) {
                             const uint4 c = st.next();
-                            const uint32_t word = i < 16 ? mq.x : (i < 32 ? mq.y : (i < 48 ? mq.z : mq.w));
-                            const uint32_t bits = word >> ((2 * i) & 31);
-#pragma unroll
-                            for (int half = 0; half < 2; half++) {
-                                const uint32_t e = half ? c.z : c.x;
-                                const float c0 = __uint_as_float(half ? c.w : c.y);
-                                float v = relu(fmaf(wbits(e), x1, fmaf(c0, x0, sml[obits(e)] +
-                                                    ((bits >> half) & 1u ? com : 0.0f))));
-                                int vi = (int)(2 * i + half);
-                                qpos += v > 0.0f;
-                                // insertion into the descending top list: a value displaces only
-                                // a strictly smaller one, so ties keep the lower channel first
-                                if (v > qb0) { float tv = qb0; int ti = qi0; qb0 = v; qi0 = vi; v = tv; vi = ti; }
-                                if (qhot > 1 && v > qb1) { float tv = qb1; int ti = qi1; qb1 = v; qi1 = vi; v = tv; vi = ti; }
-                                if (qhot > 2 && v > qb2) { float tv = qb2; int ti = qi2; qb2 = v; qi2 = vi; v = tv; vi = ti; }
-                                if (qhot > 3 && v > qb3) { qb3 = v; qi3 = vi; }
-                            }
+                            float v = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
+                                           QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
+                            int vi = (int)i;
+                            qpos += v > 0.0f;
+                            // insertion into the descending top list: a value displaces only a
+                            // strictly smaller one, so ties keep the lower channel first
+                            if (v > qb0) { float tv = qb0; int ti = qi0; qb0 = v; qi0 = vi; v = tv; vi = ti; }
+                            if (qhot > 1 && v > qb1) { float tv = qb1; int ti = qi1; qb1 = v; qi1 = vi; v = tv; vi = ti; }
+                            if (qhot > 2 && v > qb2) { float tv = qb2; int ti = qi2; qb2 = v; qi2 = vi; v = tv; vi = ti; }
+                            if (qhot > 3 && v > qb3) { qb3 = v; qi3 = vi; }
                         }
                     }
                     const int qs[4] = {qi0, qi1, qi2, qi3};
@@ -323,13 +303,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 for (uint32_t task = warp; task < n * 4; task += QX_NW) {
                     const qx_vhead vh = d.vheads[ph.a + task / 4];
                     const int quarter = task & 3;
-                    const float x0 = sml[d.one_row];
+                    const float x0 = QX_AT(sml, d.one_row);
                     float fac = 1.0f;
                     if (vh.nrows > 0) {
-                        const float av = fmaf(vh.ca, x0, sml[vh.a_row]);
+                        const float av = fmaf(vh.ca, x0, QX_AT(sml, vh.a_row));
                         fac = av == 0.0f ? 1.0f : (av == 110.0f ? 0.5f : 0.0f);
                     }
-                    const float bv = fmaf(vh.cb, x0, sml[vh.b_row]) + vh.bconst;
+                    const float bv = fmaf(vh.cb, x0, QX_AT(sml, vh.b_row)) + vh.bconst;
                     const int kr = ksel[vh.slot * 32 + lane];
                     const int wrow = (kr >= 0 && bv == 1.0f) ? kr : -1;
                     int q[4];
@@ -379,12 +359,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             }
                             if (wr[b] >= 0) {
                                 const float *smm = sm + mmv[b];
-                                const float x0m = smm[d.one_row];
+                                const float x0m = QX_ATC(smm, d.one_row);
                                 float v[4];
 #pragma unroll
                                 for (int i = 0; i < 4; i++) {
                                     const qx_colform cf = d.vform[vh.col + lane * 4 + i];
-                                    v[i] = cf.live ? relu(fmaf(cf.c, x0m, smm[cf.row])) : 0.0f;
+                                    v[i] = cf.live ? relu(fmaf(cf.c, x0m, QX_ATC(smm, cf.row))) : 0.0f;
                                 }
                                 *reinterpret_cast<float4 *>(Sb + wr[b] * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
                                 rows++;
@@ -414,7 +394,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         for (int b = 0; b < 4; b++) {
                             if (!any[b]) continue;
                             const float *smm = sm + mmv[b];
-                            const float x0m = smm[d.one_row];
+                            const float x0m = QX_ATC(smm, d.one_row);
                             float ref = __fadd_rn(__fmul_rn(o[b].x, o[b].x), __fmul_rn(o[b].y, o[b].y));
                             ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
                             const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
@@ -422,12 +402,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
 #pragma unroll
                             for (int i = 0; i < 4; i++) {
                                 const int c = lane * 4 + i;
-                                const uint16_t orow = d.out_row[vh.col + c];
-                                if (orow == QX_NONE) continue;
+                                const uint32_t orow = d.out_row[vh.col + c];
+                                if (orow == QX_NONE32) continue;
                                 const qx_colform zf = d.zform[vh.col + c];
-                                const float z = zf.live ? relu(fmaf(zf.c, x0m, smm[zf.row])) : 0.0f;
+                                const float z = zf.live ? relu(fmaf(zf.c, x0m, QX_ATC(smm, zf.row))) : 0.0f;
                                 const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
-                                atomicAdd(&sm[orow + mmv[b]], __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
+                                atomicAdd(&QX_AT(sm + mmv[b], orow), __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
                             }
                         }
                     }
@@ -438,9 +418,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 if (warp == 0) {
                     float fam = 0.0f, psum = 0.0f;
                     for (int i = 0; i < d.n_fam; i++)
-                        fam = __fadd_rn(fam, __fmul_rn(rintf(sml[d.fam_row[i]]), ldexpf(1.0f, i)));
+                        fam = __fadd_rn(fam, __fmul_rn(rintf(QX_AT(sml, d.fam_row[i])), ldexpf(1.0f, i)));
                     for (int i = 0; i < d.n_pay; i++) {
-                        const float p = rintf(sml[d.pay_row[i]]);
+                        const float p = rintf(QX_AT(sml, d.pay_row[i]));
                         dec_pay[i * 32 + lane] = p;
                         psum = __fadd_rn(psum, __fmul_rn(p, ldexpf(1.0f, i)));
                     }
@@ -463,19 +443,19 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 for (int mm = warp; mm < 32; mm += QX_NW) {
                     const int fid = dec_i[mm], p = dec_i[32 + mm];
                     const int row0 = d.fam_row0[fid];
-                    float *smm = sm + mm;
+                    float *smw = sm + mm;
                     if (row0 >= 0) {
                         int r = row0 + p;
                         r = r < 0 ? 0 : (r > d.n_emb_rows - 1 ? d.n_emb_rows - 1 : r);
                         for (int f = lane; f < d.n_feat; f += 32)
-                            smm[d.feat_row[f]] = __ldg(d.emb_table + (size_t)r * d.n_feat + f);
+                            QX_AT(smw, d.feat_row[f]) = __ldg(d.emb_table + (size_t)r * d.n_feat + f);
                     } else {
                         const float *bits = d.emb_bits + (size_t)fid * d.n_pay * d.n_feat;
                         for (int f = lane; f < d.n_feat; f += 32) {
                             float acc = 0.0f;
                             for (int i = 0; i < d.n_pay; i++)
                                 acc = __fadd_rn(acc, __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
-                            smm[d.feat_row[f]] = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), acc);
+                            QX_AT(smw, d.feat_row[f]) = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), acc);
                         }
                     }
                 }
@@ -491,7 +471,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
     if (RUN) {
         for (int i = warp; i < d.n_born0; i += QX_NW) {
             uint2 p = d.pairs[i];
-            if (act) d.x[(size_t)m * d.D + p.y] = sml[p.x];
+            if (act) d.x[(size_t)m * d.D + p.y] = QX_AT(sml, p.x);
         }
         if (warp == 0 && act) {
             d.hash[m] = hash;

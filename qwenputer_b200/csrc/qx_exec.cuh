@@ -10,10 +10,14 @@
 #define QX_MAX_HL 16             // head sublayers a plan may have
 #define QX_HD 128
 
+// the float at a byte offset from a (shared-memory) base
+#define QX_AT(base, off) (*reinterpret_cast<float *>(reinterpret_cast<char *>(base) + (off)))
+#define QX_ATC(base, off) (*reinterpret_cast<const float *>(reinterpret_cast<const char *>(base) + (off)))
+
 struct QxDev {
     // plan sections (device)
     const qx_phase *run_prog, *step_prog;
-    const uint16_t *rows;
+    const uint32_t *rows;
     const uint2 *pairs;
     const uint4 *stream;
     const uint32_t *nnz;
@@ -21,9 +25,9 @@ struct QxDev {
     const qx_stage *stages;
     const qx_vhead *vheads;
     const qx_colform *vform, *zform;
-    const uint16_t *out_row;
+    const uint32_t *out_row;
     const float *out_w;
-    const uint16_t *fam_row, *pay_row, *feat_row;
+    const uint32_t *fam_row, *pay_row, *feat_row;
     const int32_t *fam_ids, *fam_size, *fam_row0;
     const float *emb_base, *emb_bits, *emb_table;
     const uint32_t *tables;     // [99][2]
@@ -56,7 +60,7 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
     uint32_t anchor, n;
 };
 
-// shared memory: the rows (word offsets row * 33; row smem_rows is kept at zero), then the
+// shared memory: the rows (byte offsets row * 132; row smem_rows is kept at zero), then the
 // key-select slots, the decode area ([2][32] ints, [16][32] payload floats), a 64-byte counter
 // block and the per-warp stream rings ([NW][2][32] quads)
 __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {

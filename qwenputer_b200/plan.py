@@ -26,21 +26,20 @@ Form, unit and key-head work is serialised into one stream of 16-byte quads, spl
 contiguous per-warp ranges balanced at compile time (longest first); the kernel streams each
 warp's range through shared memory with asynchronous copies.
 
-Stream records (all fields little-endian uint32; "row" fields are shared-memory word offsets,
-row * 33, so the kernel adds them to its lane's base without a multiply):
-  form      [dst, n entry quads, 0, 0] + entry quads (4 entries: row | bf16 weight << 16;
-            padding entries read the zero row with weight +0)
+Stream records (all fields little-endian uint32; "row" fields are shared-memory byte offsets,
+row * 132, so the kernel adds them to its lane's base; the row after the last one is kept at
+zero and stands for "no form"):
+  form      [dst, n entry quads, 0, 0] + entry quads of two entries [row, w, row, w] (fp32 w)
   FFN node  [out, n groups, n quads, 0] + per group of units sharing their (a, b) forms:
-              constant a: [a | b << 16, n, k, cb] + (n - 1) / 2 quads [k, cb, k, cb], where
-                          k = coef * ca and the unit is k x0 relu(F[b] + cb x0)
-              a form:     [a | b << 16, n | 1 << 16, 0, 0] + n quads [coef, ca, cb, 0], the unit
+              constant a: [a, b, n, 0] + (n + 1) / 2 quads [k, cb, k, cb], k = coef * ca, each
+                          unit k x0 relu(F[b] + cb x0) (a padding unit has k = 0)
+              a form:     [a, b, n | 1 << 31, 0] + n quads [coef, ca, cb, 0], each unit
                           coef (F[a] + ca x0) relu(F[b] + cb x0)
             (a node may be split into several records that add into the same row)
-  key head  [slot | qhot << 16, k common | q common << 16, nk | nq << 16,
-             k lag-ONE row | q lag-ONE row << 16] + a quad of the 128-bit existence mask of the
-            key channels and one of the query channels (when nk / nq > 0), then nk key quads and
-            nq query quads, two channels each [row | bf16 c1 << 16, c0, row | bf16 c1 << 16, c0]:
-            channel = relu(F[row] + (exists ? F[common] : 0) + c0 x0 + c1 x0(t - lag))
+  key head  [slot | qhot << 16, k common, q common, nk | nq << 16], [k lag-ONE row, q lag-ONE
+            row, 0, 0], then nk key-channel quads and nq query-channel quads
+            [row | exists << 31, c0, c1, 0]: channel = relu(F[row] + (exists ? F[common] : 0)
+            + c0 x0 + c1 x0(t - lag))
 """
 
 from __future__ import annotations
@@ -54,9 +53,10 @@ import numpy as np
 from .graphfile import HD, ONE, GraphData
 
 NONE = 0xFFFF
+NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 5
+VERSION = 6
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -75,10 +75,10 @@ SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
 
 DT = {
     "phase": np.dtype([("kind", "<u4"), ("a", "<u4"), ("b", "<u4"), ("c", "<u4")]),
-    "stage": np.dtype([("e", "<u4"), ("x_row", "<u2"), ("ml", "<u2"), ("s0", "<u2"),
-                       ("s1", "<u2"), ("s2", "<u2"), ("pad", "<u2")]),
+    "stage": np.dtype([("e", "<u4"), ("x_row", "<u4"), ("ml", "<u4"), ("s0", "<u4"),
+                       ("s1", "<u4"), ("s2", "<u4")]),
     "vhead": np.dtype([("hl", "<u4"), ("vh", "<u4"), ("col", "<u4"), ("slot", "<u2"),
-                       ("nrows", "<u2"), ("a_row", "<u2"), ("b_row", "<u2"), ("ca", "<f4"),
+                       ("nrows", "<u2"), ("a_row", "<u4"), ("b_row", "<u4"), ("ca", "<f4"),
                        ("cb", "<f4"), ("bconst", "<f4")]),
     "colform": np.dtype([("row", "<u4"), ("pad", "<u2"), ("live", "<u2"), ("c", "<f4")]),
 }
@@ -255,12 +255,11 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     zero_row = smem_rows  # an extra row the kernel keeps at zero (reads of "no form")
 
     def W(r: int) -> int:
-        """Shared-memory word offset of a row (rows are ROW_PAD floats apart)."""
-        return r * ROW_PAD
+        """Shared-memory byte offset of a row (rows are ROW_PAD floats apart)."""
+        return r * ROW_PAD * 4
 
     ZW = W(zero_row)
     one_w = W(slot[ONE])
-    assert W(zero_row) < NONE
 
     # ---- builders -----------------------------------------------------------------------------
     rows_l: list[int] = []
@@ -271,10 +270,10 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     stages_l, vheads_l, vform_l, zform_l, out_row_l, out_w_l = [], [], [], [], [], []
 
     def entry_quads(terms, rowmap) -> list[tuple]:
-        ents = [W(rowmap(t)) | _bf16_bits(w) << 16 for t, w in terms]
-        while len(ents) % 4:
-            ents.append(ZW)  # the zero row times +0
-        return [tuple(ents[i:i + 4]) for i in range(0, len(ents), 4)]
+        ents = [(W(rowmap(t)), _fbits(w)) for t, w in terms]
+        if len(ents) % 2:
+            ents.append((ZW, 0))  # the zero row times +0
+        return [(ents[i][0], ents[i][1], ents[i + 1][0], ents[i + 1][1]) for i in range(0, len(ents), 2)]
 
     def pack_terms(terms, rowmap) -> tuple[int, int]:
         """Packed entries of a lazily evaluated column form (NNZ array, 4-aligned)."""
@@ -314,7 +313,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         for terms, dst in zip(form_list, dst_rows):
             qs = entry_quads(terms, rowmap)
             recs.append([(W(dst), len(qs), 0, 0)] + qs)
-            costs.append(22 * len(qs) + 12)
+            costs.append(9 * len(qs) + 14)
             stats["form_nnz"] += len(terms)
         stream_phase(PH["FORMS"], recs, costs, prog)
 
@@ -399,14 +398,15 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                             if cur_u + len(part) > UNIT_CHUNK:
                                 flush()
                             if ta:
-                                qs = [(ra | rb << 16, len(part) | 1 << 16, 0, 0)]
+                                qs = [(ra, rb, len(part) | 1 << 31, 0)]
                                 qs += [(_fbits(cf), _fbits(ca), _fbits(cb), 0) for cf, ca, cb in part]
                             else:
                                 ks = [(_fbits(np.float32(cf) * np.float32(ca)), _fbits(cb)) for cf, ca, cb in part]
-                                qs = [(ra | rb << 16, len(part), ks[0][0], ks[0][1])]
-                                rest = ks[1:] + ([(0, 0)] if len(ks[1:]) % 2 else [])
-                                qs += [(rest[i][0], rest[i][1], rest[i + 1][0], rest[i + 1][1])
-                                       for i in range(0, len(rest), 2)]
+                                qs = [(ra, rb, len(part), 0)]
+                                if len(ks) % 2:
+                                    ks.append((0, 0))  # k = 0: adds +0
+                                qs += [(ks[i][0], ks[i][1], ks[i + 1][0], ks[i + 1][1])
+                                       for i in range(0, len(ks), 2)]
                             cur_q += qs
                             cur_g += 1
                             cur_u += len(part)
@@ -439,8 +439,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 s0 = len(stages_l)
                 for e, d in enumerate(lag_dims):
                     ml = max(lag for lag, dd in lag_pairs if dd == d)
-                    st = [W(stage_row[(lag, d)]) if (lag, d) in stage_row else NONE for lag in (1, 2, 3)]
-                    stages_l.append((e, W(slot[d]), ml, *st, 0))
+                    st = [W(stage_row[(lag, d)]) if (lag, d) in stage_row else NONE32 for lag in (1, 2, 3)]
+                    stages_l.append((e, W(slot[d]), ml, *st))
                 body.append((PH["STAGE"], s0, len(lag_dims), hi))
             ffree = free[len(lag_pairs):]
             cap = len(ffree)
@@ -521,27 +521,22 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         com, lag, res = hf[h][nm]
                         com_rows[nm] = frow[com] if com else ZW
                         one_rows[nm] = W(stage_row[(lag, ONE)]) if lag else ZW
-                        mask = [0, 0, 0, 0]
                         chans = []
                         for c in range(HD):
                             if c in res:
                                 t, c0, c1 = res[c]
-                                if com:
-                                    mask[c // 32] |= 1 << (c % 32)
-                                chans.append(((frow[t] if t else ZW) | _bf16_bits(c1) << 16, _fbits(c0)))
+                                chans.append(((frow[t] if t else ZW) | (1 << 31 if com else 0),
+                                              _fbits(c0), _fbits(c1), 0))
                             else:
-                                chans.append((ZW, 0))
-                        masks[nm] = tuple(mask)
-                        quads[nm] = [] if not res else [masks[nm]] + [
-                            (chans[2 * i][0], chans[2 * i][1], chans[2 * i + 1][0], chans[2 * i + 1][1])
-                            for i in range(HD // 2)]
+                                chans.append((ZW, 0, 0, 0))
+                        quads[nm] = chans if res else []
                     nk, nq = len(quads["k"]), len(quads["q"])
-                    rec = [(sl | int(g.head_qhot[h]) << 16, com_rows["k"] | com_rows["q"] << 16,
-                            nk | nq << 16, one_rows["k"] | one_rows["q"] << 16)]
+                    rec = [(sl | int(g.head_qhot[h]) << 16, com_rows["k"], com_rows["q"], nk | nq << 16),
+                           (one_rows["k"], one_rows["q"], 0, 0)]
                     rec += quads["k"] + quads["q"]
                     recs.append(rec)
-                    costs.append(26 * (nk + nq) + 40)
-                    stats["kq_channels"] += 2 * (nk + nq)
+                    costs.append(14 * (nk + nq) + 40)
+                    stats["kq_channels"] += nk + nq
                 stream_phase(PH["KSEL"], recs, costs, body)
                 v0 = len(vheads_l)
                 for sl, h in enumerate(gheads):
@@ -554,7 +549,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                                     dstl.append((frow[t] if t else ZW, 0, 1, cc))
                                 else:
                                     dstl.append((ZW, 0, 0, 0.0))
-                        orow = [NONE] * HD
+                        orow = [NONE32] * HD
                         ow = [0.0] * HD
                         for e in range(int(g.vh_out_ptr[j]), int(g.vh_out_ptr[j + 1])):
                             c = int(g.out_col[e])
@@ -599,7 +594,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     s = P.sec
     s["RUN_PROG"] = arr(run_prog, "phase")
     s["STEP_PROG"] = arr(step_prog, "phase")
-    s["ROWS"] = np.asarray(rows_l or [0], np.uint16)
+    s["ROWS"] = np.asarray(rows_l or [0], np.uint32)
     s["PAIRS"] = np.asarray(pairs_l or [(0, 0)], np.uint32).reshape(-1, 2)
     s["STREAM"] = np.asarray(stream or [(0, 0, 0, 0)], np.uint32).reshape(-1, 4)
     s["NNZ"] = np.asarray(nnz_l or [0, 0, 0, 0], np.uint32)
@@ -608,13 +603,13 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     s["VHEADS"] = arr(vheads_l, "vhead")
     s["VFORM"] = arr(vform_l, "colform")
     s["ZFORM"] = arr(zform_l, "colform")
-    s["OUT_ROW"] = np.asarray(out_row_l, np.uint16)
+    s["OUT_ROW"] = np.asarray(out_row_l, np.uint32)
     s["OUT_W"] = np.asarray(out_w_l, np.float32)
     s["HL_V"] = np.asarray([len(g.vheads_at(lv)) for lv in head_levels], np.uint32)
     s["HL_NE"] = np.asarray([max(1, n) for n in hl_ne], np.uint32)
-    s["FAM_ROW"] = np.asarray([W(slot[int(d)]) for d in g.fam_dims], np.uint16)
-    s["PAY_ROW"] = np.asarray([W(slot[int(d)]) for d in g.pay_dims], np.uint16)
-    s["FEAT_ROW"] = np.asarray([W(slot[d]) for d in feat], np.uint16)
+    s["FAM_ROW"] = np.asarray([W(slot[int(d)]) for d in g.fam_dims], np.uint32)
+    s["PAY_ROW"] = np.asarray([W(slot[int(d)]) for d in g.pay_dims], np.uint32)
+    s["FEAT_ROW"] = np.asarray([W(slot[d]) for d in feat], np.uint32)
     s["FAM_IDS"] = np.asarray(g.fam_ids, np.int32)
     s["FAM_SIZE"] = np.asarray(g.fam_size, np.int32)
     s["FAM_ROW0"] = np.asarray([int(r) if sm else -1 for r, sm in zip(g.fam_row0, g.fam_small)],

@@ -6,7 +6,25 @@ import numpy as np
 
 from qwenputer_b200.plan import PH
 
-NONE = 0xFFFF
+NONE = 0xFFFFFFFF
+
+
+class _ByteIndexed:
+    """Rows of the word-indexed array addressed by byte offsets."""
+
+    def __init__(self, a):
+        self.a = a
+
+    def __getitem__(self, k):
+        if isinstance(k, tuple):
+            return self.a[(int(k[0]) // 4,) + k[1:]]
+        return self.a[int(k) // 4]
+
+    def __setitem__(self, k, v):
+        if isinstance(k, tuple):
+            self.a[(int(k[0]) // 4,) + k[1:]] = v
+        else:
+            self.a[int(k) // 4] = v
 
 
 def _f32(x):
@@ -20,8 +38,10 @@ class PlanInterp:
         self.s = s
         h = P.hdr
         self.rows = h["n_slots"] + h["n_scratch"]
-        # indexed by shared-memory word offset (row * 33); the row after the last is zero
-        self.X = np.zeros(((self.rows + 1) * 33, B), np.float32)
+        # indexed by shared-memory word offset (byte offset / 4, rows 33 words apart); the row
+        # after the last is zero
+        self.Xw = np.zeros(((self.rows + 1) * 33, B), np.float32)
+        self.X = _ByteIndexed(self.Xw)
         self.hl_v = s["HL_V"]
         self.S = [np.zeros((B, int(v), 128, 128), np.float32) for v in s["HL_V"]]
         self.H = [np.zeros((3, int(ne), B), np.float32) for ne in s["HL_NE"]]
@@ -48,18 +68,17 @@ class PlanInterp:
             recs = []
             while i < end:
                 h = st[i]
-                n = h[1] if k == PH["FORMS"] else (h[2] if k == PH["UNITS"] else (h[2] & 0xFFFF) + (h[2] >> 16))
+                n = h[1] if k == PH["FORMS"] else (h[2] if k == PH["UNITS"] else 1 + (h[3] & 0xFFFF) + (h[3] >> 16))
                 recs.append((h, st[i + 1:i + 1 + n]))
                 i += 1 + n
             out.append(recs)
         return out
 
     def entries(self, ent):
-        rows = (ent & 0xFFFF).astype(np.int64)
-        w = (ent.astype(np.uint32) & 0xFFFF0000).view(np.float32)
+        q = ent.reshape(-1, 4)
         acc = np.zeros(self.B, np.float32)
-        for r, ww in zip(rows, w):
-            acc = acc + ww * self.X[r]
+        for off, w in list(zip(q[:, 0], q[:, 1])) + list(zip(q[:, 2], q[:, 3])):
+            acc = acc + np.uint32(w).view(np.float32) * self.X[off]
         return acc
 
     def row(self, r, m=slice(None)):
@@ -101,8 +120,7 @@ class PlanInterp:
             elif k == PH["FORMS"]:
                 for recs in self.warp_records(c, k):
                     for h, q in recs:
-                        ent = q.reshape(-1)
-                        self.X[h[0]] = self.entries(ent)
+                        self.X[h[0]] = self.entries(q.reshape(-1))
             elif k == PH["UNITS"]:
                 x0 = self.X[self.one]
                 f32 = lambda v: np.uint32(v).view(np.float32)
@@ -113,18 +131,17 @@ class PlanInterp:
                         for _ in range(int(h[1])):
                             gq = q[i]
                             i += 1
-                            ra, rb = int(gq[0]) & 0xFFFF, int(gq[0]) >> 16
-                            n, has_a = int(gq[1]) & 0xFFFF, int(gq[1]) >> 16
-                            fb = self.X[rb]
+                            n, has_a = int(gq[2]) & 0x7FFFFFFF, int(gq[2]) >> 31
+                            fb = self.X[gq[1]]
                             if not has_a:
-                                ks = [(gq[2], gq[3])]
-                                for _ in range((n - 1 + 1) // 2):
+                                ks = []
+                                for _ in range((n + 1) // 2):
                                     ks += [(q[i][0], q[i][1]), (q[i][2], q[i][3])]
                                     i += 1
                                 for kk, cb in ks[:n]:
                                     acc = acc + (f32(kk) * x0) * np.maximum(fb + f32(cb) * x0, 0)
                             else:
-                                fa = self.X[ra]
+                                fa = self.X[gq[0]]
                                 for _ in range(n):
                                     coef, ca, cb = (f32(v) for v in q[i][:3])
                                     i += 1
@@ -132,28 +149,25 @@ class PlanInterp:
                         self.X[h[0]] = self.X[h[0]] + acc
             elif k == PH["KSEL"]:
                 x0 = self.X[self.one]
+                f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
                     for h, q in recs:
+                        h2 = q[0]
                         slot, qhot = int(h[0]) & 0xFFFF, int(h[0]) >> 16
-                        nk, nq = int(h[2]) & 0xFFFF, int(h[2]) >> 16
+                        nk, nq = int(h[3]) & 0xFFFF, int(h[3]) >> 16
 
                         def chans(quads, com, x1):
                             if not len(quads):
                                 return np.zeros((128, self.B), np.float32)
-                            mask = [int(w) for w in quads[0]]
                             vals = []
-                            for i, qq in enumerate(quads[1:]):
-                                for half, (e, cc) in enumerate(((qq[0], qq[1]), (qq[2], qq[3]))):
-                                    ch = 2 * i + half
-                                    e = int(e)
-                                    c1 = np.uint32(e & 0xFFFF0000).view(np.float32)
-                                    ex = (mask[ch // 32] >> (ch % 32)) & 1
-                                    v = (self.X[e & 0xFFFF] + (com if ex else 0)) + np.uint32(cc).view(np.float32) * x0 + c1 * x1
-                                    vals.append(np.maximum(v, 0))
+                            for qq in quads:
+                                e = int(qq[0])
+                                v = (self.X[e & 0x7FFFFFFF] + (com if e >> 31 else 0)) + f32(qq[1]) * x0 + f32(qq[2]) * x1
+                                vals.append(np.maximum(v, 0))
                             return np.stack(vals)
 
-                        kv = chans(q[:nk], self.X[int(h[1]) & 0xFFFF], self.X[int(h[3]) & 0xFFFF])
-                        qv = chans(q[nk:nk + nq], self.X[int(h[1]) >> 16], self.X[int(h[3]) >> 16])
+                        kv = chans(q[1:1 + nk], self.X[h[1]], self.X[h2[0]])
+                        qv = chans(q[1 + nk:1 + nk + nq], self.X[h[2]], self.X[h2[1]])
                         km, ka = kv.max(0), kv.argmax(0)
                         self.ksel[slot] = np.where(km > 0, ka, -1)
                         sel = []

@@ -63,7 +63,7 @@ def test_plan_is_consistent(graph):
 
     P = compile_plan(graph)
     s = P.sec
-    rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * 33  # word offsets, zero row included
+    rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * 33 * 4  # byte offsets, zero row included
     nw = P.hdr["nw"]
     st = s["STREAM"].astype(np.int64)
     wp = s["WARP_PTR"].astype(np.int64)
@@ -79,29 +79,28 @@ def test_plan_is_consistent(graph):
             while i < end:
                 h = st[i]
                 if k == PH["FORMS"]:
-                    assert h[0] < rows
-                    ent = st[i + 1:i + 1 + h[1]].reshape(-1)
-                    assert np.all((ent & 0xFFFF) < rows)
+                    assert h[0] < rows and h[0] % 132 == 0
+                    ent = st[i + 1:i + 1 + h[1]]
+                    assert np.all(ent[:, 0] < rows) and np.all(ent[:, 2] < rows)
                     i += 1 + h[1]
                 elif k == PH["UNITS"]:
                     assert h[0] < rows
                     j, n_g = i + 1, 0
                     while j < i + 1 + h[2]:
                         gq = st[j]
-                        for r in (gq[0] & 0xFFFF, gq[0] >> 16):
-                            assert r < rows
-                        n, has_a = gq[1] & 0xFFFF, gq[1] >> 16
-                        j += 1 + (n if has_a else n // 2)
+                        assert gq[0] < rows and gq[1] < rows
+                        n, has_a = gq[2] & 0x7FFFFFFF, gq[2] >> 31
+                        j += 1 + (n if has_a else (n + 1) // 2)
                         n_g += 1
                     assert j == i + 1 + h[2] and n_g == h[1]
                     i += 1 + h[2]
                 else:
-                    nk, nq = h[2] & 0xFFFF, h[2] >> 16
-                    assert nk in (0, 65) and nq in (0, 65) and (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"]
-                    c = np.concatenate([st[i + 2:i + 1 + nk], st[i + 2 + nk:i + 1 + nk + nq]])
-                    for r in np.concatenate([c[:, 0] & 0xFFFF, c[:, 2] & 0xFFFF]):
-                        assert r < rows or r == 0xFFFF
-                    i += 1 + nk + nq
+                    nk, nq = h[3] & 0xFFFF, h[3] >> 16
+                    assert nk in (0, 128) and nq in (0, 128) and (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"]
+                    assert h[1] < rows and h[2] < rows and st[i + 1][0] < rows and st[i + 1][1] < rows
+                    c = st[i + 2:i + 2 + nk + nq]
+                    assert np.all((c[:, 0] & 0x7FFFFFFF) < rows)
+                    i += 2 + nk + nq
             assert i == end
     kinds = [int(k) & 0xFF for k in s["RUN_PROG"]["kind"]]
     assert kinds[-2:] == [PH["DECODE"], PH["END"]] and kinds.count(PH["END"]) == 1
