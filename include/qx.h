@@ -52,7 +52,8 @@ enum { /* phase kinds of the per-token program */
     QX_PH_FORMS = 4,    /* form records of the stream; warp w reads quads warp_ptr[c + w ..] */
     QX_PH_UNITS = 5,    /* FFN node records of the stream; warp ranges at warp_ptr[c] */
     QX_PH_KSEL = 6,     /* key-head records of the stream: key argmax, query top-k per machine */
-    QX_PH_VH = 7,       /* value heads [a, b): decay, write, read, output, per machine */
+    QX_PH_VH = 7,       /* value heads [a, b): list every (value head, machine) with row work */
+    QX_PH_VHRUN = 12,   /* value heads [a, b): serve the listed work: decay, write, read, output */
     QX_PH_APPLY = 8,    /* X[dst] += X[src] for pairs [a, a + b) */
     QX_PH_WRITEOUT = 9, /* step mode: x[machine][dim] = X[row] for pairs [a, a + b) */
     QX_PH_DECODE = 10,  /* run mode: output code -> token; next embedding into X */
@@ -150,7 +151,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 6
+#define QX_PLAN_VERSION 7
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

@@ -118,6 +118,25 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     return QX_OK;
 }
 
+// every program ends, and every value-head phase names at most QX_VH_CHUNK heads of the section
+qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
+    for (int id : {QX_S_RUN_PROG, QX_S_STEP_PROG}) {
+        const qx_phase *p = reinterpret_cast<const qx_phase *>(plan + h.off[id]);
+        bool ended = false;
+        for (uint64_t i = 0; i < h.cnt[id] && !ended; i++) {
+            const uint32_t kind = p[i].kind & 0xFFu;
+            if (kind > QX_PH_VHRUN) return fail(QX_ERR_INVALID_PLAN, "unknown phase kind %u", kind);
+            ended = kind == QX_PH_END;
+            if ((kind == QX_PH_VH || kind == QX_PH_VHRUN) &&
+                (p[i].b < p[i].a || p[i].b - p[i].a > QX_VH_CHUNK || p[i].b > h.cnt[QX_S_VHEADS]))
+                return fail(QX_ERR_INVALID_PLAN, "value-head phase [%u, %u) beyond %d heads or the section",
+                            p[i].a, p[i].b, QX_VH_CHUNK);
+        }
+        if (!ended) return fail(QX_ERR_INVALID_PLAN, "program without an END phase");
+    }
+    return QX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -132,6 +151,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     if (plan_bytes < sizeof(h)) return fail(QX_ERR_INVALID_PLAN, "plan too short");
     memcpy(&h, plan, sizeof(h));
     qx_status s = validate(h, plan_bytes);
+    if (s == QX_OK) s = validate_programs(h, static_cast<const uint8_t *>(plan));
     if (s != QX_OK) return s;
     CU(cudaSetDevice(device));
     qx_executor *ex = new (std::nothrow) qx_executor();
@@ -179,6 +199,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.Bpad = ex->Bpad;
     d.D = (int32_t)h.D;
     d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
+    d.zero_row = (uint32_t)d.smem_rows * QX_RP * 4;
     d.one_row = (int32_t)h.one_row;
     d.n_fam = (int32_t)h.n_fam;
     d.n_pay = (int32_t)h.n_pay;

@@ -106,8 +106,11 @@ __global__ void __launch_bounds__(QX_NT, 1)
     uint4 *ring = reinterpret_cast<uint4 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d)) +
                   warp * 2 * QX_RING_QUADS;
     float *sml = sm + lane;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
+    unsigned int *wcount = touched + 1;  // [2] value-head worklist lengths, used in turn
+    int vpar = 0;                        // which of the two the next VH phase appends to
+    uint2 *wl = reinterpret_cast<uint2 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d));  // the rings
     if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
-    if (threadIdx.x == 0) *touched = 0;
+    if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; }
     const int m = blockIdx.x * 32 + lane;  // this lane's machine
     const bool act = m < d.B;
     const int mbase = blockIdx.x * 32;
@@ -183,13 +186,28 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 st.start(d.stream, ring, b0, b1, lane);
                 while (st.more()) {
                     const uint4 h = st.next();
-                    float a0 = 0.0f, a1 = 0.0f;
+                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
                     int nq = (int)h.y;
                     while (nq > 0) {
                         if (st.left == 0) st.advance();
                         const int n = nq < st.left ? nq : st.left;
                         const uint4 *rp = st.rp;
-                        for (int j = 0; j < n; j++) {
+                        int j = 0;
+                        for (; j + 4 <= n; j += 4) {
+                            const uint4 e0 = rp[j], e1 = rp[j + 1], e2 = rp[j + 2], e3 = rp[j + 3];
+                            const float v0 = QX_AT(sml, e0.x), v1 = QX_AT(sml, e0.z), v2 = QX_AT(sml, e1.x),
+                                        v3 = QX_AT(sml, e1.z), v4 = QX_AT(sml, e2.x), v5 = QX_AT(sml, e2.z),
+                                        v6 = QX_AT(sml, e3.x), v7 = QX_AT(sml, e3.z);
+                            a0 = fmaf(__uint_as_float(e0.y), v0, a0);
+                            a1 = fmaf(__uint_as_float(e0.w), v1, a1);
+                            a2 = fmaf(__uint_as_float(e1.y), v2, a2);
+                            a3 = fmaf(__uint_as_float(e1.w), v3, a3);
+                            a0 = fmaf(__uint_as_float(e2.y), v4, a0);
+                            a1 = fmaf(__uint_as_float(e2.w), v5, a1);
+                            a2 = fmaf(__uint_as_float(e3.y), v6, a2);
+                            a3 = fmaf(__uint_as_float(e3.w), v7, a3);
+                        }
+                        for (; j < n; j++) {
                             const uint4 e = rp[j];
                             a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
                             a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
@@ -198,7 +216,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         st.left -= n;
                         nq -= n;
                     }
-                    QX_AT(sml, h.x) = a0 + a1;
+                    QX_AT(sml, h.x) = (a0 + a1) + (a2 + a3);
                 }
                 st.finish();
                 break;
@@ -217,14 +235,32 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         const uint32_t n = gq.z & 0x7FFFFFFFu;
                         const float fb = QX_AT(sml, gq.y);
                         if (!(gq.z >> 31)) {
-                            // constant a: k x0 relu(F[b] + cb x0), two units a quad
-                            for (uint32_t u = 0; u < n; u += 2) {
-                                const uint4 q = st.next();
-                                acc += __fmul_rn(__fmul_rn(__uint_as_float(q.x), x0),
-                                                 relu(fmaf(__uint_as_float(q.y), x0, fb)));
-                                acc += __fmul_rn(__fmul_rn(__uint_as_float(q.z), x0),
-                                                 relu(fmaf(__uint_as_float(q.w), x0, fb)));
+                            // constant a: k x0 relu(F[b] + cb x0), two units a quad, read
+                            // straight from the ring (up to four quads per step)
+                            float acc2 = 0.0f;
+                            int nqd = (int)((n + 1) / 2);
+                            while (nqd > 0) {
+                                if (st.left == 0) st.advance();
+                                const int cnt = nqd < st.left ? nqd : st.left;
+                                const uint4 *rp = st.rp;
+                                int j = 0;
+                                for (; j + 2 <= cnt; j += 2) {
+                                    const uint4 q0 = rp[j], q1 = rp[j + 1];
+                                    acc += __fmul_rn(__fmul_rn(__uint_as_float(q0.x), x0), relu(fmaf(__uint_as_float(q0.y), x0, fb)));
+                                    acc2 += __fmul_rn(__fmul_rn(__uint_as_float(q0.z), x0), relu(fmaf(__uint_as_float(q0.w), x0, fb)));
+                                    acc += __fmul_rn(__fmul_rn(__uint_as_float(q1.x), x0), relu(fmaf(__uint_as_float(q1.y), x0, fb)));
+                                    acc2 += __fmul_rn(__fmul_rn(__uint_as_float(q1.z), x0), relu(fmaf(__uint_as_float(q1.w), x0, fb)));
+                                }
+                                if (j < cnt) {
+                                    const uint4 q0 = rp[j];
+                                    acc += __fmul_rn(__fmul_rn(__uint_as_float(q0.x), x0), relu(fmaf(__uint_as_float(q0.y), x0, fb)));
+                                    acc2 += __fmul_rn(__fmul_rn(__uint_as_float(q0.z), x0), relu(fmaf(__uint_as_float(q0.w), x0, fb)));
+                                }
+                                st.rp += cnt;
+                                st.left -= cnt;
+                                nqd -= cnt;
                             }
+                            acc += acc2;
                         } else {
                             const float fa = QX_AT(sml, gq.x);
                             for (uint32_t u = 0; u < n; u++) {
@@ -257,12 +293,36 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     {
                         const float com = QX_AT(sml, h.y), x1 = QX_AT(sml, h2.x);
                         float bk = 0.0f;
-                        for (uint32_t i = 0; i < nk; i++) {
-                            const uint4 c = st.next();
-                            const float v = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
-                                                 QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
-                            npos += v > 0.0f;
-                            if (v > bk) { bk = v; ik = (int)i; }
+                        uint32_t i = 0;
+                        while (i < nk) {
+                            if (st.left == 0) st.advance();
+                            const int cnt = (int)(nk - i) < st.left ? (int)(nk - i) : st.left;
+                            const uint4 *rp = st.rp;
+                            int j = 0;
+                            for (; j + 4 <= cnt; j += 4) {
+                                float v[4];
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    const uint4 c = rp[j + u];
+                                    v[u] = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
+                                                QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
+                                }
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    npos += v[u] > 0.0f;
+                                    if (v[u] > bk) { bk = v[u]; ik = (int)(i + j + u); }
+                                }
+                            }
+                            for (; j < cnt; j++) {
+                                const uint4 c = rp[j];
+                                const float v = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
+                                                     QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
+                                npos += v > 0.0f;
+                                if (v > bk) { bk = v; ik = (int)(i + j); }
+                            }
+                            st.rp += cnt;
+                            st.left -= cnt;
+                            i += cnt;
                         }
                     }
                     ksel[slot * 32 + lane] = ik;
@@ -271,18 +331,35 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     int qi0 = -1, qi1 = -1, qi2 = -1, qi3 = -1, qpos = 0;
                     {
                         const float com = QX_AT(sml, h.z), x1 = QX_AT(sml, h2.y);
-                        for (uint32_t i = 0; i < nq; i++) {
-                            const uint4 c = st.next();
-                            float v = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
-                                           QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
-                            int vi = (int)i;
-                            qpos += v > 0.0f;
-                            // insertion into the descending top list: a value displaces only a
-                            // strictly smaller one, so ties keep the lower channel first
-                            if (v > qb0) { float tv = qb0; int ti = qi0; qb0 = v; qi0 = vi; v = tv; vi = ti; }
-                            if (qhot > 1 && v > qb1) { float tv = qb1; int ti = qi1; qb1 = v; qi1 = vi; v = tv; vi = ti; }
-                            if (qhot > 2 && v > qb2) { float tv = qb2; int ti = qi2; qb2 = v; qi2 = vi; v = tv; vi = ti; }
-                            if (qhot > 3 && v > qb3) { qb3 = v; qi3 = vi; }
+                        uint32_t i = 0;
+                        while (i < nq) {
+                            if (st.left == 0) st.advance();
+                            const int cnt = (int)(nq - i) < st.left ? (int)(nq - i) : st.left;
+                            const uint4 *rp = st.rp;
+                            for (int j = 0; j < cnt; j += 4) {
+                                float vv[4];
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    const uint4 c = j + u < cnt ? rp[j + u] : make_uint4(d.zero_row, 0u, 0u, 0u);
+                                    vv[u] = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
+                                                 QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
+                                }
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    float v = vv[u];
+                                    int vi = (int)(i + j + u);
+                                    qpos += v > 0.0f;
+                                    // insertion into the descending top list: a value displaces only
+                                    // a strictly smaller one, so ties keep the lower channel first
+                                    if (v > qb0) { float tv = qb0; int ti = qi0; qb0 = v; qi0 = vi; v = tv; vi = ti; }
+                                    if (qhot > 1 && v > qb1) { float tv = qb1; int ti = qi1; qb1 = v; qi1 = vi; v = tv; vi = ti; }
+                                    if (qhot > 2 && v > qb2) { float tv = qb2; int ti = qi2; qb2 = v; qi2 = vi; v = tv; vi = ti; }
+                                    if (qhot > 3 && v > qb3) { qb3 = v; qi3 = vi; }
+                                }
+                            }
+                            st.rp += cnt;
+                            st.left -= cnt;
+                            i += cnt;
                         }
                     }
                     const int qs[4] = {qi0, qi1, qi2, qi3};
@@ -295,120 +372,132 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             case QX_PH_VH: {
-                // per value head and quarter of the CTA's machines: lanes evaluate each
-                // machine's decay / write / read conditions; the machines that touch a row are
-                // then served four at a time with lanes over columns (4 each): first their decays
-                // and writes, then all their row reads in flight together, then the outputs
+                // per value head, lanes walk machines: list every machine whose decay, write or
+                // read touches a state row (record: value head, machine, decay factor, write row,
+                // query rows) in the CTA's worklist, which lives in the idle stream rings
                 const uint32_t n = ph.b - ph.a;
-                for (uint32_t task = warp; task < n * 4; task += QX_NW) {
-                    const qx_vhead vh = d.vheads[ph.a + task / 4];
-                    const int quarter = task & 3;
+                for (uint32_t i = warp; i < n; i += QX_NW) {
+                    const qx_vhead vh = d.vheads[ph.a + i];
                     const float x0 = QX_AT(sml, d.one_row);
-                    float fac = 1.0f;
+                    uint32_t fcode = 0;  // decay factor: 0 -> 1, 1 -> 1/2, 2 -> 0
                     if (vh.nrows > 0) {
                         const float av = fmaf(vh.ca, x0, QX_AT(sml, vh.a_row));
-                        fac = av == 0.0f ? 1.0f : (av == 110.0f ? 0.5f : 0.0f);
+                        fcode = av == 0.0f ? 0u : (av == 110.0f ? 1u : 2u);
                     }
                     const float bv = fmaf(vh.cb, x0, QX_AT(sml, vh.b_row)) + vh.bconst;
                     const int kr = ksel[vh.slot * 32 + lane];
                     const int wrow = (kr >= 0 && bv == 1.0f) ? kr : -1;
-                    int q[4];
+                    uint32_t qpack = 0;
                     bool anyq = false;
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
-                        q[j] = j < d.qhot_max ? qsel[(vh.slot * d.qhot_max + j) * 32 + lane] : -1;
-                        anyq |= q[j] >= 0;
+                        const int qj = j < d.qhot_max ? qsel[(vh.slot * d.qhot_max + j) * 32 + lane] : -1;
+                        qpack |= (uint32_t)(qj + 1) << (8 * j);
+                        anyq |= qj >= 0;
                     }
-                    const bool need = act && (lane >> 3) == quarter && (fac != 1.0f || wrow >= 0 || anyq);
-                    unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
-                    float *const Sh = d.S[vh.hl] + (size_t)vh.vh * (QX_HD * QX_HD) + lane * 4;
-                    const size_t mstride = (size_t)d.V[vh.hl] * (QX_HD * QX_HD);
-                    while (mask) {
-                        int mmv[4], wr[4], qr[4][4];
-                        float f[4];
-                        bool valid[4];
+                    const bool need = act && (fcode != 0 || wrow >= 0 || anyq);
+                    const unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
+                    if (!mask) continue;
+                    unsigned base = 0;
+                    if (lane == 0) base = atomicAdd(wcount + vpar, (unsigned)__popc(mask));
+                    base = __shfl_sync(0xFFFFFFFFu, base, 0);
+                    if (need) {
+                        const unsigned pos = base + __popc(mask & ((1u << lane) - 1u));
+                        wl[pos] = make_uint2(i | (uint32_t)lane << 8 | fcode << 13 | (uint32_t)(wrow + 1) << 16, qpack);
+                    }
+                }
+                break;
+            }
+            case QX_PH_VHRUN: {
+                // the listed row work, four records a warp at a time with lanes over columns
+                // (4 each): decays and writes first, then every record's query rows in flight
+                // together, then the outputs
+                // the other length was last read by the previous serve phase, a barrier ago
+                const uint32_t cnt = wcount[vpar];
+                if (threadIdx.x == 0) wcount[vpar ^ 1] = 0;
+                vpar ^= 1;
+                for (uint32_t r0 = warp * 4; r0 < cnt; r0 += QX_NW * 4) {
+                    qx_vhead vh[4];
+                    int mmv[4], wr[4], qr[4][4];
+                    float f[4];
+                    bool valid[4];
 #pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            valid[b] = mask != 0;
-                            const int mm = valid[b] ? __ffs(mask) - 1 : 0;
-                            if (valid[b]) mask &= mask - 1;
-                            mmv[b] = mm;
-                            f[b] = __shfl_sync(0xFFFFFFFFu, fac, mm);
-                            wr[b] = valid[b] ? __shfl_sync(0xFFFFFFFFu, wrow, mm) : -1;
+                    for (int b = 0; b < 4; b++) {
+                        valid[b] = r0 + b < cnt;
+                        const uint2 rec = valid[b] ? wl[r0 + b] : make_uint2(0u, 0u);
+                        vh[b] = d.vheads[ph.a + (rec.x & 0xFFu)];
+                        mmv[b] = (rec.x >> 8) & 31;
+                        const uint32_t fc = (rec.x >> 13) & 3u;
+                        f[b] = fc == 0 ? 1.0f : (fc == 1 ? 0.5f : 0.0f);
+                        wr[b] = valid[b] ? (int)((rec.x >> 16) & 0xFFu) - 1 : -1;
 #pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                const int v = __shfl_sync(0xFFFFFFFFu, q[j], mm);
-                                qr[b][j] = valid[b] ? v : -1;
+                        for (int j = 0; j < 4; j++) qr[b][j] = valid[b] ? (int)((rec.y >> (8 * j)) & 0xFFu) - 1 : -1;
+                    }
+                    unsigned int rows = 0;  // 512-byte row transfers
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        if (!valid[b]) continue;
+                        float *Sb = d.S[vh[b].hl] + ((size_t)(mbase + mmv[b]) * d.V[vh[b].hl] + vh[b].vh) * (QX_HD * QX_HD) + lane * 4;
+                        if (f[b] != 1.0f) {
+                            rows += 2 * vh[b].nrows;
+                            for (int r = 0; r < vh[b].nrows; r++) {
+                                float4 *p = reinterpret_cast<float4 *>(Sb + r * QX_HD);
+                                float4 sv = *p;
+                                sv.x = __fmul_rn(sv.x, f[b]); sv.y = __fmul_rn(sv.y, f[b]);
+                                sv.z = __fmul_rn(sv.z, f[b]); sv.w = __fmul_rn(sv.w, f[b]);
+                                *p = sv;
                             }
                         }
-                        unsigned int rows = 0;  // 512-byte row transfers
-                        // decays and writes (each machine's own rows: program order suffices)
+                        if (wr[b] >= 0) {
+                            const float *smm = sm + mmv[b];
+                            const float x0m = QX_ATC(smm, d.one_row);
+                            float v[4];
 #pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            if (!valid[b]) continue;
-                            float *Sb = Sh + (size_t)(mbase + mmv[b]) * mstride;
-                            if (f[b] != 1.0f) {
-                                rows += 2 * vh.nrows;
-                                for (int r = 0; r < vh.nrows; r++) {
-                                    float4 *p = reinterpret_cast<float4 *>(Sb + r * QX_HD);
-                                    float4 s = *p;
-                                    s.x = __fmul_rn(s.x, f[b]); s.y = __fmul_rn(s.y, f[b]);
-                                    s.z = __fmul_rn(s.z, f[b]); s.w = __fmul_rn(s.w, f[b]);
-                                    *p = s;
-                                }
+                            for (int i = 0; i < 4; i++) {
+                                const qx_colform cf = d.vform[vh[b].col + lane * 4 + i];
+                                v[i] = cf.live ? relu(fmaf(cf.c, x0m, QX_ATC(smm, cf.row))) : 0.0f;
                             }
-                            if (wr[b] >= 0) {
-                                const float *smm = sm + mmv[b];
-                                const float x0m = QX_ATC(smm, d.one_row);
-                                float v[4];
+                            *reinterpret_cast<float4 *>(Sb + wr[b] * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
+                            rows++;
+                        }
+                    }
+                    float4 o[4];
+                    bool any[4];
 #pragma unroll
-                                for (int i = 0; i < 4; i++) {
-                                    const qx_colform cf = d.vform[vh.col + lane * 4 + i];
-                                    v[i] = cf.live ? relu(fmaf(cf.c, x0m, QX_ATC(smm, cf.row))) : 0.0f;
-                                }
-                                *reinterpret_cast<float4 *>(Sb + wr[b] * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
+                    for (int b = 0; b < 4; b++) {
+                        o[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        any[b] = false;
+                        const float *Sb = d.S[vh[b].hl] + ((size_t)(mbase + mmv[b]) * d.V[vh[b].hl] + vh[b].vh) * (QX_HD * QX_HD) + lane * 4;
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            if (qr[b][j] >= 0) {
+                                const float4 sv = *reinterpret_cast<const float4 *>(Sb + qr[b][j] * QX_HD);
+                                o[b].x = __fadd_rn(o[b].x, sv.x); o[b].y = __fadd_rn(o[b].y, sv.y);
+                                o[b].z = __fadd_rn(o[b].z, sv.z); o[b].w = __fadd_rn(o[b].w, sv.w);
+                                any[b] = true;
                                 rows++;
                             }
                         }
-                        // the reads: every machine's query rows in flight together
-                        float4 o[4];
-                        bool any[4];
+                    }
+                    if (lane == 0) atomicAdd(touched, rows);
 #pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            o[b] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            any[b] = false;
-                            const float *Sb = Sh + (size_t)(mbase + mmv[b]) * mstride;
+                    for (int b = 0; b < 4; b++) {
+                        if (!any[b]) continue;
+                        const float *smm = sm + mmv[b];
+                        const float x0m = QX_ATC(smm, d.one_row);
+                        float ref = __fadd_rn(__fmul_rn(o[b].x, o[b].x), __fmul_rn(o[b].y, o[b].y));
+                        ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
+                        const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
+                        const float oc[4] = {o[b].x, o[b].y, o[b].z, o[b].w};
 #pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                if (qr[b][j] >= 0) {
-                                    const float4 s = *reinterpret_cast<const float4 *>(Sb + qr[b][j] * QX_HD);
-                                    o[b].x = __fadd_rn(o[b].x, s.x); o[b].y = __fadd_rn(o[b].y, s.y);
-                                    o[b].z = __fadd_rn(o[b].z, s.z); o[b].w = __fadd_rn(o[b].w, s.w);
-                                    any[b] = true;
-                                    rows++;
-                                }
-                            }
-                        }
-                        if (lane == 0) atomicAdd(touched, rows);
-#pragma unroll
-                        for (int b = 0; b < 4; b++) {
-                            if (!any[b]) continue;
-                            const float *smm = sm + mmv[b];
-                            const float x0m = QX_ATC(smm, d.one_row);
-                            float ref = __fadd_rn(__fmul_rn(o[b].x, o[b].x), __fmul_rn(o[b].y, o[b].y));
-                            ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
-                            const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
-                            const float oc[4] = {o[b].x, o[b].y, o[b].z, o[b].w};
-#pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const int c = lane * 4 + i;
-                                const uint32_t orow = d.out_row[vh.col + c];
-                                if (orow == QX_NONE32) continue;
-                                const qx_colform zf = d.zform[vh.col + c];
-                                const float z = zf.live ? relu(fmaf(zf.c, x0m, QX_ATC(smm, zf.row))) : 0.0f;
-                                const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
-                                atomicAdd(&QX_AT(sm + mmv[b], orow), __fmul_rn(__fmul_rn(out, z), d.out_w[vh.col + c]));
-                            }
+                        for (int i = 0; i < 4; i++) {
+                            const int c = lane * 4 + i;
+                            const uint32_t orow = d.out_row[vh[b].col + c];
+                            if (orow == QX_NONE32) continue;
+                            const qx_colform zf = d.zform[vh[b].col + c];
+                            const float z = zf.live ? relu(fmaf(zf.c, x0m, QX_ATC(smm, zf.row))) : 0.0f;
+                            const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
+                            atomicAdd(&QX_AT(sm + mmv[b], orow), __fmul_rn(__fmul_rn(out, z), d.out_w[vh[b].col + c]));
                         }
                     }
                 }

@@ -46,6 +46,7 @@ struct QxDev {
     int32_t B, Bpad, D;
     int32_t smem_rows, one_row, n_fam, n_pay, n_feat, n_families, n_emb_rows, n_born0;
     int32_t qhot_max, ksel_slots, n_hl, halt_tok;
+    uint32_t zero_row;  // byte offset of the row kept at zero
 };
 
 // per-machine error bits
@@ -63,6 +64,10 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
 // shared memory: the rows (byte offsets row * 132; row smem_rows is kept at zero), then the
 // key-select slots, the decode area ([2][32] ints, [16][32] payload floats), a 64-byte counter
 // block and the per-warp stream rings ([NW][2][32] quads)
+// value heads one VH phase may list: its 8-byte (value head, machine) records fill the stream
+// rings, 32 machines a value head
+#define QX_VH_CHUNK (QX_NW * 2 * QX_RING_QUADS * 16 / 8 / 32)
+
 __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
     // rows (plus the zero row), key-select slots, decode area, counters
     size_t o = (size_t)(d.smem_rows + 1) * QX_RP * 4 + (size_t)d.ksel_slots * 32 * (1 + d.qhot_max) * 4 +

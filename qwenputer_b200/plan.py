@@ -56,12 +56,15 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 6
+VERSION = 7
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
-          DECODE=10, END=11)
+          DECODE=10, END=11, VHRUN=12)
 NOSYNC = 0x100  # phase kind flag: no barrier after the phase
+# value heads a VH phase lists: its worklist of (value head, machine) records, 8 bytes each,
+# lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps)
+VH_CHUNK = 64
 UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most this many
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "NNZ", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
@@ -563,7 +566,10 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         vheads_l.append((hi, vhs_level.index(j), col, sl, int(g.vh_nrows[j]),
                                          frow[ta] if ta else ZW, frow[tb] if tb else ZW,
                                          ca, cb, 0.0 if g.vh_has_beta[j] else 1.0))
-                body.append((PH["VH"], v0, len(vheads_l), 0))
+                for c0 in range(v0, len(vheads_l), VH_CHUNK):
+                    c1 = min(c0 + VH_CHUNK, len(vheads_l))
+                    body.append((PH["VH"], c0, c1, 0))  # list the machines' row work
+                    body.append((PH["VHRUN"], c0, c1, 0))  # serve it
             group_stats.append((lv, "head", len(groups)))
         apply_pairs = [(W(slot[d]), W(slot[k])) for (l2, d), k in temps.items() if l2 == lv]
         tail = []

@@ -176,6 +176,8 @@ class PlanInterp:
                             sel.append(np.where(qm > 0, qa, -1))
                             qv[qa, np.arange(self.B)] = 0
                         self.qsel[slot] = sel
+            elif k == PH["VHRUN"]:
+                pass  # the row work a VH phase lists is done here while it is listed
             elif k == PH["VH"]:
                 x0 = self.X[self.one]
                 for vh in s["VHEADS"][a:b]:
