@@ -241,6 +241,26 @@ QX_API size_t qx_gdn_work_bytes(int64_t BH);
 QX_API qx_status qx_gdn_step(int64_t BH, float *S, const float *q, const float *k, const float *v,
                       const float *alpha, const float *beta, float *o, void *work, void *stream);
 
+/* qx_gdn_step for callers that must not allocate device memory: hosts whose own allocator has
+ * been handed the whole device heap, and latency-bound loops in which a cudaMalloc, which can
+ * synchronise the device, is not allowed.  No counterpart in the reference.
+ *
+ * Same step, same arguments and results as qx_gdn_step, without `work`: the scratch is a
+ * fixed array inside this library (QX_GDN_NOALLOC_MAX_BH heads, 256 KB + 8 B per device, kept
+ * until the process exits), so the call allocates nothing.  BH above QX_GDN_NOALLOC_MAX_BH is
+ * rejected with QX_ERR_INVALID_ARG (use qx_gdn_step with a caller buffer).  The first call on a
+ * device sets that device up (looks up the array's address, which can load this library's
+ * kernels onto the device, and sets the step kernel's shared-memory limit): make that first
+ * call before any stream capture.  Every call on a device shares the one array and clears its
+ * count and error word on the stream first, so calls whose kernels can overlap on the GPU
+ * (different streams without ordering between them) race; calls on one stream, or otherwise
+ * ordered, do not.  err (dev, optional): receives the step's error word (0, or
+ * QX_ERR_DEVICE_FLAG when a bounded wait of the full-matrix path gave up). */
+#define QX_GDN_NOALLOC_MAX_BH 65536
+QX_API qx_status qx_gdn_step_noalloc(int64_t BH, float *S, const float *q, const float *k, const float *v,
+                                     const float *alpha, const float *beta, float *o, uint32_t *err,
+                                     void *stream);
+
 #ifdef __cplusplus
 }
 #endif

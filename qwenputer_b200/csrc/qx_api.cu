@@ -22,6 +22,7 @@ __global__ void qx_reset_kernel(float *H, uint32_t ne, uint32_t bpad, int32_t ro
 size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
                      const float *beta, float *o, uint32_t *work, cudaStream_t st);
 cudaError_t qx_gdn_prepare();
+cudaError_t qx_gdn_noalloc_scratch(uint32_t **out);
 
 namespace {
 
@@ -479,6 +480,25 @@ qx_status qx_gdn_step(int64_t BH, float *S, const float *q, const float *k, cons
         prepared = 1;
     }
     qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, static_cast<uint32_t *>(work), static_cast<cudaStream_t>(stream));
+    CU(cudaGetLastError());
+    return QX_OK;
+}
+
+qx_status qx_gdn_step_noalloc(int64_t BH, float *S, const float *q, const float *k, const float *v,
+                              const float *alpha, const float *beta, float *o, uint32_t *err, void *stream) {
+    if (BH < 0 || BH > QX_GDN_NOALLOC_MAX_BH)
+        return fail(QX_ERR_INVALID_ARG,
+                    "qx_gdn_step_noalloc: %lld heads; its built-in scratch holds at most %d "
+                    "(qx_gdn_step takes a caller buffer for more)",
+                    (long long)BH, QX_GDN_NOALLOC_MAX_BH);
+    if (BH == 0) return QX_OK;
+    if (!S || !q || !k || !v || !alpha || !beta || !o)
+        return fail(QX_ERR_INVALID_ARG, "qx_gdn_step_noalloc: null argument");
+    uint32_t *work = nullptr;
+    CU(qx_gdn_noalloc_scratch(&work));  // the first call on a device sets it up
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, work, st);  // clears the count and error word first
+    if (err) CU(cudaMemcpyAsync(err, work + 1, 4, cudaMemcpyDeviceToDevice, st));
     CU(cudaGetLastError());
     return QX_OK;
 }

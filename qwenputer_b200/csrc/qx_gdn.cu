@@ -17,10 +17,11 @@
 //
 // The row path runs first and queues the matrix-path heads in `work` (a count, an error word,
 // then head indices); the matrix kernel drains that queue.  Waits on the TMA barrier are bounded:
-// on timeout the CTA records QX_E_BUSY in the error word and returns.
+// on timeout the CTA records QX_ERR_DEVICE_FLAG in the error word and returns.
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "qx.h"
 
@@ -185,4 +186,36 @@ size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const
 
 cudaError_t qx_gdn_prepare() {
     return cudaFuncSetAttribute(qx_gdn_matrix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_MAT * 4);
+}
+
+// ---- scratch for the allocation-free entry point (qx_gdn_step_noalloc) ------------------------
+// The queue of the step (count, error word, head indices) for up to QX_GDN_NOALLOC_MAX_BH heads,
+// as a fixed array of this library's device image: 256 KB + 8 B on every device that loads the
+// library, held until the process exits.  Every call on a device shares it; the launch clears the
+// count and the error word, and the row kernel writes each index before the matrix kernel reads it.
+static __device__ __align__(256) uint32_t g_gdn_scratch[2 + QX_GDN_NOALLOC_MAX_BH];
+
+#define QX_GDN_MAX_DEVICES 64
+
+// The array's address on the current device.  The first request on a device, with that device
+// current, looks the address up (which can load this library's kernels onto the device) and sets
+// the matrix kernel's shared-memory limit there; later requests only read the cached address.
+cudaError_t qx_gdn_noalloc_scratch(uint32_t **out) {
+    static std::mutex mu;
+    static uint32_t *addr[QX_GDN_MAX_DEVICES] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= QX_GDN_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_gdn_scratch);
+        if (e != cudaSuccess) return e;
+        e = qx_gdn_prepare();
+        if (e != cudaSuccess) return e;
+        addr[dev] = static_cast<uint32_t *>(p);
+    }
+    *out = addr[dev];
+    return cudaSuccess;
 }

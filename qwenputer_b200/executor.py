@@ -50,7 +50,7 @@ def lib():
         L.qx_last_error.restype = C.c_char_p
         for name in ("qx_create", "qx_destroy", "qx_buffer", "qx_reset", "qx_load_machines",
                      "qx_step", "qx_run", "qx_set_tokens", "qx_readback", "qx_checksums",
-                     "qx_errors", "qx_gdn_step"):
+                     "qx_errors", "qx_gdn_step", "qx_gdn_step_noalloc"):
             getattr(L, name).restype = C.c_int
         L.qx_gdn_work_bytes.restype = C.c_size_t
         L.qx_gdn_work_bytes.argtypes = [C.c_int64]

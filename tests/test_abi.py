@@ -20,7 +20,7 @@ def test_library_exports_every_declared_symbol():
 
     lib = C.CDLL(str(build.build()))
     names = declared_symbols()
-    assert len(names) == 14, names
+    assert len(names) == 15, names
     for n in names:
         assert hasattr(lib, n), n
 
