@@ -51,6 +51,8 @@ def parse():
                     help="split --machines across the ranks instead of running them per GPU")
     ap.add_argument("--tokens-per-step", type=int, default=200)
     ap.add_argument("--no-gdn", action="store_true")
+    ap.add_argument("--gdn-sequences", type=int, default=1024,
+                    help="sequences of the gated delta-rule microbenchmark (48 heads each)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--seed", type=int, default=1000)
@@ -136,11 +138,11 @@ def cpu_baseline(programs, seconds: float = 12.0) -> dict:
             "sample": f"{B} machines x {n} free-running tokens of the same workload ({dt:.1f} s)"}
 
 
-def gdn_bench(torch, steps: int, warmup: int, peak_gbs: float) -> dict:
-    """One gated delta-rule decode step over 1,024 x 48 heads; bytes from the realised draws."""
+def gdn_bench(torch, steps: int, warmup: int, peak_gbs: float, B: int = 1024) -> dict:
+    """One gated delta-rule decode step over B x 48 heads; bytes from the realised draws."""
     from qwenputer_b200.executor import gdn_step
 
-    B, H, D = 1024, 48, 128
+    H, D = 48, 128
     BH = B * H
     g = torch.Generator(device="cpu").manual_seed(7)
     S = torch.randint(0, 2, (BH, D, D), generator=g, dtype=torch.uint8).to("cuda").float()
@@ -355,7 +357,7 @@ def main() -> None:
 
     gdn = None
     if not args.no_gdn and rank == 0:
-        gdn = gdn_bench(torch, max(args.steps, 5), args.warmup, peak)
+        gdn = gdn_bench(torch, max(args.steps, 5), args.warmup, peak, args.gdn_sequences)
     cpu = None
     if not args.no_cpu and rank == 0 and world == 1:
         cpu = cpu_baseline(progs)

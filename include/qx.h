@@ -52,8 +52,10 @@ enum { /* phase kinds of the per-token program */
     QX_PH_FORMS = 4,    /* form records of the stream; warp w reads quads warp_ptr[c + w ..] */
     QX_PH_UNITS = 5,    /* FFN node records of the stream; warp ranges at warp_ptr[c] */
     QX_PH_KSEL = 6,     /* key-head records of the stream: key argmax, query top-k per machine */
-    QX_PH_VH = 7,       /* value heads [a, b): list every (value head, machine) with row work */
+    QX_PH_VH = 7,       /* value heads [a, b): list every (value head, machine) with row work;
+                           c: output delta rows of the phase (cluster plans, else 0) */
     QX_PH_VHRUN = 12,   /* value heads [a, b): serve the listed work: decay, write, read, output */
+    QX_PH_VHSUM = 13,   /* cluster plans: rows VHSUM_ROWS[a, a + b) += every CTA's delta row */
     QX_PH_APPLY = 8,    /* X[dst] += X[src] for pairs [a, a + b) */
     QX_PH_WRITEOUT = 9, /* step mode: x[machine][dim] = X[row] for pairs [a, a + b) */
     QX_PH_DECODE = 10,  /* run mode: output code -> token; next embedding into X */
@@ -116,6 +118,9 @@ typedef struct {
     uint32_t vocab;
     uint32_t n_born0;              /* PAIRS[0 : n_born0] = (row, dim) of the dims set by an
                                       embedding (ONE and the token features) */
+    uint32_t cluster;              /* CTAs (a thread-block cluster) that share one group of 32
+                                      machines; stream ranges exist for nw * cluster warps */
+    uint32_t reserved;
     /* sections: byte offset from the blob start, element count */
     uint64_t off[32];
     uint64_t cnt[32];
@@ -127,7 +132,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_ROWS,           /* uint32: row lists (byte offsets) */
     QX_S_PAIRS,          /* uint32 pairs (row, dim) / (dst, src) */
     QX_S_STREAM,         /* uint4 quads: form, FFN node and key-head records */
-    QX_S_NNZ,            /* uint32: unused (kept for the section numbering) */
+    QX_S_VHSUM_ROWS,     /* uint32: rows (byte offsets) that VHSUM phases add output deltas into */
     QX_S_WARP_PTR,       /* uint32: per phase, nw + 1 quad offsets into STREAM */
     QX_S_STAGES,         /* qx_stage */
     QX_S_VHEADS,         /* qx_vhead */
@@ -151,7 +156,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 7
+#define QX_PLAN_VERSION 9
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */
@@ -226,6 +231,19 @@ QX_API qx_status qx_checksums(qx_t *ex, uint64_t *out /*dev*/, void *stream);
 
 /* OR of every machine's error word (dev -> host copy; synchronises the stream). */
 QX_API qx_status qx_errors(qx_t *ex, uint32_t *any /*host*/, void *stream);
+
+/* Facts of the executor's launch shape: QX_INFO_CLUSTER, the CTAs (a thread-block cluster) that
+ * share one group of 32 machines; QX_INFO_MAX_CLUSTERS, how many such clusters the device holds at
+ * once; QX_INFO_CTAS, the CTAs of one token-kernel launch; QX_INFO_SMEM, shared memory per CTA.
+ * No counterpart in the reference (its Executor2 has no launch-shape queries). */
+enum { QX_INFO_CLUSTER = 0, QX_INFO_MAX_CLUSTERS = 1, QX_INFO_CTAS = 2, QX_INFO_SMEM = 3 };
+QX_API qx_status qx_info(qx_t *ex, int32_t what, int64_t *out /*host*/);
+
+/* How many clusters of `cluster` CTAs (1..8) of the token kernel, with the plan's shared memory
+ * per CTA, the device holds at once (cudaOccupancyMaxActiveClusters); lets a caller choose the
+ * cluster size for a batch before compiling the plan for it.  No counterpart in the reference. */
+QX_API qx_status qx_cluster_capacity(const void *plan, size_t plan_bytes, int32_t device, int32_t cluster,
+                                     int32_t *max_clusters /*host*/);
 
 /* The text of the last error on this thread ("" if none). */
 QX_API const char *qx_last_error(void);

@@ -52,6 +52,7 @@ struct qx_executor {
     QxDev d{};
     int n_hl = 0;
     size_t smem = 0;
+    int max_clusters = 0;         // clusters of the token kernel that fit on the device at once
     int32_t *dtok = nullptr;      // [B] scratch for qx_set_tokens
     qx_state *dstate = nullptr;   // readback staging
     int32_t state_cap = 0;
@@ -66,6 +67,31 @@ struct qx_executor {
 };
 
 namespace {
+
+// One launch of the token kernel: a CTA per group of 32 machines, or a cluster of d.cluster CTAs
+// per group (launched with the cluster-dimension attribute).
+template <int RUN>
+cudaError_t launch_token(const qx_t *ex, const QxDev &d, int32_t n_tokens, int32_t *tokens, cudaStream_t st) {
+    const int C = d.cluster;
+    const unsigned grid = (unsigned)(ex->Bpad / 32 * C);
+    if (C == 1) {
+        qx_token_kernel<RUN><<<grid, QX_NT, ex->smem, st>>>(d, n_tokens, tokens);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(QX_NT);
+    cfg.dynamicSmemBytes = ex->smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)C;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qx_token_kernel<RUN>, d, n_tokens, tokens);
+}
 
 qx_status dev_alloc(qx_t *ex, void **p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes);
@@ -95,12 +121,13 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
         return fail(QX_ERR_INVALID_PLAN, "plan version %u, expected %d", h.version, QX_PLAN_VERSION);
     if (h.qhot_max > 4) return fail(QX_ERR_INVALID_PLAN, "queries read at most 4 rows");
     if (h.nw != QX_NW) return fail(QX_ERR_INVALID_PLAN, "plan balanced for %u warps, kernel has %d", h.nw, QX_NW);
+    if (h.cluster < 1 || h.cluster > 8) return fail(QX_ERR_INVALID_PLAN, "cluster of %u CTAs (1 to 8)", h.cluster);
     if (h.n_head_levels > QX_MAX_HL) return fail(QX_ERR_INVALID_PLAN, "too many head sublayers");
     if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
     if (h.n_born0 != h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
     const SecSpec specs[] = {
         {QX_S_RUN_PROG, sizeof(qx_phase)}, {QX_S_STEP_PROG, sizeof(qx_phase)}, {QX_S_ROWS, 4},
-        {QX_S_PAIRS, 8}, {QX_S_STREAM, 16}, {QX_S_NNZ, 4}, {QX_S_WARP_PTR, 4},
+        {QX_S_PAIRS, 8}, {QX_S_STREAM, 16}, {QX_S_VHSUM_ROWS, 4}, {QX_S_WARP_PTR, 4},
         {QX_S_STAGES, sizeof(qx_stage)}, {QX_S_VHEADS, sizeof(qx_vhead)},
         {QX_S_VFORM, sizeof(qx_colform)}, {QX_S_ZFORM, sizeof(qx_colform)}, {QX_S_OUT_ROW, 4}, {QX_S_OUT_W, 4},
         {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 4}, {QX_S_PAY_ROW, 4}, {QX_S_FEAT_ROW, 4},
@@ -115,7 +142,6 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     if (h.cnt[QX_S_HL_V] != h.n_head_levels || h.cnt[QX_S_FEAT_ROW] != h.n_feat ||
         h.cnt[QX_S_FAM_ROW] != h.n_fam || h.cnt[QX_S_PAY_ROW] != h.n_pay)
         return fail(QX_ERR_INVALID_PLAN, "section counts disagree with the header");
-    if (h.cnt[QX_S_NNZ] % 4) return fail(QX_ERR_INVALID_PLAN, "packed entries not padded to 4");
     return QX_OK;
 }
 
@@ -126,12 +152,20 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
         bool ended = false;
         for (uint64_t i = 0; i < h.cnt[id] && !ended; i++) {
             const uint32_t kind = p[i].kind & 0xFFu;
-            if (kind > QX_PH_VHRUN) return fail(QX_ERR_INVALID_PLAN, "unknown phase kind %u", kind);
+            if (kind > QX_PH_VHSUM) return fail(QX_ERR_INVALID_PLAN, "unknown phase kind %u", kind);
             ended = kind == QX_PH_END;
+            if ((kind == QX_PH_FORMS || kind == QX_PH_UNITS || kind == QX_PH_KSEL) &&
+                (uint64_t)p[i].c + (uint64_t)h.nw * h.cluster >= h.cnt[QX_S_WARP_PTR])
+                return fail(QX_ERR_INVALID_PLAN, "stream phase %llu: warp ranges beyond the section",
+                            (unsigned long long)i);
             if ((kind == QX_PH_VH || kind == QX_PH_VHRUN) &&
-                (p[i].b < p[i].a || p[i].b - p[i].a > QX_VH_CHUNK || p[i].b > h.cnt[QX_S_VHEADS]))
-                return fail(QX_ERR_INVALID_PLAN, "value-head phase [%u, %u) beyond %d heads or the section",
-                            p[i].a, p[i].b, QX_VH_CHUNK);
+                (p[i].b < p[i].a || p[i].b - p[i].a > QX_VH_CHUNK || p[i].b > h.cnt[QX_S_VHEADS] ||
+                 (p[i].c > 0 && h.cluster == 1) ||
+                 qx_vh_worklist_offset(p[i].c) + (size_t)(p[i].b - p[i].a) * 32 * 8 > QX_RING_BYTES))
+                return fail(QX_ERR_INVALID_PLAN, "value-head phase [%u, %u) with %u delta rows exceeds the rings",
+                            p[i].a, p[i].b, p[i].c);
+            if (kind == QX_PH_VHSUM && (h.cluster == 1 || (uint64_t)p[i].a + p[i].b > h.cnt[QX_S_VHSUM_ROWS]))
+                return fail(QX_ERR_INVALID_PLAN, "delta-sum phase beyond its rows");
         }
         if (!ended) return fail(QX_ERR_INVALID_PLAN, "program without an END phase");
     }
@@ -177,7 +211,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.rows = sec<uint32_t>(ex, QX_S_ROWS);
     d.pairs = sec<uint2>(ex, QX_S_PAIRS);
     d.stream = sec<uint4>(ex, QX_S_STREAM);
-    d.nnz = sec<uint32_t>(ex, QX_S_NNZ);
+    d.vhsum_rows = sec<uint32_t>(ex, QX_S_VHSUM_ROWS);
     d.warp_ptr = sec<uint32_t>(ex, QX_S_WARP_PTR);
     d.stages = sec<qx_stage>(ex, QX_S_STAGES);
     d.vheads = sec<qx_vhead>(ex, QX_S_VHEADS);
@@ -201,6 +235,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.D = (int32_t)h.D;
     d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
     d.zero_row = (uint32_t)d.smem_rows * QX_RP * 4;
+    d.cluster = (int32_t)h.cluster;
     d.one_row = (int32_t)h.one_row;
     d.n_fam = (int32_t)h.n_fam;
     d.n_pay = (int32_t)h.n_pay;
@@ -271,6 +306,24 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
         cudaFuncSetAttribute(qx_token_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
             cudaSuccess || qx_gdn_prepare() != cudaSuccess)
         return bail(fail(QX_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError())));
+    {
+        // how many clusters (or CTAs) of the token kernel the device holds at once
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(ex->Bpad / 32 * d.cluster));
+        cfg.blockDim = dim3(QX_NT);
+        cfg.dynamicSmemBytes = ex->smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)d.cluster;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        cudaError_t e2 = cudaOccupancyMaxActiveClusters(&ex->max_clusters, qx_token_kernel<1>, &cfg);
+        if (e2 != cudaSuccess || ex->max_clusters < 1)
+            return bail(fail(QX_ERR_CUDA, "a cluster of %d CTAs with %zu B of shared memory each does not fit: %s",
+                             d.cluster, ex->smem, cudaGetErrorString(e2)));
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(QX_ERR_CUDA, "init sync"));
     *out = ex;
     return QX_OK;
@@ -390,17 +443,14 @@ qx_status qx_step(qx_t *ex, float *x, void *stream) {
     if (!ex || !x) return fail(QX_ERR_INVALID_ARG, "qx_step: null argument");
     QxDev d = ex->d;
     d.x = x;
-    qx_token_kernel<0><<<ex->Bpad / 32, QX_NT, ex->smem, static_cast<cudaStream_t>(stream)>>>(d, 1, nullptr);
-    CU(cudaGetLastError());
+    CU(launch_token<0>(ex, d, 1, nullptr, static_cast<cudaStream_t>(stream)));
     return QX_OK;
 }
 
 qx_status qx_run(qx_t *ex, int32_t n_tokens, int32_t *tokens, void *stream) {
     if (!ex || n_tokens < 0) return fail(QX_ERR_INVALID_ARG, "qx_run: bad arguments");
     if (n_tokens == 0) return QX_OK;
-    qx_token_kernel<1><<<ex->Bpad / 32, QX_NT, ex->smem, static_cast<cudaStream_t>(stream)>>>(ex->d, n_tokens,
-                                                                                            tokens);
-    CU(cudaGetLastError());
+    CU(launch_token<1>(ex, ex->d, n_tokens, tokens, static_cast<cudaStream_t>(stream)));
     return QX_OK;
 }
 
@@ -464,6 +514,50 @@ qx_status qx_errors(qx_t *ex, uint32_t *any, void *stream) {
     for (int i = 0; i < ex->B; i++) acc |= ex->err_host[i];
     *any = acc;
     return QX_OK;
+}
+
+qx_status qx_cluster_capacity(const void *plan, size_t plan_bytes, int32_t device, int32_t cluster,
+                              int32_t *max_clusters) {
+    if (!plan || !max_clusters || cluster < 1 || cluster > 8)
+        return fail(QX_ERR_INVALID_ARG, "qx_cluster_capacity: bad arguments");
+    qx_plan_header h;
+    if (plan_bytes < sizeof(h)) return fail(QX_ERR_INVALID_PLAN, "plan too short");
+    memcpy(&h, plan, sizeof(h));
+    qx_status st = validate(h, plan_bytes);
+    if (st != QX_OK) return st;
+    QxDev d{};
+    d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
+    d.qhot_max = (int32_t)h.qhot_max;
+    d.ksel_slots = (int32_t)h.n_ksel_slots;
+    const size_t smem = qx_smem_bytes(d);
+    CU(cudaSetDevice(device));
+    CU(cudaFuncSetAttribute(qx_token_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cluster);
+    cfg.blockDim = dim3(QX_NT);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)cluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    CU(cudaOccupancyMaxActiveClusters(&n, qx_token_kernel<1>, &cfg));
+    *max_clusters = n;
+    return QX_OK;
+}
+
+qx_status qx_info(qx_t *ex, int32_t what, int64_t *out) {
+    if (!ex || !out) return fail(QX_ERR_INVALID_ARG, "qx_info: null argument");
+    switch (what) {
+    case QX_INFO_CLUSTER: *out = ex->d.cluster; return QX_OK;
+    case QX_INFO_MAX_CLUSTERS: *out = ex->max_clusters; return QX_OK;
+    case QX_INFO_CTAS: *out = (int64_t)ex->Bpad / 32 * ex->d.cluster; return QX_OK;
+    case QX_INFO_SMEM: *out = (int64_t)ex->smem; return QX_OK;
+    default: return fail(QX_ERR_INVALID_ARG, "qx_info: unknown item %d", what);
+    }
 }
 
 size_t qx_gdn_work_bytes(int64_t BH) { return 8 + 4 * (size_t)(BH > 0 ? BH : 0); }

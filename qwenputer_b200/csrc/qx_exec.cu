@@ -35,6 +35,56 @@ __device__ __forceinline__ uint64_t fnv_word(uint64_t h, uint32_t w) {
     return h;
 }
 
+// ---- the machine group's cluster: every CTA keeps a full copy of the group's rows ----------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the address of a shared-memory location in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void *p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(a)
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+    return a;
+}
+// a row value every copy must see: stored in each CTA of the cluster
+__device__ __forceinline__ void put_all(float *p, float v, int C) {
+    if (C == 1) {
+        *p = v;
+        return;
+    }
+    for (int r = 0; r < C; r++)
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(peer_addr(p, r)), "f"(v) : "memory");
+}
+__device__ __forceinline__ void put_all(int *p, int v, int C) {
+    if (C == 1) {
+        *p = v;
+        return;
+    }
+    for (int r = 0; r < C; r++)
+        asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(peer_addr(p, r)), "r"(v) : "memory");
+}
+// a contribution to a row that several records sum into, added in each CTA of the cluster
+__device__ __forceinline__ void add_all(float *p, float v, int C) {
+    if (C == 1) {
+        atomicAdd(p, v);
+        return;
+    }
+    for (int r = 0; r < C; r++)
+        asm volatile("red.relaxed.cluster.shared::cluster.add.f32 [%0], %1;" ::"r"(peer_addr(p, r)), "f"(v) : "memory");
+}
+// the end of a phase: every warp of the CTA, or of the whole cluster (whose writes into this
+// CTA's rows are then visible here)
+__device__ __forceinline__ void phase_sync(int C) {
+    if (C == 1) {
+        __syncthreads();
+    } else {
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    }
+}
+
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
@@ -103,17 +153,25 @@ __global__ void __launch_bounds__(QX_NT, 1)
     float *dec_pay = reinterpret_cast<float *>(dec_i + 64);                  // [16][32]
     unsigned int *touched = reinterpret_cast<unsigned int *>(dec_pay + 16 * 32);  // state rows
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // a group of 32 machines runs on C CTAs; stream ranges are per warp of the group (gw of nwv)
+    const int C = d.cluster;
+    const int crank = C > 1 ? (int)cluster_rank() : 0;
+    const int gw = crank * QX_NW + warp, nwv = C * QX_NW;
     uint4 *ring = reinterpret_cast<uint4 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d)) +
                   warp * 2 * QX_RING_QUADS;
     float *sml = sm + lane;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
     unsigned int *wcount = touched + 1;  // [2] value-head worklist lengths, used in turn
     int vpar = 0;                        // which of the two the next VH phase appends to
-    uint2 *wl = reinterpret_cast<uint2 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d));  // the rings
+    // value-head phases reuse the stream rings: the CTA's output delta rows (cluster plans) and
+    // then the worklist
+    char *rings = reinterpret_cast<char *>(sm) + qx_ring_offset(d);
+    float *delta = reinterpret_cast<float *>(rings);
     if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
     if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; }
-    const int m = blockIdx.x * 32 + lane;  // this lane's machine
+    const int grp = blockIdx.x / C;
+    const int m = grp * 32 + lane;  // this lane's machine
     const bool act = m < d.B;
-    const int mbase = blockIdx.x * 32;
+    const int mbase = grp * 32;
 
     // run mode: the embedding of each machine's next input comes from x
     uint64_t hash = 0;
@@ -129,7 +187,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
             halt_at = d.halt_at[m];
         }
     }
-    __syncthreads();
+    phase_sync(C);  // (with C > 1, also: every CTA of the cluster runs before rows are shared)
     const qx_phase *prog = RUN ? d.run_prog : d.step_prog;
     for (int32_t t = 0; t < n_tokens; t++) {
         for (int pc = 0;; pc++) {
@@ -148,7 +206,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             case QX_PH_WRITEOUT:
                 if (act)
-                    for (uint32_t i = warp; i < ph.b; i += QX_NW) {
+                    for (uint32_t i = gw; i < ph.b; i += nwv) {
                         uint2 p = d.pairs[ph.a + i];
                         d.x[(size_t)m * d.D + p.y] = QX_AT(sml, p.x);
                     }
@@ -164,15 +222,15 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // the history on: lag 1 <- the input x, lag k <- lag k-1
                 float *H = d.hist[ph.c];
                 const size_t ne = d.NE[ph.c], bp = d.Bpad;
-                for (uint32_t i = warp; i < ph.b; i += QX_NW) {
+                for (uint32_t i = gw; i < ph.b; i += nwv) {
                     const qx_stage s = d.stages[ph.a + i];
                     float *h = H + (size_t)s.e * bp + m;
                     float h0 = h[0];
                     float h1 = s.ml >= 2 ? h[ne * bp] : 0.0f;
                     float h2 = s.ml >= 3 ? h[2 * ne * bp] : 0.0f;
-                    if (s.stage[0] != QX_NONE32) QX_AT(sml, s.stage[0]) = h0;
-                    if (s.stage[1] != QX_NONE32) QX_AT(sml, s.stage[1]) = h1;
-                    if (s.stage[2] != QX_NONE32) QX_AT(sml, s.stage[2]) = h2;
+                    if (s.stage[0] != QX_NONE32) put_all(&QX_AT(sml, s.stage[0]), h0, C);
+                    if (s.stage[1] != QX_NONE32) put_all(&QX_AT(sml, s.stage[1]), h1, C);
+                    if (s.stage[2] != QX_NONE32) put_all(&QX_AT(sml, s.stage[2]), h2, C);
                     h[0] = QX_AT(sml, s.x_row);
                     if (s.ml >= 2) h[ne * bp] = h0;
                     if (s.ml >= 3) h[2 * ne * bp] = h1;
@@ -180,7 +238,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             case QX_PH_FORMS: {
-                const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
+                const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
@@ -216,13 +274,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         st.left -= n;
                         nq -= n;
                     }
-                    QX_AT(sml, h.x) = (a0 + a1) + (a2 + a3);
+                    put_all(&QX_AT(sml, h.x), (a0 + a1) + (a2 + a3), C);
                 }
                 st.finish();
                 break;
             }
             case QX_PH_UNITS: {
-                const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
+                const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 const float x0 = QX_AT(sml, d.one_row);
                 Stream st;
@@ -271,7 +329,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             }
                         }
                     }
-                    atomicAdd(&QX_AT(sml, h.x), acc);  // records into one row may meet
+                    if (h.w & 1)
+                        put_all(&QX_AT(sml, h.x), QX_AT(sml, h.x) + acc, C);  // the row's only record
+                    else
+                        add_all(&QX_AT(sml, h.x), acc, C);  // records into one row meet
                 }
                 st.finish();
                 break;
@@ -279,7 +340,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
             case QX_PH_KSEL: {
                 // per key head, lanes walk machines: the key's first maximal channel (a write
                 // when it is positive) and the query's top-qhot positive channels
-                const uint32_t b0 = d.warp_ptr[ph.c + warp], b1 = d.warp_ptr[ph.c + warp + 1];
+                const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 const float x0 = QX_AT(sml, d.one_row);
                 Stream st;
@@ -325,7 +386,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             i += cnt;
                         }
                     }
-                    ksel[slot * 32 + lane] = ik;
+                    put_all(&ksel[slot * 32 + lane], ik, C);
                     if (npos > 1 && act) atomicOr(&d.err[m], QX_E_KEY);
                     float qb0 = 0.f, qb1 = 0.f, qb2 = 0.f, qb3 = 0.f;
                     int qi0 = -1, qi1 = -1, qi2 = -1, qi3 = -1, qpos = 0;
@@ -365,7 +426,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     const int qs[4] = {qi0, qi1, qi2, qi3};
 #pragma unroll
                     for (int j = 0; j < 4; j++)
-                        if (j < d.qhot_max) qsel[(slot * d.qhot_max + j) * 32 + lane] = j < (int)qhot ? qs[j] : -1;
+                        if (j < d.qhot_max) put_all(&qsel[(slot * d.qhot_max + j) * 32 + lane], j < (int)qhot ? qs[j] : -1, C);
                     if (qpos > (int)qhot && act) atomicOr(&d.err[m], QX_E_QUERY);
                 }
                 st.finish();
@@ -376,7 +437,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // read touches a state row (record: value head, machine, decay factor, write row,
                 // query rows) in the CTA's worklist, which lives in the idle stream rings
                 const uint32_t n = ph.b - ph.a;
-                for (uint32_t i = warp; i < n; i += QX_NW) {
+                uint2 *wl = reinterpret_cast<uint2 *>(rings + qx_vh_worklist_offset(ph.c));
+                for (uint32_t j = warp; j < ph.c; j += QX_NW) delta[j * QX_RP + lane] = 0.0f;
+                for (uint32_t i = gw; i < n; i += nwv) {
                     const qx_vhead vh = d.vheads[ph.a + i];
                     const float x0 = QX_AT(sml, d.one_row);
                     uint32_t fcode = 0;  // decay factor: 0 -> 1, 1 -> 1/2, 2 -> 0
@@ -414,6 +477,8 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // together, then the outputs
                 // the other length was last read by the previous serve phase, a barrier ago
                 const uint32_t cnt = wcount[vpar];
+                const uint2 *wl = reinterpret_cast<const uint2 *>(rings + qx_vh_worklist_offset(ph.c));
+                float *obase = C > 1 ? delta : sm;  // outputs: the CTA's deltas, or the rows
                 if (threadIdx.x == 0) wcount[vpar ^ 1] = 0;
                 vpar ^= 1;
                 for (uint32_t r0 = warp * 4; r0 < cnt; r0 += QX_NW * 4) {
@@ -497,12 +562,24 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             const qx_colform zf = d.zform[vh[b].col + c];
                             const float z = zf.live ? relu(fmaf(zf.c, x0m, QX_ATC(smm, zf.row))) : 0.0f;
                             const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
-                            atomicAdd(&QX_AT(sm + mmv[b], orow), __fmul_rn(__fmul_rn(out, z), d.out_w[vh[b].col + c]));
+                            atomicAdd(&QX_AT(obase + mmv[b], orow), __fmul_rn(__fmul_rn(out, z), d.out_w[vh[b].col + c]));
                         }
                     }
                 }
                 break;
             }
+            case QX_PH_VHSUM:
+                // every CTA's output deltas, in rank order, into this copy's rows
+                for (uint32_t j = warp; j < ph.b; j += QX_NW) {
+                    float v = 0.0f;
+                    for (int r = 0; r < C; r++) {
+                        float pv;
+                        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(peer_addr(delta + j * QX_RP + lane, r)) : "memory");
+                        v += pv;
+                    }
+                    QX_AT(sml, d.vhsum_rows[ph.a + j]) += v;
+                }
+                break;
             case QX_PH_DECODE: {
                 if (warp == 0) {
                     float fam = 0.0f, psum = 0.0f;
@@ -520,8 +597,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     dec_i[lane] = fid;
                     dec_i[32 + lane] = (int)p;
                     if (act) {
-                        if (fraw != fid || p < 0 || p >= d.fam_size[fid]) atomicOr(&d.err[m], QX_E_CODE);
-                        if (tokens) tokens[(size_t)t * d.B + m] = (int32_t)tok;
+                        if (crank == 0) {
+                            if (fraw != fid || p < 0 || p >= d.fam_size[fid]) atomicOr(&d.err[m], QX_E_CODE);
+                            if (tokens) tokens[(size_t)t * d.B + m] = (int32_t)tok;
+                        }
                         hash = fnv_word(hash, (uint32_t)tok);
                         count++;
                         if (halt_at < 0 && tok == d.halt_tok) halt_at = count;
@@ -553,11 +632,11 @@ __global__ void __launch_bounds__(QX_NT, 1)
             default:
                 break;
             }
-            if (!(ph.kind & QX_PH_NOSYNC)) __syncthreads();
+            if (!(ph.kind & QX_PH_NOSYNC)) phase_sync(C);
         }
     }
     if (threadIdx.x == 0 && d.state_bytes) atomicAdd(d.state_bytes, 512ull * *touched);
-    if (RUN) {
+    if (RUN && crank == 0) {
         for (int i = warp; i < d.n_born0; i += QX_NW) {
             uint2 p = d.pairs[i];
             if (act) d.x[(size_t)m * d.D + p.y] = QX_AT(sml, p.x);
@@ -568,6 +647,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
             d.halt_at[m] = halt_at;
         }
     }
+    if (C > 1) phase_sync(C);  // no CTA leaves while a peer may still address its rows
 }
 
 template __global__ void qx_token_kernel<0>(const __grid_constant__ QxDev, int32_t, int32_t *);

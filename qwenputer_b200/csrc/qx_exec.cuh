@@ -20,7 +20,7 @@ struct QxDev {
     const uint32_t *rows;
     const uint2 *pairs;
     const uint4 *stream;
-    const uint32_t *nnz;
+    const uint32_t *vhsum_rows;  // residual rows the cluster's output deltas add into
     const uint32_t *warp_ptr;
     const qx_stage *stages;
     const qx_vhead *vheads;
@@ -47,6 +47,7 @@ struct QxDev {
     int32_t smem_rows, one_row, n_fam, n_pay, n_feat, n_families, n_emb_rows, n_born0;
     int32_t qhot_max, ksel_slots, n_hl, halt_tok;
     uint32_t zero_row;  // byte offset of the row kept at zero
+    int32_t cluster;    // CTAs sharing one group of 32 machines (a thread-block cluster)
 };
 
 // per-machine error bits
@@ -64,9 +65,14 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
 // shared memory: the rows (byte offsets row * 132; row smem_rows is kept at zero), then the
 // key-select slots, the decode area ([2][32] ints, [16][32] payload floats), a 64-byte counter
 // block and the per-warp stream rings ([NW][2][32] quads)
-// value heads one VH phase may list: its 8-byte (value head, machine) records fill the stream
-// rings, 32 machines a value head
-#define QX_VH_CHUNK (QX_NW * 2 * QX_RING_QUADS * 16 / 8 / 32)
+// value heads one VH phase may list (the record packs the phase-local index in 8 bits); its
+// 8-byte (value head, machine) records live in the stream rings, after the phase's output delta
+// rows when the group runs on a cluster
+#define QX_VH_CHUNK 64
+#define QX_RING_BYTES (QX_NW * 2 * QX_RING_QUADS * 16)
+__host__ __device__ inline size_t qx_vh_worklist_offset(uint32_t delta_rows) {
+    return ((size_t)delta_rows * QX_RP * 4 + 15) / 16 * 16;
+}
 
 __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
     // rows (plus the zero row), key-select slots, decode area, counters

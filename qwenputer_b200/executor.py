@@ -50,7 +50,8 @@ def lib():
         L.qx_last_error.restype = C.c_char_p
         for name in ("qx_create", "qx_destroy", "qx_buffer", "qx_reset", "qx_load_machines",
                      "qx_step", "qx_run", "qx_set_tokens", "qx_readback", "qx_checksums",
-                     "qx_errors", "qx_gdn_step", "qx_gdn_step_noalloc"):
+                     "qx_errors", "qx_gdn_step", "qx_gdn_step_noalloc", "qx_info",
+                     "qx_cluster_capacity"):
             getattr(L, name).restype = C.c_int
         L.qx_gdn_work_bytes.restype = C.c_size_t
         L.qx_gdn_work_bytes.argtypes = [C.c_int64]
@@ -104,11 +105,30 @@ def load_graph(c=None) -> graphfile.GraphData:
     return graphfile.export_graph(c)
 
 
-def plan_for(g: graphfile.GraphData):
-    key = id(g)
+def plan_for(g: graphfile.GraphData, cluster: int = 1):
+    key = (id(g), cluster)
     if key not in _plans:
-        _plans[key] = (g, compile_plan(g))
+        _plans[key] = (g, compile_plan(g, cluster=cluster))
     return _plans[key][1]
+
+
+def cluster_capacity(g: graphfile.GraphData, cluster: int, device: int) -> int:
+    """Clusters of `cluster` token-kernel CTAs the device holds at once (qx_cluster_capacity)."""
+    blob = plan_for(g, 1).blob()
+    n = C.c_int32()
+    check(lib().qx_cluster_capacity(blob, C.c_size_t(len(blob)), C.c_int32(device), C.c_int32(cluster),
+                                    C.byref(n)), "qx_cluster_capacity")
+    return int(n.value)
+
+
+def pick_cluster(batch: int, g: graphfile.GraphData, device: int) -> int:
+    """CTAs per group of 32 machines: the largest size (up to 8) whose clusters all fit on the
+    device at once, so a small batch still spreads its work over the SMs (4,096 machines: 1)."""
+    groups = (batch + 31) // 32
+    for c in range(8, 1, -1):
+        if cluster_capacity(g, c, device) >= groups:
+            return c
+    return 1
 
 
 def program_image(prog, keep: list) -> Machine:
@@ -135,15 +155,18 @@ def program_image(prog, keep: list) -> Machine:
 class Executor:
     """Executor2's surface (tritonexec.py:173-289) on the B200 kernel."""
 
-    def __init__(self, c=None, batch: int = 1, device="cuda"):
+    def __init__(self, c=None, batch: int = 1, device="cuda", cluster: int | None = None):
         torch = _torch()
         self.g = load_graph(c)
         self.c = c
-        self.plan = plan_for(self.g)
         self.B = int(batch)
         self.dev = torch.device(device)
         if self.dev.index is None:
             self.dev = torch.device("cuda", torch.cuda.current_device())
+        if cluster is None:
+            cluster = pick_cluster(self.B, self.g, self.dev.index)
+        self.cluster = int(cluster)
+        self.plan = plan_for(self.g, self.cluster)
         self.D = int(self.g.D)
         blob = self.plan.blob()
         self._blob = C.create_string_buffer(blob, len(blob))
@@ -175,6 +198,12 @@ class Executor:
             self.hist_dims.append(self.plan.lag_dims[int(lv)])
             hl += 1
         self.feat_ids = [int(d) for d in self.g.feat_dims[1:]]
+
+    def info(self, what: int) -> int:
+        """qx_info: 0 cluster size, 1 clusters the device holds at once, 2 CTAs a launch, 3 smem."""
+        v = C.c_int64()
+        check(lib().qx_info(self.h, C.c_int32(what), C.byref(v)), "qx_info")
+        return int(v.value)
 
     def _buffer(self, kind: int, i: int, shape, typestr: str):
         torch = _torch()

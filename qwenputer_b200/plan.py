@@ -44,6 +44,7 @@ zero and stands for "no form"):
 
 from __future__ import annotations
 
+import collections
 import heapq
 import struct
 from collections import defaultdict
@@ -56,17 +57,18 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 7
+VERSION = 9
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
-          DECODE=10, END=11, VHRUN=12)
+          DECODE=10, END=11, VHRUN=12, VHSUM=13)
 NOSYNC = 0x100  # phase kind flag: no barrier after the phase
 # value heads a VH phase lists: its worklist of (value head, machine) records, 8 bytes each,
-# lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps)
+# lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps); with a
+# cluster the rings also hold the CTA's output deltas (one row per output row of the phase)
 VH_CHUNK = 64
 UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most this many
-SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "NNZ", "WARP_PTR", "STAGES",
+SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
        "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
        "TABLES", "REG_COLS"]
@@ -85,7 +87,7 @@ DT = {
                        ("cb", "<f4"), ("bconst", "<f4")]),
     "colform": np.dtype([("row", "<u4"), ("pad", "<u2"), ("live", "<u2"), ("c", "<f4")]),
 }
-HEADER = struct.Struct("<QII" + "I" * 14 + "32Q32Q")
+HEADER = struct.Struct("<QII" + "I" * 16 + "32Q32Q")
 
 
 def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int) -> int:
@@ -142,7 +144,7 @@ class Plan:
         head = HEADER.pack(MAGIC, VERSION, h["D"], h["n_slots"], h["n_scratch"], h["nw"],
                            h["n_head_levels"], h["one_row"], h["n_ksel_slots"], h["qhot_max"],
                            h["n_fam"], h["n_pay"], h["n_feat"], h["n_emb_rows"], h["n_families"],
-                           h["vocab"], h["n_born0"], *offs, *cnts)
+                           h["vocab"], h["n_born0"], h["cluster"], 0, *offs, *cnts)
         out = bytearray(pos)
         out[:len(head)] = head
         for p, b in parts:
@@ -151,7 +153,12 @@ class Plan:
 
 
 def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAULT,
-                 ksel_slots: int = 16) -> Plan:
+                 ksel_slots: int = 16, cluster: int = 1) -> Plan:
+    """The phase program and stream of the graph, for CTAs of ``nw`` warps; one group of 32
+    machines runs on a cluster of ``cluster`` CTAs, so stream records are balanced over
+    nw * cluster warps."""
+    assert 1 <= cluster <= 8, cluster
+    ring_bytes = nw * 2 * RING_QUADS * 16
     qhot = int(g.head_qhot.max())
     assert qhot <= 4, "queries may read at most 4 rows"
     if smem_rows is None:
@@ -270,6 +277,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     stream: list[tuple[int, int, int, int]] = []
     warp_ptr_l: list[int] = []
     nnz_l: list[int] = []
+    vhsum_l: list[int] = []  # residual rows (byte offsets) the cluster's output deltas add into
     stages_l, vheads_l, vform_l, zform_l, out_row_l, out_w_l = [], [], [], [], [], []
 
     def entry_quads(terms, rowmap) -> list[tuple]:
@@ -285,19 +293,21 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
             nnz_l.extend(q)
         return start, (len(nnz_l) - start) // 4
 
+    nwv = nw * cluster  # warps of a machine group: every warp of its cluster
+
     def balance(costs: list[float]) -> list[list[int]]:
-        """Longest-first assignment of items to the nw warps."""
-        loads = [(0.0, w) for w in range(nw)]
+        """Longest-first assignment of items to the group's nwv warps."""
+        loads = [(0.0, w) for w in range(nwv)]
         heapq.heapify(loads)
-        per = [[] for _ in range(nw)]
+        per = [[] for _ in range(nwv)]
         for i in sorted(range(len(costs)), key=lambda i: -costs[i]):
             ld, w = heapq.heappop(loads)
             per[w].append(i)
             heapq.heappush(loads, (ld + costs[i], w))
         tot = sum(costs)
         if tot:
-            stats["imbalance_sum"] += max(l for l, _ in loads) - tot / nw
-            stats["balanced_sum"] += tot / nw
+            stats["imbalance_sum"] += max(l for l, _ in loads) - tot / nwv
+            stats["balanced_sum"] += tot / nwv
         return per
 
     def stream_phase(kind: int, records: list[list[tuple]], costs: list[float], prog, a=0, b=0):
@@ -305,7 +315,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         per = balance(costs)
         wp = len(warp_ptr_l)
         warp_ptr_l.append(len(stream))
-        for w in range(nw):
+        for w in range(nwv):
             for i in per[w]:
                 stream.extend(records[i])
             warp_ptr_l.append(len(stream))
@@ -376,7 +386,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 flist = list(gforms)
                 forms_phase(flist, [free[i] for i in range(len(flist))], lambda t: slot[t[1]], body)
                 frow = {f: W(free[i]) for f, i in gforms.items()}
-                recs, costs = [], []
+                recs, costs, outs = [], [], []
                 for n in gnodes:
                     # units grouped by their (a, b) forms; a constant-a unit is (k, cb) with
                     # k = coef * ca rounded as the reference rounds coef * a when a = ca * 1
@@ -417,8 +427,16 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                     for rec, nu, ng in chunks:
                         recs.append(rec)
                         costs.append(6 * nu + 10 * ng + 14)
+                        outs.append(out)
                     stats["units"] += int(g.ffn_uptr[n + 1] - g.ffn_uptr[n])
                     stats["unit_groups"] += len(grp)
+                # a row that only one record of the phase adds into is updated with a plain
+                # read-add-store (header flag 1); rows several records meet in take atomic adds
+                nrec = collections.Counter(outs)
+                for rec, out in zip(recs, outs):
+                    if nrec[out] == 1:
+                        h0 = rec[0]
+                        rec[0] = (h0[0], h0[1], h0[2], 1)
                 stream_phase(PH["UNITS"], recs, costs, body)
             group_stats.append((lv, "ffn", len(groups)))
         else:
@@ -566,10 +584,40 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         vheads_l.append((hi, vhs_level.index(j), col, sl, int(g.vh_nrows[j]),
                                          frow[ta] if ta else ZW, frow[tb] if tb else ZW,
                                          ca, cb, 0.0 if g.vh_has_beta[j] else 1.0))
-                for c0 in range(v0, len(vheads_l), VH_CHUNK):
-                    c1 = min(c0 + VH_CHUNK, len(vheads_l))
-                    body.append((PH["VH"], c0, c1, 0))  # list the machines' row work
-                    body.append((PH["VHRUN"], c0, c1, 0))  # serve it
+                if cluster == 1:
+                    for c0 in range(v0, len(vheads_l), VH_CHUNK):
+                        c1 = min(c0 + VH_CHUNK, len(vheads_l))
+                        body.append((PH["VH"], c0, c1, 0))  # list the machines' row work
+                        body.append((PH["VHRUN"], c0, c1, 0))  # serve it
+                else:
+                    # each CTA sums its outputs into delta rows in its rings (worklist after
+                    # them); a VHSUM phase adds every CTA's deltas into each copy's rows
+                    def fits(nh, nr):
+                        return nh <= VH_CHUNK and (nr * ROW_PAD * 4 + 15) // 16 * 16 + nh * 32 * 8 <= ring_bytes
+
+                    c0 = v0
+                    while c0 < len(vheads_l):
+                        rows: list[int] = []
+                        c1 = c0
+                        while c1 < len(vheads_l):
+                            col = vheads_l[c1][2]
+                            new = [r for r in dict.fromkeys(out_row_l[col:col + HD]) if r != NONE32 and r not in rows]
+                            if not fits(c1 - c0 + 1, len(rows) + len(new)):
+                                break
+                            rows += new
+                            c1 += 1
+                        assert c1 > c0, "one value head's outputs exceed the rings"
+                        dpos = {r: i * ROW_PAD * 4 for i, r in enumerate(rows)}
+                        for v in range(c0, c1):
+                            col = vheads_l[v][2]
+                            for c in range(col, col + HD):
+                                if out_row_l[c] != NONE32:
+                                    out_row_l[c] = dpos[out_row_l[c]]
+                        body.append((PH["VH"], c0, c1, len(rows)))
+                        body.append((PH["VHRUN"], c0, c1, len(rows)))
+                        body.append((PH["VHSUM"], len(vhsum_l), len(rows), 0))
+                        vhsum_l.extend(rows)
+                        c0 = c1
             group_stats.append((lv, "head", len(groups)))
         apply_pairs = [(W(slot[d]), W(slot[k])) for (l2, d), k in temps.items() if l2 == lv]
         tail = []
@@ -603,7 +651,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     s["ROWS"] = np.asarray(rows_l or [0], np.uint32)
     s["PAIRS"] = np.asarray(pairs_l or [(0, 0)], np.uint32).reshape(-1, 2)
     s["STREAM"] = np.asarray(stream or [(0, 0, 0, 0)], np.uint32).reshape(-1, 4)
-    s["NNZ"] = np.asarray(nnz_l or [0, 0, 0, 0], np.uint32)
+    assert not nnz_l
+    s["VHSUM_ROWS"] = np.asarray(vhsum_l or [0], np.uint32)
     s["WARP_PTR"] = np.asarray(warp_ptr_l or [0], np.uint32)
     s["STAGES"] = arr(stages_l, "stage")
     s["VHEADS"] = arr(vheads_l, "vhead")
@@ -633,7 +682,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                  one_row=one_w, n_ksel_slots=ksel_slots, qhot_max=qhot,
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
                  n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
-                 vocab=int(g.vocab), n_born0=len(born0))
+                 vocab=int(g.vocab), n_born0=len(born0), cluster=cluster)
     stats["n_slots"] = n_slots
     stats["n_scratch"] = n_scratch
     stats["phases_run"] = len(run_prog)

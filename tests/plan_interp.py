@@ -47,21 +47,17 @@ class PlanInterp:
         self.H = [np.zeros((3, int(ne), B), np.float32) for ne in s["HL_NE"]]
         self.one = h["one_row"]
         self.ksel, self.qsel = {}, {}
-
-    def form(self, nnz0, nnz4, m=slice(None)):
-        e = self.s["NNZ"][nnz0:nnz0 + 4 * nnz4]
-        rows = (e & 0xFFFF).astype(np.int64)
-        w = (e & 0xFFFF0000).view(np.float32)
-        acc = np.zeros(self.X[0, m].shape, np.float32)
-        for r, ww in zip(rows, w):
-            acc = acc + ww * self.X[r, m]
-        return acc
+        # cluster plans: value-head outputs go to delta rows (in the stream rings), which VHSUM
+        # phases add into the residual rows
+        self.cluster = h["cluster"]
+        self.Dw = np.zeros((128 * 33, B), np.float32)
+        self.delta = _ByteIndexed(self.Dw)
 
     def warp_records(self, c, k):
         """Per warp, the (header, body quads) records of a stream phase."""
         st = self.s["STREAM"].astype(np.int64)
         wp = self.s["WARP_PTR"].astype(np.int64)
-        nw = self.P.hdr["nw"]
+        nw = self.P.hdr["nw"] * self.P.hdr["cluster"]  # the warps of a group's cluster
         out = []
         for w in range(nw):
             i, end = wp[c + w], wp[c + w + 1]
@@ -178,7 +174,12 @@ class PlanInterp:
                         self.qsel[slot] = sel
             elif k == PH["VHRUN"]:
                 pass  # the row work a VH phase lists is done here while it is listed
+            elif k == PH["VHSUM"]:
+                for jj in range(b):
+                    self.X[int(s["VHSUM_ROWS"][a + jj])] += self.delta[jj * 33 * 4]
             elif k == PH["VH"]:
+                self.Dw[:c * 33] = 0
+                out_rows = self.delta if self.cluster > 1 else self.X
                 x0 = self.X[self.one]
                 for vh in s["VHEADS"][a:b]:
                     hl, j, col, sl = int(vh["hl"]), int(vh["vh"]), int(vh["col"]), int(vh["slot"])
@@ -215,5 +216,5 @@ class PlanInterp:
                             zf = s["ZFORM"][col + cc]
                             z = max(self.X[int(zf["row"]), m] + zf["c"] * x0[m], 0) if zf["live"] else 0
                             out = o[cc] / norm if ref > 0 else np.float32(0)
-                            self.X[orow, m] += np.float32(out * np.float32(z)) * s["OUT_W"][col + cc]
+                            out_rows[orow, m] += np.float32(out * np.float32(z)) * s["OUT_W"][col + cc]
         return x

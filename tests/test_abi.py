@@ -6,6 +6,7 @@ import re
 from pathlib import Path
 
 import numpy as np
+import pytest
 
 from conftest import REPO
 
@@ -20,7 +21,7 @@ def test_library_exports_every_declared_symbol():
 
     lib = C.CDLL(str(build.build()))
     names = declared_symbols()
-    assert len(names) == 15, names
+    assert len(names) == 17, names
     for n in names:
         assert hasattr(lib, n), n
 
@@ -58,13 +59,15 @@ def test_bad_plans_are_rejected():
     assert lib.qx_create(bytes(blob[:1000]), C.c_size_t(1000), 4, 0, C.byref(h)) == 1
 
 
-def test_plan_is_consistent(graph):
+@pytest.mark.parametrize("cluster", [1, 4])
+def test_plan_is_consistent(graph, cluster):
     from qwenputer_b200.plan import PH, RING_QUADS, SMEM_MAX, compile_plan, smem_extra_bytes
 
-    P = compile_plan(graph)
+    P = compile_plan(graph, cluster=cluster)
     s = P.sec
     rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * 33 * 4  # byte offsets, zero row included
-    nw = P.hdr["nw"]
+    assert P.hdr["cluster"] == cluster
+    nw = P.hdr["nw"] * cluster  # the warps of a machine group's cluster
     st = s["STREAM"].astype(np.int64)
     wp = s["WARP_PTR"].astype(np.int64)
     # walk every stream record of every phase: rows in range, records end on their warp's range
@@ -105,7 +108,7 @@ def test_plan_is_consistent(graph):
     kinds = [int(k) & 0xFF for k in s["RUN_PROG"]["kind"]]
     assert kinds[-2:] == [PH["DECODE"], PH["END"]] and kinds.count(PH["END"]) == 1
     assert len(s["TABLES"]) == 198
-    smem = (P.hdr["n_slots"] + P.hdr["n_scratch"]) * 33 * 4 + smem_extra_bytes(P.hdr["n_ksel_slots"], P.hdr["qhot_max"], nw)
+    smem = (P.hdr["n_slots"] + P.hdr["n_scratch"]) * 33 * 4 + smem_extra_bytes(P.hdr["n_ksel_slots"], P.hdr["qhot_max"], P.hdr["nw"])
     assert smem <= SMEM_MAX, smem
     assert RING_QUADS == 32
     assert P.hdr["n_born0"] == P.hdr["n_feat"]

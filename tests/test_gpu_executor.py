@@ -42,15 +42,16 @@ def test_load_machines_matches_snapshot(qx, oracle_, programs):
         assert np.array_equal(got, want["S"][i]), f"head sublayer {i}"
 
 
-@pytest.mark.parametrize("batch", [1, 5, 37])
-def test_step_matches_oracle(qx, oracle_, graph, programs, batch):
-    """Teacher-forced steps: every dim of every row equals the oracle's Executor2 step."""
+@pytest.mark.parametrize("batch,cluster", [(1, None), (5, 1), (37, None), (37, 2)])
+def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster):
+    """Teacher-forced steps: every dim of every row equals the oracle's Executor2 step (cluster
+    None: the executor's own choice, 8 CTAs a group at these batches)."""
     pool = ["gen_small_7", "div_fuzz_0", "mul_fuzz_1", "digit_file", "gen_base_1", "refresh_70",
             "zba_rodata", "gen_many_11", "csr_putchar"]
     names = [pool[i % len(pool)] for i in range(batch)]
     progs = [programs[n]["prog"] for n in names]
     traces = [programs[n]["trace"] for n in names]
-    ex = qx.Executor(None, batch=batch)
+    ex = qx.Executor(None, batch=batch, cluster=cluster)
     ex.load_machines(0, progs)
     ost = _oracle_state(oracle_, progs)
     T = 60 if batch > 8 else 120
@@ -68,8 +69,8 @@ def test_step_matches_oracle(qx, oracle_, graph, programs, batch):
     assert ex.errors() == 0
 
 
-@pytest.mark.parametrize("batch,n", [(1, 3000), (40, 1500)])
-def test_free_run_matches_machine(qx, programs, batch, n):
+@pytest.mark.parametrize("batch,n,cluster", [(1, 3000, None), (40, 1500, None), (40, 1500, 1)])
+def test_free_run_matches_machine(qx, programs, batch, n, cluster):
     """Free-running generation: every token equals the traced machine's, and the machine state
     read back from the heads equals the traced state after the last complete record."""
     from qwenputer_b200 import workload
@@ -77,7 +78,7 @@ def test_free_run_matches_machine(qx, programs, batch, n):
     progs = [programs[k]["prog"] for k in sorted(programs)]
     progs += workload.workload_programs("many", max(0, batch - len(progs)), 500)
     progs = progs[:batch]
-    ex = qx.Executor(None, batch=batch)
+    ex = qx.Executor(None, batch=batch, cluster=cluster)
     ex.load_machines(0, progs)
     ex.reset()
     go = int(oracle.lib().qxo_tok_family(18, 0))  # GO: the seventh control after 12 families
@@ -98,6 +99,34 @@ def test_free_run_matches_machine(qx, programs, batch, n):
         assert np.array_equal(np.ctypeslib.as_array(rb.ram), np.ctypeslib.as_array(st.ram)), r
         assert int(sums[r]) == st.checksum(), r
     assert ex.errors() == 0
+
+
+def test_cluster_sizes_agree(qx):
+    """One group of 32 machines on 1, 2, 4 or 8 CTAs of a cluster: the same tokens, states and
+    checksums (96 machines of the bignum workload, 400 tokens)."""
+    from qwenputer_b200 import workload
+
+    progs = workload.workload_programs("bignum", 96, 77)
+    go = int(oracle.lib().qxo_tok_family(18, 0))
+    outs = []
+    for cluster in (1, 2, 4, 8):
+        ex = qx.Executor(None, batch=96, cluster=cluster)
+        assert ex.info(0) == cluster and ex.info(2) == 3 * cluster and ex.info(1) >= 1
+        ex.load_machines(0, progs)
+        ex.reset()
+        ex.set_tokens(0, [go] * 96)
+        out = torch.zeros(400, 96, dtype=torch.int32, device="cuda")
+        ex.run(400, out)
+        heads = [s["S"] for s in ex.steps if s["kind"] == "head"]
+        outs.append((out.cpu().numpy(), ex.checksums().cpu().numpy(),
+                     [float(h.double().sum()) for h in heads], ex.x.cpu().numpy()))
+        assert ex.errors() == 0
+        del ex
+    for o in outs[1:]:
+        assert np.array_equal(o[0], outs[0][0])
+        assert np.array_equal(o[1], outs[0][1])
+        assert o[2] == outs[0][2]
+        assert np.array_equal(o[3], outs[0][3])
 
 
 def test_free_run_in_chunks_equals_one_run(qx, programs):

@@ -8,11 +8,11 @@ import oracle
 from plan_interp import PlanInterp
 
 
-@pytest.mark.parametrize("names", [["gen_small_7", "div_fuzz_0"], ["digit_file", "refresh_70"]])
-def test_plan_program_matches_oracle(oracle_, graph, programs, names):
+@pytest.mark.parametrize("names,cluster", [(["gen_small_7", "div_fuzz_0"], 1), (["digit_file", "refresh_70"], 8)])
+def test_plan_program_matches_oracle(oracle_, graph, programs, names, cluster):
     from qwenputer_b200.plan import compile_plan
 
-    P = compile_plan(graph)
+    P = compile_plan(graph, cluster=cluster)
     B = len(names)
     it = PlanInterp(P, B)
     ost = oracle_.new_state(B)
