@@ -5,13 +5,15 @@
     torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU)
 
 Workload: the bignum-heavy mix of seeded RV32IM programs (40% MUL/MULH/DIVU chains, 20% loads /
-stores over a 16 KB range, the rest like the base generator), ``--machines`` independent machines
-per GPU (4,096 by default) started from their program images.  A step is one launch of the
-persistent token kernel: ``--tokens-per-step`` free-running tokens for every local machine (each
-token is decoded into the next input on the device).  Machines are sharded across ranks with no
-per-step communication ("scaling": "weak": every GPU runs its own 4,096 machines); one NCCL
-all-gather of the per-machine state checksums closes the run.  The head states (12.5 MB per
-machine, 51 GB per GPU) are far larger than L2, so no flush is needed between steps.
+stores over a 16 KB range, the rest like the base generator): ``--machines`` independent machines
+(4,096 by default) started from their program images and split evenly over the ranks ("scaling":
+"strong": 4,096 on one GPU, 512 on each of eight; ``--weak`` runs ``--machines`` on every GPU).
+A step is one launch of the persistent token kernel: ``--tokens-per-step`` free-running tokens
+for every local machine (each token is decoded into the next input on the device).  With fewer
+machines per GPU each group of 32 machines runs on a thread-block cluster of several CTAs, so the
+SMs stay busy.  Ranks exchange nothing per step; one NCCL all-gather of the per-machine state
+checksums closes the run.  The head states (12.5 MB per machine, 51 GB on one GPU) are far larger
+than L2, so no flush is needed between steps.
 
 The JSON line also carries the gated delta-rule decode-step microbenchmark (1,024 sequences x 48
 heads, dk = dv = 128) with its HBM roofline.
@@ -36,6 +38,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "rv32im_trace_tokens_per_s"
+WORKLOAD = "rv32im free-run, bignum mix (40% MUL/MULH/DIVU chains, 20% LW/SW over 16 KB)"
 UNIT = "tokens/s"
 GO_TOKEN = 230322  # the run-start control (families then controls: NT .. HALT, GO, SC)
 
@@ -46,9 +49,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--machines", type=int, default=4096, help="machines per GPU")
-    ap.add_argument("--strong", action="store_true",
-                    help="split --machines across the ranks instead of running them per GPU")
+    ap.add_argument("--machines", type=int, default=4096,
+                    help="machines of the whole job, split evenly over the ranks")
+    ap.add_argument("--weak", action="store_true", help="run --machines on every GPU instead")
+    ap.add_argument("--cluster", type=int, default=None,
+                    help="CTAs per group of 32 machines (default: the executor's choice)")
     ap.add_argument("--tokens-per-step", type=int, default=200)
     ap.add_argument("--no-gdn", action="store_true")
     ap.add_argument("--gdn-sequences", type=int, default=1024,
@@ -226,9 +231,10 @@ def reference_arm(args) -> None:
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: seeded RV32IM programs (bignum mix)",
-        "config": {"workload": "rv32im free-run, bignum mix", "machines_per_gpu": args.machines,
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic: seeded RV32IM programs (bignum mix)",
+        "config": {"workload": WORKLOAD,
+                   "machines_total": args.machines * (args.gpus if args.weak else 1),
                    "tokens_per_step": tps, "sample_machines": B},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -258,10 +264,10 @@ def main() -> None:
     from qwenputer_b200 import workload
     from qwenputer_b200.executor import Executor
 
-    B = args.machines // world if args.strong else args.machines
+    B = args.machines if args.weak else args.machines // world
     seed0 = args.seed + rank * B
     progs = workload.workload_programs("bignum", B, seed0)
-    ex = Executor(None, batch=B)
+    ex = Executor(None, batch=B, cluster=args.cluster)
     ex.load_machines(0, progs)
     ex.reset()
     ex.set_tokens(0, [GO_TOKEN] * B)
@@ -365,12 +371,14 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded RV32IM programs (bignum mix), machines start from their images",
-            "config": {"workload": "rv32im free-run, bignum mix (40% MUL/MULH/DIVU chains, 20% LW/SW over 16 KB)",
+            "config": {"workload": WORKLOAD,
                        "machines_per_gpu": B, "machines_total": B * world,
                        "tokens_per_step": tps, "parallelism": f"machines sharded over {world} GPU(s)",
-                       "l2": "no flush: 51 GB of head states per GPU, far above L2"},
+                       "ctas_per_group": ex.cluster, "groups_per_gpu": (B + 31) // 32,
+                       "clusters_resident": ex.info(1),
+                       "l2": f"no flush: {B * 12.5e6 / 1e9:.0f} GB of head states per GPU, far above L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
                          "algorithmic_bytes_per_launch": alg_bytes,

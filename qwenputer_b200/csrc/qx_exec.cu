@@ -93,43 +93,48 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// A warp's view of its range [begin, end) of the plan stream, read through a ring of two halves
-// of QX_RING_QUADS quads: while the warp reads one half, the next half is in flight.
+// A warp's view of its range [begin, end) of the plan stream, read through a ring of QX_NCHUNK
+// chunks of QX_CHUNK quads: while the warp reads one chunk, the next QX_NCHUNK - 1 are in flight.
+#define QX_CHUNK 32
+#define QX_NCHUNK 2
+static_assert(QX_CHUNK * QX_NCHUNK == 2 * QX_RING_QUADS, "a warp's ring holds 2 * QX_RING_QUADS quads");
 struct Stream {
     const uint4 *g;
-    uint4 *ring;        // this warp's 2 * QX_RING_QUADS quads
+    uint4 *ring;        // this warp's QX_NCHUNK * QX_CHUNK quads
     const uint4 *rp;    // next quad to read (in the ring)
     uint32_t begin, end, chunk;
-    int left, lane;     // quads left in the current half
+    int left, lane;     // quads left in the current chunk
 
     __device__ __forceinline__ void issue(uint32_t c) {
-        const uint32_t q = begin + c * QX_RING_QUADS + lane;
-        if (q < end) cp_async16(ring + (c & 1) * QX_RING_QUADS + lane, g + q);
+        const uint32_t q = begin + c * QX_CHUNK + lane;
+        if (lane < QX_CHUNK && q < end) cp_async16(ring + (c % QX_NCHUNK) * QX_CHUNK + lane, g + q);
         cp_commit();
     }
     __device__ __forceinline__ void settle() {
-        rp = ring + (chunk & 1) * QX_RING_QUADS;
-        const uint32_t rest = end - (begin + chunk * QX_RING_QUADS);
-        left = rest < QX_RING_QUADS ? (int)rest : QX_RING_QUADS;
+        rp = ring + (chunk % QX_NCHUNK) * QX_CHUNK;
+        const uint32_t rest = end - (begin + chunk * QX_CHUNK);
+        left = rest < QX_CHUNK ? (int)rest : QX_CHUNK;
     }
+    // begin reading: the first QX_NCHUNK chunks in flight, wait for the first
     __device__ __forceinline__ void start(const uint4 *g_, uint4 *ring_, uint32_t b, uint32_t e, int l) {
         g = g_; ring = ring_; begin = b; end = e; lane = l; chunk = 0;
-        issue(0);
-        issue(1);
-        cp_wait<1>();
+#pragma unroll
+        for (int c = 0; c < QX_NCHUNK; c++) issue(c);
+        cp_wait<QX_NCHUNK - 1>();
         __syncwarp();
         settle();
     }
-    // the next half: once every lane is done with the current one, refill it two halves ahead
+    // the next chunk: once every lane is done with the current one, refill its slot
+    // QX_NCHUNK chunks ahead
     __device__ __forceinline__ void advance() {
         chunk++;
         __syncwarp();
-        issue(chunk + 1);
-        cp_wait<1>();
+        issue(chunk + QX_NCHUNK - 1);
+        cp_wait<QX_NCHUNK - 1>();
         __syncwarp();
         settle();
     }
-    __device__ __forceinline__ bool more() const { return left > 0 || begin + (chunk + 1) * QX_RING_QUADS < end; }
+    __device__ __forceinline__ bool more() const { return left > 0 || begin + (chunk + 1) * QX_CHUNK < end; }
     __device__ __forceinline__ uint4 next() {
         if (left == 0) advance();
         left--;
@@ -153,12 +158,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
     float *dec_pay = reinterpret_cast<float *>(dec_i + 64);                  // [16][32]
     unsigned int *touched = reinterpret_cast<unsigned int *>(dec_pay + 16 * 32);  // state rows
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // a group of 32 machines runs on C CTAs; stream ranges are per warp of the group (gw of nwv)
+    // a group of 32 machines runs on C CTAs; stream ranges are per warp of the group (gw of nwv),
+    // interleaved over the CTAs (the plan hands its largest records to the lowest warps)
     const int C = d.cluster;
     const int crank = C > 1 ? (int)cluster_rank() : 0;
-    const int gw = crank * QX_NW + warp, nwv = C * QX_NW;
+    const int gw = warp * C + crank, nwv = C * QX_NW;
     uint4 *ring = reinterpret_cast<uint4 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d)) +
-                  warp * 2 * QX_RING_QUADS;
+                  warp * QX_NCHUNK * QX_CHUNK;
     float *sml = sm + lane;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
     unsigned int *wcount = touched + 1;  // [2] value-head worklist lengths, used in turn
     int vpar = 0;                        // which of the two the next VH phase appends to
