@@ -38,6 +38,9 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "rv32im_trace_tokens_per_s"
+# DRAM bytes per machine-token of the token kernel: an ncu capture of 256 machines x 4 tokens
+# (dram__bytes_read.sum + dram__bytes_write.sum = 10.84 MB + 0 B), per machine-token
+DRAM_BYTES_PER_MACHINE_TOKEN = 10.84e6 / 1024
 WORKLOAD = "rv32im free-run, bignum mix (40% MUL/MULH/DIVU chains, 20% LW/SW over 16 KB)"
 UNIT = "tokens/s"
 GO_TOKEN = 230322  # the run-start control (families then controls: NT .. HALT, GO, SC)
@@ -380,7 +383,10 @@ def main() -> None:
                        "clusters_resident": ex.info(1),
                        "l2": f"no flush: {B * 12.5e6 / 1e9:.0f} GB of head states per GPU, far above L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": DRAM_BYTES_PER_MACHINE_TOKEN * B * tps,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                           "256-machine x 4-token launch, scaled by machine-tokens",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "weight_bytes_per_token": w_bytes,
                          "state_bytes_per_machine_token": state_per_launch / (tps * B)},
