@@ -267,8 +267,9 @@ def main() -> None:
     from qwenputer_b200 import workload
     from qwenputer_b200.executor import Executor
 
-    B = args.machines if args.weak else args.machines // world
-    seed0 = args.seed + rank * B
+    from qwenputer_b200.shard import combine, gather_checksums, shard
+
+    B, seed0 = shard(args.machines, world, rank, args.weak, args.seed)
     progs = workload.workload_programs("bignum", B, seed0)
     ex = Executor(None, batch=B, cluster=args.cluster)
     ex.load_machines(0, progs)
@@ -324,12 +325,7 @@ def main() -> None:
 
     # checksums of every machine's state: the one collective
     sums = ex.checksums()
-    if dist:
-        allsums = torch.empty(world * B, dtype=torch.int64, device="cuda")
-        dist.all_gather_into_tensor(allsums, sums)
-    else:
-        allsums = sums
-    combined = int(np.bitwise_xor.reduce(allsums.cpu().numpy().view(np.uint64)))
+    combined = combine(gather_checksums(sums, dist))
     errs = ex.errors()
 
     # end to end through the public API: per step, the machines' images go host -> device, the
