@@ -10,8 +10,14 @@
 #include "qx.h"
 #include "qx_exec.cuh"
 
-template <int RUN>
+template <int RUN, int QH>
 __global__ void qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens);
+// the token kernel instantiation for the plan: run or step mode, query rows per read (2 or 4)
+template <int RUN>
+void *token_kernel_for(const QxDev &d) {
+    return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2>)
+                           : reinterpret_cast<void *>(qx_token_kernel<RUN, 4>);
+}
 __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok);
 __global__ void qx_predecode_kernel(const QxImage *img, uint32_t *pool, int32_t n);
 __global__ void qx_load_kernel(const __grid_constant__ QxDev d, const QxImage *img, const uint32_t *pool,
@@ -74,10 +80,8 @@ template <int RUN>
 cudaError_t launch_token(const qx_t *ex, const QxDev &d, int32_t n_tokens, int32_t *tokens, cudaStream_t st) {
     const int C = d.cluster;
     const unsigned grid = (unsigned)(ex->Bpad / 32 * C);
-    if (C == 1) {
-        qx_token_kernel<RUN><<<grid, QX_NT, ex->smem, st>>>(d, n_tokens, tokens);
-        return cudaGetLastError();
-    }
+    void *args[] = {const_cast<QxDev *>(&d), &n_tokens, &tokens};
+    if (C == 1) return cudaLaunchKernel(token_kernel_for<RUN>(d), dim3(grid), dim3(QX_NT), args, ex->smem, st);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(QX_NT);
@@ -90,7 +94,7 @@ cudaError_t launch_token(const qx_t *ex, const QxDev &d, int32_t n_tokens, int32
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, qx_token_kernel<RUN>, d, n_tokens, tokens);
+    return cudaLaunchKernelExC(&cfg, token_kernel_for<RUN>(d), args);
 }
 
 qx_status dev_alloc(qx_t *ex, void **p, size_t bytes) {
@@ -301,9 +305,9 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     if ((int)ex->smem > optin)
         return bail(fail(QX_ERR_INVALID_PLAN, "plan needs %zu B of shared memory per CTA, device has %d", ex->smem,
                          optin));
-    if (cudaFuncSetAttribute(qx_token_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
+    if (cudaFuncSetAttribute(token_kernel_for<0>(d), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
             cudaSuccess ||
-        cudaFuncSetAttribute(qx_token_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
+        cudaFuncSetAttribute(token_kernel_for<1>(d), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
             cudaSuccess || qx_gdn_prepare() != cudaSuccess)
         return bail(fail(QX_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError())));
     {
@@ -319,7 +323,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
         at[0].val.clusterDim.z = 1;
         cfg.attrs = at;
         cfg.numAttrs = 1;
-        cudaError_t e2 = cudaOccupancyMaxActiveClusters(&ex->max_clusters, qx_token_kernel<1>, &cfg);
+        cudaError_t e2 = cudaOccupancyMaxActiveClusters(&ex->max_clusters, token_kernel_for<1>(d), &cfg);
         if (e2 != cudaSuccess || ex->max_clusters < 1)
             return bail(fail(QX_ERR_CUDA, "a cluster of %d CTAs with %zu B of shared memory each does not fit: %s",
                              d.cluster, ex->smem, cudaGetErrorString(e2)));
@@ -531,7 +535,7 @@ qx_status qx_cluster_capacity(const void *plan, size_t plan_bytes, int32_t devic
     d.ksel_slots = (int32_t)h.n_ksel_slots;
     const size_t smem = qx_smem_bytes(d);
     CU(cudaSetDevice(device));
-    CU(cudaFuncSetAttribute(qx_token_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    CU(cudaFuncSetAttribute(token_kernel_for<1>(d), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cluster);
     cfg.blockDim = dim3(QX_NT);
@@ -544,7 +548,7 @@ qx_status qx_cluster_capacity(const void *plan, size_t plan_bytes, int32_t devic
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    CU(cudaOccupancyMaxActiveClusters(&n, qx_token_kernel<1>, &cfg));
+    CU(cudaOccupancyMaxActiveClusters(&n, token_kernel_for<1>(d), &cfg));
     *max_clusters = n;
     return QX_OK;
 }

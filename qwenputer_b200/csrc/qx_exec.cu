@@ -148,7 +148,7 @@ struct Stream {
 
 }  // namespace
 
-template <int RUN>
+template <int RUN, int QH>
 __global__ void __launch_bounds__(QX_NT, 1)
     qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens) {
     extern __shared__ __align__(16) float sm[];
@@ -467,20 +467,27 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     const bool need = act && (fcode != 0 || wrow >= 0 || anyq);
                     const unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
                     if (!mask) continue;
+                    // the value head's records, padded to a multiple of four (pad records: bit 31)
+                    // so that every batch of four the serving warps take shares one value head
+                    const unsigned nrec = __popc(mask), npad = ((nrec + 3u) & ~3u) - nrec;
                     unsigned base = 0;
-                    if (lane == 0) base = atomicAdd(wcount + vpar, (unsigned)__popc(mask));
+                    if (lane == 0) base = atomicAdd(wcount + vpar, nrec + npad);
                     base = __shfl_sync(0xFFFFFFFFu, base, 0);
                     if (need) {
                         const unsigned pos = base + __popc(mask & ((1u << lane) - 1u));
                         wl[pos] = make_uint2(i | (uint32_t)lane << 8 | fcode << 13 | (uint32_t)(wrow + 1) << 16, qpack);
                     }
+                    if ((unsigned)lane < npad) wl[base + nrec + lane] = make_uint2(i | 1u << 31, 0u);
                 }
                 break;
             }
             case QX_PH_VHRUN: {
-                // the listed row work, four records a warp at a time with lanes over columns
-                // (4 each): decays and writes first, then every record's query rows in flight
-                // together, then the outputs
+                // the listed row work, four records (one value head, four machines) a warp at a
+                // time with lanes over columns (4 each).  Every state-row load of the batch (the
+                // decayed rows, the query rows) and every column descriptor is issued before any
+                // result is needed; reads then take the decayed or written value from registers:
+                // the read of row r sees v if r is the write row, old * f if r < nrows, else old
+                // (decay, then write, then read, as the reference orders them).
                 // the other length was last read by the previous serve phase, a barrier ago
                 const uint32_t cnt = wcount[vpar];
                 const uint2 *wl = reinterpret_cast<const uint2 *>(rings + qx_vh_worklist_offset(ph.c));
@@ -488,30 +495,63 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 if (threadIdx.x == 0) wcount[vpar ^ 1] = 0;
                 vpar ^= 1;
                 for (uint32_t r0 = warp * 4; r0 < cnt; r0 += QX_NW * 4) {
-                    qx_vhead vh[4];
-                    int mmv[4], wr[4], qr[4][4];
+                    uint2 rec[4];
+#pragma unroll
+                    for (int b = 0; b < 4; b++) rec[b] = wl[r0 + b];
+                    const qx_vhead vh = d.vheads[ph.a + (rec[0].x & 0xFFu)];
+                    const size_t mstride = (size_t)d.V[vh.hl] * (QX_HD * QX_HD);
+                    const float *S0 = d.S[vh.hl] + (size_t)vh.vh * (QX_HD * QX_HD) + lane * 4;
+                    int mmv[4], wr[4], qr[4][QH];
                     float f[4];
-                    bool valid[4];
+                    bool valid[4], anyw = false, anyq = false;
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
-                        valid[b] = r0 + b < cnt;
-                        const uint2 rec = valid[b] ? wl[r0 + b] : make_uint2(0u, 0u);
-                        vh[b] = d.vheads[ph.a + (rec.x & 0xFFu)];
-                        mmv[b] = (rec.x >> 8) & 31;
-                        const uint32_t fc = (rec.x >> 13) & 3u;
+                        valid[b] = !(rec[b].x >> 31);
+                        mmv[b] = (rec[b].x >> 8) & 31;
+                        const uint32_t fc = (rec[b].x >> 13) & 3u;
                         f[b] = fc == 0 ? 1.0f : (fc == 1 ? 0.5f : 0.0f);
-                        wr[b] = valid[b] ? (int)((rec.x >> 16) & 0xFFu) - 1 : -1;
+                        wr[b] = valid[b] ? (int)((rec[b].x >> 16) & 0xFFu) - 1 : -1;
+                        anyw |= wr[b] >= 0;
 #pragma unroll
-                        for (int j = 0; j < 4; j++) qr[b][j] = valid[b] ? (int)((rec.y >> (8 * j)) & 0xFFu) - 1 : -1;
+                        for (int j = 0; j < QH; j++) {
+                            qr[b][j] = valid[b] ? (int)((rec[b].y >> (8 * j)) & 0xFFu) - 1 : -1;
+                            anyq |= qr[b][j] >= 0;
+                        }
+                    }
+                    // loads: query rows (old values), then the column descriptors
+                    float4 qv[4][QH];
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        const float *Sb = S0 + (size_t)(mbase + mmv[b]) * mstride;
+#pragma unroll
+                        for (int j = 0; j < QH; j++)
+                            qv[b][j] = qr[b][j] >= 0 ? *reinterpret_cast<const float4 *>(Sb + qr[b][j] * QX_HD)
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                    qx_colform vf[4], zf[4];
+                    uint32_t orow[4];
+                    float ow[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const uint32_t c = vh.col + lane * 4 + k;
+                        if (anyw) vf[k] = d.vform[c];
+                        if (anyq) {
+                            zf[k] = d.zform[c];
+                            orow[k] = d.out_row[c];
+                            ow[k] = d.out_w[c];
+                        }
                     }
                     unsigned int rows = 0;  // 512-byte row transfers
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
                         if (!valid[b]) continue;
-                        float *Sb = d.S[vh[b].hl] + ((size_t)(mbase + mmv[b]) * d.V[vh[b].hl] + vh[b].vh) * (QX_HD * QX_HD) + lane * 4;
+                        float *Sb = const_cast<float *>(S0) + (size_t)(mbase + mmv[b]) * mstride;
+                        const float *smm = sm + mmv[b];
+                        const float x0m = QX_ATC(smm, d.one_row);
+                        // decay of the first nrows rows (rare: a read-modify-write of its own)
                         if (f[b] != 1.0f) {
-                            rows += 2 * vh[b].nrows;
-                            for (int r = 0; r < vh[b].nrows; r++) {
+                            rows += 2 * vh.nrows;
+                            for (int r = 0; r < vh.nrows; r++) {
                                 float4 *p = reinterpret_cast<float4 *>(Sb + r * QX_HD);
                                 float4 sv = *p;
                                 sv.x = __fmul_rn(sv.x, f[b]); sv.y = __fmul_rn(sv.y, f[b]);
@@ -519,58 +559,48 @@ __global__ void __launch_bounds__(QX_NT, 1)
                                 *p = sv;
                             }
                         }
+                        float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
                         if (wr[b] >= 0) {
-                            const float *smm = sm + mmv[b];
-                            const float x0m = QX_ATC(smm, d.one_row);
                             float v[4];
 #pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                const qx_colform cf = d.vform[vh[b].col + lane * 4 + i];
-                                v[i] = cf.live ? relu(fmaf(cf.c, x0m, QX_ATC(smm, cf.row))) : 0.0f;
-                            }
-                            *reinterpret_cast<float4 *>(Sb + wr[b] * QX_HD) = make_float4(v[0], v[1], v[2], v[3]);
+                            for (int k = 0; k < 4; k++)
+                                v[k] = vf[k].live ? relu(fmaf(vf[k].c, x0m, QX_ATC(smm, vf[k].row))) : 0.0f;
+                            wv = make_float4(v[0], v[1], v[2], v[3]);
+                            *reinterpret_cast<float4 *>(Sb + wr[b] * QX_HD) = wv;
                             rows++;
                         }
-                    }
-                    float4 o[4];
-                    bool any[4];
+                        // the read: sum of the query rows as decayed and written
+                        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                        bool any = false;
 #pragma unroll
-                    for (int b = 0; b < 4; b++) {
-                        o[b] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        any[b] = false;
-                        const float *Sb = d.S[vh[b].hl] + ((size_t)(mbase + mmv[b]) * d.V[vh[b].hl] + vh[b].vh) * (QX_HD * QX_HD) + lane * 4;
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            if (qr[b][j] >= 0) {
-                                const float4 sv = *reinterpret_cast<const float4 *>(Sb + qr[b][j] * QX_HD);
-                                o[b].x = __fadd_rn(o[b].x, sv.x); o[b].y = __fadd_rn(o[b].y, sv.y);
-                                o[b].z = __fadd_rn(o[b].z, sv.z); o[b].w = __fadd_rn(o[b].w, sv.w);
-                                any[b] = true;
-                                rows++;
+                        for (int j = 0; j < QH; j++) {
+                            if (qr[b][j] < 0) continue;
+                            float4 sv = qv[b][j];
+                            if (qr[b][j] == wr[b]) {
+                                sv = wv;
+                            } else if (qr[b][j] < (int)vh.nrows && f[b] != 1.0f) {
+                                sv.x = __fmul_rn(sv.x, f[b]); sv.y = __fmul_rn(sv.y, f[b]);
+                                sv.z = __fmul_rn(sv.z, f[b]); sv.w = __fmul_rn(sv.w, f[b]);
                             }
+                            o.x = __fadd_rn(o.x, sv.x); o.y = __fadd_rn(o.y, sv.y);
+                            o.z = __fadd_rn(o.z, sv.z); o.w = __fadd_rn(o.w, sv.w);
+                            any = true;
+                            rows++;
+                        }
+                        if (!any) continue;
+                        float ref = __fadd_rn(__fmul_rn(o.x, o.x), __fmul_rn(o.y, o.y));
+                        ref = __shfl_sync(0xFFFFFFFFu, ref, 0);  // (uniform: the batch's records are)
+                        const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
+                        const float oc[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            if (orow[k] == QX_NONE32) continue;
+                            const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
+                            const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
+                            atomicAdd(&QX_AT(obase + mmv[b], orow[k]), __fmul_rn(__fmul_rn(out, z), ow[k]));
                         }
                     }
                     if (lane == 0) atomicAdd(touched, rows);
-#pragma unroll
-                    for (int b = 0; b < 4; b++) {
-                        if (!any[b]) continue;
-                        const float *smm = sm + mmv[b];
-                        const float x0m = QX_ATC(smm, d.one_row);
-                        float ref = __fadd_rn(__fmul_rn(o[b].x, o[b].x), __fmul_rn(o[b].y, o[b].y));
-                        ref = __shfl_sync(0xFFFFFFFFu, ref, 0);
-                        const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
-                        const float oc[4] = {o[b].x, o[b].y, o[b].z, o[b].w};
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const int c = lane * 4 + i;
-                            const uint32_t orow = d.out_row[vh[b].col + c];
-                            if (orow == QX_NONE32) continue;
-                            const qx_colform zf = d.zform[vh[b].col + c];
-                            const float z = zf.live ? relu(fmaf(zf.c, x0m, QX_ATC(smm, zf.row))) : 0.0f;
-                            const float out = ref > 0.0f ? __fdiv_rn(oc[i], norm) : 0.0f;
-                            atomicAdd(&QX_AT(obase + mmv[b], orow), __fmul_rn(__fmul_rn(out, z), d.out_w[vh[b].col + c]));
-                        }
-                    }
                 }
                 break;
             }
@@ -656,8 +686,11 @@ __global__ void __launch_bounds__(QX_NT, 1)
     if (C > 1) phase_sync(C);  // no CTA leaves while a peer may still address its rows
 }
 
-template __global__ void qx_token_kernel<0>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1>(const __grid_constant__ QxDev, int32_t, int32_t *);
+// QH: query rows a value head reads, at most (2 when the plan's heads read at most 2, else 4)
+template __global__ void qx_token_kernel<0, 2>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<1, 2>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<0, 4>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<1, 4>(const __grid_constant__ QxDev, int32_t, int32_t *);
 
 // Sets rows [row0, row0 + n) of x to the embeddings of the given tokens (FreeRun.load).
 __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok) {
