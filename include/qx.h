@@ -156,7 +156,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 9
+#define QX_PLAN_VERSION 10
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

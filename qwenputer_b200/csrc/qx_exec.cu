@@ -135,11 +135,6 @@ struct Stream {
         settle();
     }
     __device__ __forceinline__ bool more() const { return left > 0 || begin + (chunk + 1) * QX_CHUNK < end; }
-    __device__ __forceinline__ uint4 next() {
-        if (left == 0) advance();
-        left--;
-        return *rp++;
-    }
     __device__ __forceinline__ void finish() {
         cp_wait<0>();
         __syncwarp();
@@ -244,196 +239,186 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             case QX_PH_FORMS: {
+                // pieces [dst, 0, 0, n | flags] + n quads [row, w, row, w]: F = sum w * X[row]
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
-                while (st.more()) {
-                    const uint4 h = st.next();
-                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                    int nq = (int)h.y;
-                    while (nq > 0) {
-                        if (st.left == 0) st.advance();
-                        const int n = nq < st.left ? nq : st.left;
-                        const uint4 *rp = st.rp;
-                        int j = 0;
-                        for (; j + 4 <= n; j += 4) {
-                            const uint4 e0 = rp[j], e1 = rp[j + 1], e2 = rp[j + 2], e3 = rp[j + 3];
-                            const float v0 = QX_AT(sml, e0.x), v1 = QX_AT(sml, e0.z), v2 = QX_AT(sml, e1.x),
-                                        v3 = QX_AT(sml, e1.z), v4 = QX_AT(sml, e2.x), v5 = QX_AT(sml, e2.z),
-                                        v6 = QX_AT(sml, e3.x), v7 = QX_AT(sml, e3.z);
-                            a0 = fmaf(__uint_as_float(e0.y), v0, a0);
-                            a1 = fmaf(__uint_as_float(e0.w), v1, a1);
-                            a2 = fmaf(__uint_as_float(e1.y), v2, a2);
-                            a3 = fmaf(__uint_as_float(e1.w), v3, a3);
-                            a0 = fmaf(__uint_as_float(e2.y), v4, a0);
-                            a1 = fmaf(__uint_as_float(e2.w), v5, a1);
-                            a2 = fmaf(__uint_as_float(e3.y), v6, a2);
-                            a3 = fmaf(__uint_as_float(e3.w), v7, a3);
-                        }
-                        for (; j < n; j++) {
-                            const uint4 e = rp[j];
-                            a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
-                            a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
-                        }
-                        st.rp += n;
-                        st.left -= n;
-                        nq -= n;
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                while (true) {
+                    if (st.left == 0) {
+                        if (!st.more()) break;
+                        st.advance();
                     }
-                    put_all(&QX_AT(sml, h.x), (a0 + a1) + (a2 + a3), C);
+                    const uint4 h = st.rp[0];
+                    const uint32_t n = h.w & 0xFFFFFFu, fl = h.w >> 24;
+                    if (fl & QX_R_SKIP) {
+                        st.left = 0;
+                        continue;
+                    }
+                    const uint4 *q = st.rp + 1;
+                    if (fl & QX_R_FIRST) a0 = a1 = a2 = a3 = 0.0f;
+                    uint32_t j = 0;
+                    for (; j + 2 <= n; j += 2) {
+                        const uint4 e0 = q[j], e1 = q[j + 1];
+                        const float v0 = QX_AT(sml, e0.x), v1 = QX_AT(sml, e0.z), v2 = QX_AT(sml, e1.x),
+                                    v3 = QX_AT(sml, e1.z);
+                        a0 = fmaf(__uint_as_float(e0.y), v0, a0);
+                        a1 = fmaf(__uint_as_float(e0.w), v1, a1);
+                        a2 = fmaf(__uint_as_float(e1.y), v2, a2);
+                        a3 = fmaf(__uint_as_float(e1.w), v3, a3);
+                    }
+                    if (j < n) {
+                        const uint4 e = q[j];
+                        a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
+                        a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
+                    }
+                    if (fl & QX_R_LAST) put_all(&QX_AT(sml, h.x), (a0 + a1) + (a2 + a3), C);
+                    st.rp += 1 + n;
+                    st.left -= 1 + (int)n;
                 }
                 st.finish();
                 break;
             }
             case QX_PH_UNITS: {
+                // pieces [out, n_const, 0, n | flags] + n_const quads [F[b] row, k, cb, 0]
+                // (k relu(F[b] + cb)) + two quads per unit with an a form, [F[a] row, F[b] row,
+                // coef, ca] [cb, ...] (coef (F[a] + ca) relu(F[b] + cb)); ONE is 1 on every
+                // machine (no sublayer writes it), so its constant terms enter as plain constants
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
-                const float x0 = QX_AT(sml, d.one_row);
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
-                while (st.more()) {
-                    const uint4 h = st.next();  // [out, groups, quads, 0]
-                    float acc = 0.0f;
-                    for (uint32_t gi = 0; gi < h.y; gi++) {
-                        const uint4 gq = st.next();  // [a, b, n | has_a << 31, 0]
-                        const uint32_t n = gq.z & 0x7FFFFFFFu;
-                        const float fb = QX_AT(sml, gq.y);
-                        if (!(gq.z >> 31)) {
-                            // constant a: k x0 relu(F[b] + cb x0), two units a quad, read
-                            // straight from the ring (up to four quads per step)
-                            float acc2 = 0.0f;
-                            int nqd = (int)((n + 1) / 2);
-                            while (nqd > 0) {
-                                if (st.left == 0) st.advance();
-                                const int cnt = nqd < st.left ? nqd : st.left;
-                                const uint4 *rp = st.rp;
-                                int j = 0;
-                                for (; j + 2 <= cnt; j += 2) {
-                                    const uint4 q0 = rp[j], q1 = rp[j + 1];
-                                    acc += __fmul_rn(__fmul_rn(__uint_as_float(q0.x), x0), relu(fmaf(__uint_as_float(q0.y), x0, fb)));
-                                    acc2 += __fmul_rn(__fmul_rn(__uint_as_float(q0.z), x0), relu(fmaf(__uint_as_float(q0.w), x0, fb)));
-                                    acc += __fmul_rn(__fmul_rn(__uint_as_float(q1.x), x0), relu(fmaf(__uint_as_float(q1.y), x0, fb)));
-                                    acc2 += __fmul_rn(__fmul_rn(__uint_as_float(q1.z), x0), relu(fmaf(__uint_as_float(q1.w), x0, fb)));
-                                }
-                                if (j < cnt) {
-                                    const uint4 q0 = rp[j];
-                                    acc += __fmul_rn(__fmul_rn(__uint_as_float(q0.x), x0), relu(fmaf(__uint_as_float(q0.y), x0, fb)));
-                                    acc2 += __fmul_rn(__fmul_rn(__uint_as_float(q0.z), x0), relu(fmaf(__uint_as_float(q0.w), x0, fb)));
-                                }
-                                st.rp += cnt;
-                                st.left -= cnt;
-                                nqd -= cnt;
-                            }
-                            acc += acc2;
-                        } else {
-                            const float fa = QX_AT(sml, gq.x);
-                            for (uint32_t u = 0; u < n; u++) {
-                                const uint4 q = st.next();
-                                const float av = fmaf(__uint_as_float(q.y), x0, fa);
-                                const float bv = fmaf(__uint_as_float(q.z), x0, fb);
-                                acc += __fmul_rn(__fmul_rn(__uint_as_float(q.x), av), relu(bv));
-                            }
-                        }
+                float acc0 = 0.0f, acc1 = 0.0f;
+                while (true) {
+                    if (st.left == 0) {
+                        if (!st.more()) break;
+                        st.advance();
                     }
-                    if (h.w & 1)
-                        put_all(&QX_AT(sml, h.x), QX_AT(sml, h.x) + acc, C);  // the row's only record
-                    else
-                        add_all(&QX_AT(sml, h.x), acc, C);  // records into one row meet
+                    const uint4 h = st.rp[0];
+                    const uint32_t n = h.w & 0xFFFFFFu, fl = h.w >> 24;
+                    if (fl & QX_R_SKIP) {
+                        st.left = 0;
+                        continue;
+                    }
+                    const uint4 *q = st.rp + 1;
+                    if (fl & QX_R_FIRST) acc0 = acc1 = 0.0f;
+                    const uint32_t nc = h.y;
+                    uint32_t j = 0;
+                    for (; j + 2 <= nc; j += 2) {
+                        const uint4 u0 = q[j], u1 = q[j + 1];
+                        const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x);
+                        acc0 = fmaf(__uint_as_float(u0.y), relu(f0 + __uint_as_float(u0.z)), acc0);
+                        acc1 = fmaf(__uint_as_float(u1.y), relu(f1 + __uint_as_float(u1.z)), acc1);
+                    }
+                    if (j < nc) {
+                        const uint4 u0 = q[j];
+                        acc0 = fmaf(__uint_as_float(u0.y), relu(QX_AT(sml, u0.x) + __uint_as_float(u0.z)), acc0);
+                        j++;
+                    }
+                    for (; j < n; j += 2) {
+                        const uint4 u = q[j], u2 = q[j + 1];
+                        const float av = QX_AT(sml, u.x) + __uint_as_float(u.w);
+                        const float bv = QX_AT(sml, u.y) + __uint_as_float(u2.x);
+                        acc1 += __fmul_rn(__fmul_rn(__uint_as_float(u.z), av), relu(bv));
+                    }
+                    if (fl & QX_R_LAST) {
+                        const float tot = acc0 + acc1;
+                        if (fl & QX_R_STORE)
+                            put_all(&QX_AT(sml, h.x), QX_AT(sml, h.x) + tot, C);  // the row's only record
+                        else
+                            add_all(&QX_AT(sml, h.x), tot, C);  // records into one row meet
+                    }
+                    st.rp += 1 + n;
+                    st.left -= 1 + (int)n;
                 }
                 st.finish();
                 break;
             }
             case QX_PH_KSEL: {
-                // per key head, lanes walk machines: the key's first maximal channel (a write
-                // when it is positive) and the query's top-qhot positive channels
+                // per key head, lanes walk machines: pieces [slot | qhot << 16, common row,
+                // lag-ONE row, n | flags] + n channels [row, c0, c1, has common]: the key's first
+                // maximal channel (a write when positive), then (R_QUERY) the query's top-qhot
+                // positive channels
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
-                const float x0 = QX_AT(sml, d.one_row);
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
-                while (st.more()) {
-                    const uint4 h = st.next();   // [slot | qhot << 16, k common, q common, nk | nq << 16]
-                    const uint4 h2 = st.next();  // [k lag-ONE row, q lag-ONE row, 0, 0]
+                float bk = 0.0f, qb[QH];
+                int ik = -1, npos = 0, qi[QH], base = 0;
+                while (true) {
+                    if (st.left == 0) {
+                        if (!st.more()) break;
+                        st.advance();
+                    }
+                    const uint4 h = st.rp[0];
+                    const uint32_t n = h.w & 0xFFFFFFu, fl = h.w >> 24;
+                    if (fl & QX_R_SKIP) {
+                        st.left = 0;
+                        continue;
+                    }
+                    const uint4 *q = st.rp + 1;
+                    const float com = QX_AT(sml, h.y), x1 = QX_AT(sml, h.z);
                     const uint32_t slot = h.x & 0xFFFFu, qhot = h.x >> 16;
-                    const uint32_t nk = h.w & 0xFFFFu, nq = h.w >> 16;
-                    int ik = -1, npos = 0;
-                    {
-                        const float com = QX_AT(sml, h.y), x1 = QX_AT(sml, h2.x);
-                        float bk = 0.0f;
-                        uint32_t i = 0;
-                        while (i < nk) {
-                            if (st.left == 0) st.advance();
-                            const int cnt = (int)(nk - i) < st.left ? (int)(nk - i) : st.left;
-                            const uint4 *rp = st.rp;
-                            int j = 0;
-                            for (; j + 4 <= cnt; j += 4) {
-                                float v[4];
+                    if (fl & QX_R_FIRST) {
+                        bk = 0.0f;
+                        ik = -1;
+                        npos = 0;
+                        base = 0;
 #pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    const uint4 c = rp[j + u];
-                                    v[u] = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
-                                                QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
-                                }
-#pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    npos += v[u] > 0.0f;
-                                    if (v[u] > bk) { bk = v[u]; ik = (int)(i + j + u); }
-                                }
-                            }
-                            for (; j < cnt; j++) {
-                                const uint4 c = rp[j];
-                                const float v = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
-                                                     QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
-                                npos += v > 0.0f;
-                                if (v > bk) { bk = v; ik = (int)(i + j); }
-                            }
-                            st.rp += cnt;
-                            st.left -= cnt;
-                            i += cnt;
+                        for (int k = 0; k < QH; k++) {
+                            qb[k] = 0.0f;
+                            qi[k] = -1;
                         }
                     }
-                    put_all(&ksel[slot * 32 + lane], ik, C);
-                    if (npos > 1 && act) atomicOr(&d.err[m], QX_E_KEY);
-                    float qb0 = 0.f, qb1 = 0.f, qb2 = 0.f, qb3 = 0.f;
-                    int qi0 = -1, qi1 = -1, qi2 = -1, qi3 = -1, qpos = 0;
-                    {
-                        const float com = QX_AT(sml, h.z), x1 = QX_AT(sml, h2.y);
-                        uint32_t i = 0;
-                        while (i < nq) {
-                            if (st.left == 0) st.advance();
-                            const int cnt = (int)(nq - i) < st.left ? (int)(nq - i) : st.left;
-                            const uint4 *rp = st.rp;
-                            for (int j = 0; j < cnt; j += 4) {
-                                float vv[4];
+                    if (!(fl & QX_R_QUERY)) {
+                        for (uint32_t j = 0; j < n; j++) {
+                            const uint4 c = q[j];
+                            const float v = relu(fmaf(__uint_as_float(c.z), x1,
+                                                      __uint_as_float(c.y) + fmaf(__uint_as_float(c.w), com, QX_AT(sml, c.x))));
+                            npos += v > 0.0f;
+                            if (v > bk) {
+                                bk = v;
+                                ik = base + (int)j;
+                            }
+                        }
+                    } else {
+                        for (uint32_t j = 0; j < n; j++) {
+                            const uint4 c = q[j];
+                            float v = relu(fmaf(__uint_as_float(c.z), x1,
+                                                __uint_as_float(c.y) + fmaf(__uint_as_float(c.w), com, QX_AT(sml, c.x))));
+                            int vi = base + (int)j;
+                            npos += v > 0.0f;
+                            // insertion into the descending top list: a value displaces only a
+                            // strictly smaller one, so ties keep the lower channel first
 #pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    const uint4 c = j + u < cnt ? rp[j + u] : make_uint4(d.zero_row, 0u, 0u, 0u);
-                                    vv[u] = relu(fmaf(__uint_as_float(c.z), x1, fmaf(__uint_as_float(c.y), x0,
-                                                 QX_AT(sml, c.x & 0x7FFFFFFFu) + ((c.x >> 31) ? com : 0.0f))));
-                                }
-#pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    float v = vv[u];
-                                    int vi = (int)(i + j + u);
-                                    qpos += v > 0.0f;
-                                    // insertion into the descending top list: a value displaces only
-                                    // a strictly smaller one, so ties keep the lower channel first
-                                    if (v > qb0) { float tv = qb0; int ti = qi0; qb0 = v; qi0 = vi; v = tv; vi = ti; }
-                                    if (qhot > 1 && v > qb1) { float tv = qb1; int ti = qi1; qb1 = v; qi1 = vi; v = tv; vi = ti; }
-                                    if (qhot > 2 && v > qb2) { float tv = qb2; int ti = qi2; qb2 = v; qi2 = vi; v = tv; vi = ti; }
-                                    if (qhot > 3 && v > qb3) { qb3 = v; qi3 = vi; }
+                            for (int k = 0; k < QH; k++) {
+                                if (k < (int)qhot && v > qb[k]) {
+                                    const float tv = qb[k];
+                                    const int ti = qi[k];
+                                    qb[k] = v;
+                                    qi[k] = vi;
+                                    v = tv;
+                                    vi = ti;
                                 }
                             }
-                            st.rp += cnt;
-                            st.left -= cnt;
-                            i += cnt;
                         }
                     }
-                    const int qs[4] = {qi0, qi1, qi2, qi3};
+                    base += (int)n;
+                    if (fl & QX_R_LAST) {
+                        if (!(fl & QX_R_QUERY)) {
+                            put_all(&ksel[slot * 32 + lane], ik, C);
+                            if (npos > 1 && act) atomicOr(&d.err[m], QX_E_KEY);
+                        } else {
 #pragma unroll
-                    for (int j = 0; j < 4; j++)
-                        if (j < d.qhot_max) put_all(&qsel[(slot * d.qhot_max + j) * 32 + lane], j < (int)qhot ? qs[j] : -1, C);
-                    if (qpos > (int)qhot && act) atomicOr(&d.err[m], QX_E_QUERY);
+                            for (int k = 0; k < 4; k++)
+                                if (k < d.qhot_max)
+                                    put_all(&qsel[(slot * d.qhot_max + k) * 32 + lane], k < QH ? qi[k < QH ? k : 0] : -1, C);
+                            if (npos > (int)qhot && act) atomicOr(&d.err[m], QX_E_QUERY);
+                        }
+                    }
+                    st.rp += 1 + n;
+                    st.left -= 1 + (int)n;
                 }
                 st.finish();
                 break;

@@ -69,6 +69,12 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
 // 8-byte (value head, machine) records live in the stream rings, after the phase's output delta
 // rows when the group runs on a cluster
 #define QX_VH_CHUNK 64
+// stream piece flags (header quad .w >> 24)
+#define QX_R_FIRST 1u
+#define QX_R_LAST 2u
+#define QX_R_STORE 4u
+#define QX_R_QUERY 8u
+#define QX_R_SKIP 0x80u
 #define QX_RING_BYTES (QX_NW * 2 * QX_RING_QUADS * 16)
 __host__ __device__ inline size_t qx_vh_worklist_offset(uint32_t delta_rows) {
     return ((size_t)delta_rows * QX_RP * 4 + 15) / 16 * 16;

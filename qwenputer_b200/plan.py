@@ -57,12 +57,17 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 9
+VERSION = 10
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
           DECODE=10, END=11, VHRUN=12, VHSUM=13)
 NOSYNC = 0x100  # phase kind flag: no barrier after the phase
+# stream pieces: a header quad [x, y, z, n | flags << 24] and n <= PIECE_MAX - 1 body quads, never
+# crossing a ring chunk of RING_QUADS quads (counted from the warp's range start); a record longer
+# than a piece continues in the next pieces of the same warp
+PIECE_MAX = 16
+R_FIRST, R_LAST, R_STORE, R_QUERY, R_SKIP = 1, 2, 4, 8, 0x80
 # value heads a VH phase lists: its worklist of (value head, machine) records, 8 bytes each,
 # lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps); with a
 # cluster the rings also hold the CTA's output deltas (one row per output row of the phase)
@@ -158,6 +163,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     machines runs on a cluster of ``cluster`` CTAs, so stream records are balanced over
     nw * cluster warps."""
     assert 1 <= cluster <= 8, cluster
+    # the kernel takes the ONE dim as 1 on every machine: no sublayer may write it
+    assert ONE not in set(int(d) for d in g.ffn_out) and ONE not in set(int(d) for d in g.out_dim)
     ring_bytes = nw * 2 * RING_QUADS * 16
     qhot = int(g.head_qhot.max())
     assert qhot <= 4, "queries may read at most 4 rows"
@@ -310,14 +317,38 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
             stats["balanced_sum"] += tot / nwv
         return per
 
-    def stream_phase(kind: int, records: list[list[tuple]], costs: list[float], prog, a=0, b=0):
-        """Emit per-warp quad ranges of the records (each a list of quads) as one phase."""
+    def pieces(x: int, y: int, z: int, body: list[tuple], flags: int = 0, step: int = 1) -> list[list[tuple]]:
+        """A record as pieces of at most PIECE_MAX quads (header + body); `step`: body quads
+        that must stay together.  The first piece carries R_FIRST, the last R_LAST."""
+        out, i = [], 0
+        cap = (PIECE_MAX - 1) // step * step
+        npc = max(1, -(-len(body) // cap))
+        cap = -(-len(body) // npc // step) * step or cap  # even pieces
+        while True:
+            part = body[i:i + cap]
+            fl = flags | (R_FIRST if i == 0 else 0) | (R_LAST if i + cap >= len(body) else 0)
+            out.append([(x, y, z, len(part) | fl << 24)] + part)
+            i += cap
+            if i >= len(body):
+                return out
+
+    def stream_phase(kind: int, records: list[list[list[tuple]]], costs: list[float], prog, a=0, b=0):
+        """Emit per-warp quad ranges of the records (each a list of pieces) as one phase: a piece
+        that would cross a ring chunk is moved to the next chunk behind an R_SKIP header."""
         per = balance(costs)
         wp = len(warp_ptr_l)
         warp_ptr_l.append(len(stream))
         for w in range(nwv):
+            start = len(stream)
             for i in per[w]:
-                stream.extend(records[i])
+                for pc in records[i]:
+                    assert len(pc) <= PIECE_MAX
+                    room = RING_QUADS - (len(stream) - start) % RING_QUADS
+                    if len(pc) > room:
+                        stream.append((0, 0, 0, R_SKIP << 24))
+                        stream.extend([(0, 0, 0, 0)] * (room - 1))
+                        stats["pad_quads"] += room
+                    stream.extend(pc)
             warp_ptr_l.append(len(stream))
         prog.append((kind, a, b, wp))
 
@@ -325,8 +356,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         recs, costs = [], []
         for terms, dst in zip(form_list, dst_rows):
             qs = entry_quads(terms, rowmap)
-            recs.append([(W(dst), len(qs), 0, 0)] + qs)
-            costs.append(9 * len(qs) + 14)
+            recs.append(pieces(W(dst), 0, 0, qs))
+            costs.append(5 * len(qs) + 12 * len(recs[-1]))
             stats["form_nnz"] += len(terms)
         stream_phase(PH["FORMS"], recs, costs, prog)
 
@@ -386,57 +417,49 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 flist = list(gforms)
                 forms_phase(flist, [free[i] for i in range(len(flist))], lambda t: slot[t[1]], body)
                 frow = {f: W(free[i]) for f, i in gforms.items()}
-                recs, costs, outs = [], [], []
+                # units as flat quads (ONE is 1 for every machine: no sublayer writes it):
+                #   constant a:  [F[b] row, k, cb, 0]          k = coef * ca rounded as the
+                #                                               reference rounds coef * a
+                #   a form a:    [F[a] row, F[b] row, coef, ca], [cb, 0, 0, 0]
+                # a node's units go out as records of at most UNIT_CHUNK units (warps balance them)
+                parts = []  # (out row, const quads, has-a quad pairs)
                 for n in gnodes:
-                    # units grouped by their (a, b) forms; a constant-a unit is (k, cb) with
-                    # k = coef * ca rounded as the reference rounds coef * a when a = ca * 1
-                    grp: dict = {}
+                    out = W(xrow(lv, int(g.ffn_out[n])))
+                    cq, hq = [], []
                     for u in range(int(g.ffn_uptr[n]), int(g.ffn_uptr[n + 1])):
                         (ta, ca), (tb, cb) = unit_a[u], unit_b[u]
-                        grp.setdefault((ta, tb), []).append((float(g.unit_coef[u]), ca, cb))
-                    out = W(xrow(lv, int(g.ffn_out[n])))
-                    chunks, cur_q, cur_g, cur_u = [], [], 0, 0
-
-                    def flush():
-                        nonlocal cur_q, cur_g, cur_u
-                        if cur_g:
-                            chunks.append(([(out, cur_g, len(cur_q), 0)] + cur_q, cur_u, cur_g))
-                        cur_q, cur_g, cur_u = [], 0, 0
-
-                    for (ta, tb), us in grp.items():
-                        ra = frow[ta] if ta else ZW
                         rb = frow[tb] if tb else ZW
-                        for c0 in range(0, len(us), UNIT_CHUNK):
-                            part = us[c0:c0 + UNIT_CHUNK]
-                            if cur_u + len(part) > UNIT_CHUNK:
-                                flush()
-                            if ta:
-                                qs = [(ra, rb, len(part) | 1 << 31, 0)]
-                                qs += [(_fbits(cf), _fbits(ca), _fbits(cb), 0) for cf, ca, cb in part]
-                            else:
-                                ks = [(_fbits(np.float32(cf) * np.float32(ca)), _fbits(cb)) for cf, ca, cb in part]
-                                qs = [(ra, rb, len(part), 0)]
-                                if len(ks) % 2:
-                                    ks.append((0, 0))  # k = 0: adds +0
-                                qs += [(ks[i][0], ks[i][1], ks[i + 1][0], ks[i + 1][1])
-                                       for i in range(0, len(ks), 2)]
-                            cur_q += qs
-                            cur_g += 1
-                            cur_u += len(part)
-                    flush()
-                    for rec, nu, ng in chunks:
-                        recs.append(rec)
-                        costs.append(6 * nu + 10 * ng + 14)
-                        outs.append(out)
+                        cf = float(g.unit_coef[u])
+                        if ta:
+                            hq.append(((frow[ta], rb, _fbits(cf), _fbits(ca)), (_fbits(cb), 0, 0, 0)))
+                        else:
+                            cq.append((rb, _fbits(np.float32(cf) * np.float32(ca)), _fbits(cb), 0))
+                    units_all = [("c", q) for q in cq] + [("h", q) for q in hq]
+                    for c0 in range(0, max(len(units_all), 1), UNIT_CHUNK):
+                        chunk = units_all[c0:c0 + UNIT_CHUNK]
+                        parts.append((out, [q for k, q in chunk if k == "c"], [q for k, q in chunk if k == "h"]))
                     stats["units"] += int(g.ffn_uptr[n + 1] - g.ffn_uptr[n])
-                    stats["unit_groups"] += len(grp)
+                    stats["unit_groups"] += 0
                 # a row that only one record of the phase adds into is updated with a plain
-                # read-add-store (header flag 1); rows several records meet in take atomic adds
-                nrec = collections.Counter(outs)
-                for rec, out in zip(recs, outs):
-                    if nrec[out] == 1:
-                        h0 = rec[0]
-                        rec[0] = (h0[0], h0[1], h0[2], 1)
+                # read-add-store (R_STORE); rows several records meet take atomic adds
+                nrec = collections.Counter(out for out, _, _ in parts)
+                recs, costs = [], []
+                for out, cq, hq in parts:
+                    body_q = cq + [q for pair in hq for q in pair]
+                    store = R_STORE if nrec[out] == 1 else 0
+                    pcs, i = [], 0
+                    while True:
+                        e = min(i + PIECE_MAX - 1, len(body_q))
+                        if e > len(cq) and (e - len(cq)) % 2:
+                            e -= 1  # a unit's two quads stay in one piece
+                        nc = max(0, min(e, len(cq)) - i)
+                        fl = store | (R_FIRST if i == 0 else 0) | (R_LAST if e >= len(body_q) else 0)
+                        pcs.append([(out, nc, 0, (e - i) | fl << 24)] + body_q[i:e])
+                        i = e
+                        if i >= len(body_q):
+                            break
+                    recs.append(pcs)
+                    costs.append(4 * len(cq) + 9 * len(hq) + 12 * len(pcs))
                 stream_phase(PH["UNITS"], recs, costs, body)
             group_stats.append((lv, "ffn", len(groups)))
         else:
@@ -535,29 +558,31 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 frow = {f: W(ffree[i]) for f, i in gforms.items()}
                 if flist:
                     forms_phase(flist, [ffree[i] for i in range(len(flist))], rowmap, body)
+                # a key head: key pieces [slot | qhot << 16, common row, lag-ONE row, n | flags]
+                # then query pieces (R_QUERY), channel quads [row, c0, c1, 1.0 if the common
+                # form applies else 0]
                 recs, costs = [], []
+                one_f = _fbits(1.0)
                 for sl, h in enumerate(gheads):
-                    quads, com_rows, one_rows, masks = {}, {}, {}, {}
-                    for nm in ("k", "q"):
+                    rec = []
+                    nkq = 0
+                    for nm, qf_flag in (("k", 0), ("q", R_QUERY)):
                         com, lag, res = hf[h][nm]
-                        com_rows[nm] = frow[com] if com else ZW
-                        one_rows[nm] = W(stage_row[(lag, ONE)]) if lag else ZW
+                        com_row = frow[com] if com else ZW
+                        one_row = W(stage_row[(lag, ONE)]) if lag else ZW
                         chans = []
-                        for c in range(HD):
-                            if c in res:
-                                t, c0, c1 = res[c]
-                                chans.append(((frow[t] if t else ZW) | (1 << 31 if com else 0),
-                                              _fbits(c0), _fbits(c1), 0))
-                            else:
-                                chans.append((ZW, 0, 0, 0))
-                        quads[nm] = chans if res else []
-                    nk, nq = len(quads["k"]), len(quads["q"])
-                    rec = [(sl | int(g.head_qhot[h]) << 16, com_rows["k"], com_rows["q"], nk | nq << 16),
-                           (one_rows["k"], one_rows["q"], 0, 0)]
-                    rec += quads["k"] + quads["q"]
+                        if res:
+                            for c in range(HD):
+                                if c in res:
+                                    t, c0, c1 = res[c]
+                                    chans.append((frow[t] if t else ZW, _fbits(c0), _fbits(c1), one_f if com else 0))
+                                else:
+                                    chans.append((ZW, 0, 0, 0))
+                        nkq += len(chans)
+                        rec += pieces(sl | int(g.head_qhot[h]) << 16, com_row, one_row, chans, qf_flag)
                     recs.append(rec)
-                    costs.append(14 * (nk + nq) + 40)
-                    stats["kq_channels"] += nk + nq
+                    costs.append(15 * nkq + 12 * len(rec))
+                    stats["kq_channels"] += nkq
                 stream_phase(PH["KSEL"], recs, costs, body)
                 v0 = len(vheads_l)
                 for sl, h in enumerate(gheads):

@@ -54,19 +54,29 @@ class PlanInterp:
         self.delta = _ByteIndexed(self.Dw)
 
     def warp_records(self, c, k):
-        """Per warp, the (header, body quads) records of a stream phase."""
+        """Per warp, its records of a stream phase: lists of (header, body quads) pieces, the
+        R_SKIP padding dropped (a record's pieces are consecutive and end with R_LAST)."""
+        from qwenputer_b200.plan import R_LAST, R_SKIP
+
         st = self.s["STREAM"].astype(np.int64)
         wp = self.s["WARP_PTR"].astype(np.int64)
         nw = self.P.hdr["nw"] * self.P.hdr["cluster"]  # the warps of a group's cluster
         out = []
         for w in range(nw):
-            i, end = wp[c + w], wp[c + w + 1]
-            recs = []
+            i, end, start = wp[c + w], wp[c + w + 1], wp[c + w]
+            recs, cur = [], []
             while i < end:
                 h = st[i]
-                n = h[1] if k == PH["FORMS"] else (h[2] if k == PH["UNITS"] else 1 + (h[3] & 0xFFFF) + (h[3] >> 16))
-                recs.append((h, st[i + 1:i + 1 + n]))
+                n, fl = int(h[3]) & 0xFFFFFF, int(h[3]) >> 24
+                if fl & R_SKIP:
+                    i = start + ((i - start) // 32 + 1) * 32
+                    continue
+                cur.append((h, st[i + 1:i + 1 + n]))
                 i += 1 + n
+                if fl & R_LAST and not (k == PH["KSEL"] and not fl & 8):
+                    recs.append(cur)
+                    cur = []
+            assert not cur
             out.append(recs)
         return out
 
@@ -115,55 +125,37 @@ class PlanInterp:
                         H[2, e] = h[1]
             elif k == PH["FORMS"]:
                 for recs in self.warp_records(c, k):
-                    for h, q in recs:
-                        self.X[h[0]] = self.entries(q.reshape(-1))
+                    for pcs in recs:
+                        body = np.concatenate([q for _, q in pcs])
+                        self.X[pcs[0][0][0]] = self.entries(body.reshape(-1))
             elif k == PH["UNITS"]:
-                x0 = self.X[self.one]
                 f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
-                    for h, q in recs:
+                    for pcs in recs:
                         acc = np.zeros(self.B, np.float32)
-                        i = 0
-                        for _ in range(int(h[1])):
-                            gq = q[i]
-                            i += 1
-                            n, has_a = int(gq[2]) & 0x7FFFFFFF, int(gq[2]) >> 31
-                            fb = self.X[gq[1]]
-                            if not has_a:
-                                ks = []
-                                for _ in range((n + 1) // 2):
-                                    ks += [(q[i][0], q[i][1]), (q[i][2], q[i][3])]
-                                    i += 1
-                                for kk, cb in ks[:n]:
-                                    acc = acc + (f32(kk) * x0) * np.maximum(fb + f32(cb) * x0, 0)
-                            else:
-                                fa = self.X[gq[0]]
-                                for _ in range(n):
-                                    coef, ca, cb = (f32(v) for v in q[i][:3])
-                                    i += 1
-                                    acc = acc + (coef * (fa + ca * x0)) * np.maximum(fb + cb * x0, 0)
-                        self.X[h[0]] = self.X[h[0]] + acc
+                        for h, q in pcs:
+                            nc = int(h[1])
+                            for u in q[:nc]:
+                                acc = acc + f32(u[1]) * np.maximum(self.X[u[0]] + f32(u[2]), 0)
+                            for j in range(nc, len(q), 2):
+                                u, u2 = q[j], q[j + 1]
+                                av = self.X[u[0]] + f32(u[3])
+                                acc = acc + (f32(u[2]) * av) * np.maximum(self.X[u[1]] + f32(u2[0]), 0)
+                        out = pcs[0][0][0]
+                        self.X[out] = self.X[out] + acc
             elif k == PH["KSEL"]:
-                x0 = self.X[self.one]
                 f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
-                    for h, q in recs:
-                        h2 = q[0]
-                        slot, qhot = int(h[0]) & 0xFFFF, int(h[0]) >> 16
-                        nk, nq = int(h[3]) & 0xFFFF, int(h[3]) >> 16
-
-                        def chans(quads, com, x1):
-                            if not len(quads):
-                                return np.zeros((128, self.B), np.float32)
-                            vals = []
-                            for qq in quads:
-                                e = int(qq[0])
-                                v = (self.X[e & 0x7FFFFFFF] + (com if e >> 31 else 0)) + f32(qq[1]) * x0 + f32(qq[2]) * x1
-                                vals.append(np.maximum(v, 0))
-                            return np.stack(vals)
-
-                        kv = chans(q[1:1 + nk], self.X[h[1]], self.X[h2[0]])
-                        qv = chans(q[1 + nk:1 + nk + nq], self.X[h[2]], self.X[h2[1]])
+                    for pcs in recs:
+                        slot, qhot = int(pcs[0][0][0]) & 0xFFFF, int(pcs[0][0][0]) >> 16
+                        vals = {0: [], 8: []}
+                        for h, q in pcs:
+                            com, x1 = self.X[h[1]], self.X[h[2]]
+                            for qq in q:
+                                v = f32(qq[2]) * x1 + (f32(qq[1]) + (f32(qq[3]) * com + self.X[qq[0]]))
+                                vals[int(h[3]) >> 24 & 8].append(np.maximum(v, 0))
+                        kv = np.stack(vals[0]) if vals[0] else np.zeros((1, self.B), np.float32)
+                        qv = np.stack(vals[8]) if vals[8] else np.zeros((1, self.B), np.float32)
                         km, ka = kv.max(0), kv.argmax(0)
                         self.ksel[slot] = np.where(km > 0, ka, -1)
                         sel = []

@@ -70,7 +70,10 @@ def test_plan_is_consistent(graph, cluster):
     nw = P.hdr["nw"] * cluster  # the warps of a machine group's cluster
     st = s["STREAM"].astype(np.int64)
     wp = s["WARP_PTR"].astype(np.int64)
-    # walk every stream record of every phase: rows in range, records end on their warp's range
+    # walk every stream piece of every phase: rows in range, pieces inside one ring chunk,
+    # records complete, ranges end on their warp's range
+    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_QUERY, R_SKIP
+
     for ph in s["RUN_PROG"]:
         k = int(ph["kind"]) & 0xFF
         if k not in (PH["FORMS"], PH["UNITS"], PH["KSEL"]):
@@ -78,32 +81,32 @@ def test_plan_is_consistent(graph, cluster):
         seg = wp[ph["c"]:ph["c"] + nw + 1]
         assert np.all(np.diff(seg) >= 0)
         for w in range(nw):
-            i, end = seg[w], seg[w + 1]
+            i, end, start = seg[w], seg[w + 1], seg[w]
+            open_rec = False
             while i < end:
                 h = st[i]
+                n, fl = int(h[3]) & 0xFFFFFF, int(h[3]) >> 24
+                if fl & R_SKIP:
+                    i = start + ((i - start) // RING_QUADS + 1) * RING_QUADS
+                    continue
+                assert 1 + n <= PIECE_MAX
+                assert (i - start) // RING_QUADS == (i + n - start) // RING_QUADS, "piece crosses a chunk"
+                assert bool(fl & R_FIRST) != open_rec or (k == PH["KSEL"] and fl & R_QUERY and fl & R_FIRST)
+                body = st[i + 1:i + 1 + n]
                 if k == PH["FORMS"]:
                     assert h[0] < rows and h[0] % 132 == 0
-                    ent = st[i + 1:i + 1 + h[1]]
-                    assert np.all(ent[:, 0] < rows) and np.all(ent[:, 2] < rows)
-                    i += 1 + h[1]
+                    assert np.all(body[:, 0] < rows) and np.all(body[:, 2] < rows)
                 elif k == PH["UNITS"]:
-                    assert h[0] < rows
-                    j, n_g = i + 1, 0
-                    while j < i + 1 + h[2]:
-                        gq = st[j]
-                        assert gq[0] < rows and gq[1] < rows
-                        n, has_a = gq[2] & 0x7FFFFFFF, gq[2] >> 31
-                        j += 1 + (n if has_a else (n + 1) // 2)
-                        n_g += 1
-                    assert j == i + 1 + h[2] and n_g == h[1]
-                    i += 1 + h[2]
+                    nc = int(h[1])
+                    assert h[0] < rows and nc <= n and (n - nc) % 2 == 0
+                    assert np.all(body[:nc, 0] < rows)
+                    assert np.all(body[nc::2, 0] < rows) and np.all(body[nc::2, 1] < rows)
                 else:
-                    nk, nq = h[3] & 0xFFFF, h[3] >> 16
-                    assert nk in (0, 128) and nq in (0, 128) and (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"]
-                    assert h[1] < rows and h[2] < rows and st[i + 1][0] < rows and st[i + 1][1] < rows
-                    c = st[i + 2:i + 2 + nk + nq]
-                    assert np.all((c[:, 0] & 0x7FFFFFFF) < rows)
-                    i += 2 + nk + nq
+                    assert (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"] and h[1] < rows and h[2] < rows
+                    assert np.all(body[:, 0] < rows)
+                open_rec = not (fl & R_LAST)
+                i += 1 + n
+            assert not open_rec
             assert i == end
     kinds = [int(k) & 0xFF for k in s["RUN_PROG"]["kind"]]
     assert kinds[-2:] == [PH["DECODE"], PH["END"]] and kinds.count(PH["END"]) == 1
