@@ -96,7 +96,11 @@ typedef struct {        /* value head task */
     uint16_t nrows;     /* decaying rows (0: the head never decays) */
     uint32_t a_row, b_row;  /* byte offsets of the decay selector and write gate forms */
     float ca, cb, bconst;
+    uint32_t nout;      /* distinct output rows when at most 4 (OUT_ROW then holds indices into
+                           out4), else QX_OUT_DIRECT (OUT_ROW holds the rows) */
+    uint32_t out4[4];   /* the output rows (byte offsets) */
 } qx_vhead;
+#define QX_OUT_DIRECT 0xFFu
 
 typedef struct {        /* a value head column's v or z: relu(F[row] + c x0) (F from the FORMS phase) */
     uint32_t row;       /* shared-memory byte offset of the form's row (the zero row if none) */
@@ -156,7 +160,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 10
+#define QX_PLAN_VERSION 11
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

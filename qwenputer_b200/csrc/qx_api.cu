@@ -64,11 +64,22 @@ struct qx_executor {
     int32_t state_cap = 0;
     uint32_t *err_host = nullptr;
     std::vector<void *> allocs;
+    // machine-image upload staging (qx_load_machines), two of each so that packing the next
+    // chunk on the host overlaps the copy and the loader kernels of the previous one
+    void *pin[2] = {nullptr, nullptr};
+    void *dstage[2] = {nullptr, nullptr};
+    size_t stage_bytes = 0;
+    cudaEvent_t staged[2] = {nullptr, nullptr};
     ~qx_executor() {
         for (void *p : allocs) cudaFree(p);
         if (dplan) cudaFree(dplan);
         if (err_host) cudaFreeHost(err_host);
         if (dstate) cudaFree(dstate);
+        for (int i = 0; i < 2; i++) {
+            if (pin[i]) cudaFreeHost(pin[i]);
+            if (dstage[i]) cudaFree(dstage[i]);
+            if (staged[i]) cudaEventDestroy(staged[i]);
+        }
     }
 };
 
@@ -375,38 +386,68 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
     if (!ex || !images || row0 < 0 || n < 0 || row0 + n > ex->B)
         return fail(QX_ERR_INVALID_ARG, "qx_load_machines: rows");
     if (n == 0) return QX_OK;
+    for (int i = 0; i < n; i++) {
+        const qx_machine &m = images[i];
+        if (m.rom_words > 65536 || m.drom_bytes > 131072 || (!m.rom && m.rom_words) || !m.ram)
+            return fail(QX_ERR_INVALID_ARG, "qx_load_machines: image %d", i);
+    }
     CU(cudaSetDevice(ex->device));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int chunk = 256;
+    // chunks of machines: [QxImage x cn][word pool], packed into pinned memory, one copy each
+    const int chunk = 512;
+    auto pool_words = [&](const qx_machine &m) {
+        return (size_t)m.rom_words + (m.drom_bytes + 3) / 4 + 8192 + (m.bn ? 256 : 0);
+    };
+    size_t need = 0;
     for (int c0 = 0; c0 < n; c0 += chunk) {
         const int cn = n - c0 < chunk ? n - c0 : chunk;
-        std::vector<QxImage> img(cn);
-        std::vector<uint32_t> pool;
+        size_t b = (size_t)cn * sizeof(QxImage);
+        for (int i = 0; i < cn; i++) b += 4 * pool_words(images[c0 + i]);
+        need = b > need ? b : need;
+    }
+    if (need > ex->stage_bytes) {
+        for (int i = 0; i < 2; i++) {
+            if (ex->staged[i]) CU(cudaEventSynchronize(ex->staged[i]));
+            if (ex->pin[i]) cudaFreeHost(ex->pin[i]);
+            if (ex->dstage[i]) cudaFree(ex->dstage[i]);
+            ex->pin[i] = ex->dstage[i] = nullptr;
+        }
+        ex->stage_bytes = 0;
+        for (int i = 0; i < 2; i++) {
+            if (cudaHostAlloc(&ex->pin[i], need, cudaHostAllocDefault) != cudaSuccess ||
+                cudaMalloc(&ex->dstage[i], need) != cudaSuccess)
+                return fail(QX_ERR_OOM, "qx_load_machines: %zu B of staging", need);
+            if (!ex->staged[i]) CU(cudaEventCreateWithFlags(&ex->staged[i], cudaEventDisableTiming));
+        }
+        ex->stage_bytes = need;
+    }
+    for (int c0 = 0, k = 0; c0 < n; c0 += chunk, k ^= 1) {
+        const int cn = n - c0 < chunk ? n - c0 : chunk;
+        CU(cudaEventSynchronize(ex->staged[k]));  // the copy that last used this buffer is done
+        QxImage *img = static_cast<QxImage *>(ex->pin[k]);
+        uint32_t *pool = reinterpret_cast<uint32_t *>(img + cn);
+        uint32_t w = 0;
         for (int i = 0; i < cn; i++) {
             const qx_machine &m = images[c0 + i];
-            if (m.rom_words > 65536 || m.drom_bytes > 131072 || (!m.rom && m.rom_words) || !m.ram)
-                return fail(QX_ERR_INVALID_ARG, "qx_load_machines: image %d", c0 + i);
             QxImage &q = img[i];
-            q.rom_off = (uint32_t)pool.size();
+            q.rom_off = w;
             q.rom_len = m.rom_words;
-            pool.insert(pool.end(), m.rom, m.rom + m.rom_words);
-            q.drom_off = (uint32_t)pool.size();
+            if (m.rom_words) memcpy(pool + w, m.rom, (size_t)m.rom_words * 4);
+            w += m.rom_words;
+            q.drom_off = w;
             q.drom_words = (m.drom_bytes + 3) / 4;
-            for (uint32_t w = 0; w < q.drom_words; w++) {
-                uint32_t v = 0;
-                for (int b = 0; b < 4; b++)
-                    if (4 * w + b < m.drom_bytes) v |= (uint32_t)m.drom[4 * w + b] << (8 * b);
-                pool.push_back(v);
+            if (q.drom_words) {
+                pool[w + q.drom_words - 1] = 0;
+                memcpy(pool + w, m.drom, m.drom_bytes);  // little-endian words of the bytes
             }
-            q.ram_off = (uint32_t)pool.size();
-            pool.insert(pool.end(), m.ram, m.ram + 8192);
+            w += q.drom_words;
+            q.ram_off = w;
+            memcpy(pool + w, m.ram, 8192 * 4);
+            w += 8192;
             if (m.bn) {
-                q.bn_off = (uint32_t)pool.size();
-                for (int w = 0; w < 256; w++) {
-                    uint32_t v = 0;
-                    for (int b = 0; b < 4; b++) v |= (uint32_t)m.bn[4 * w + b] << (8 * b);
-                    pool.push_back(v);
-                }
+                q.bn_off = w;
+                memcpy(pool + w, m.bn, 1024);
+                w += 256;
             } else {
                 q.bn_off = 0xFFFFFFFFu;
             }
@@ -415,31 +456,23 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
             q.anchor = m.anchor;
             q.n = m.n;
         }
-        void *dimg = nullptr, *dpool = nullptr;
-        CU(cudaMalloc(&dimg, img.size() * sizeof(QxImage)));
-        cudaError_t e = cudaMalloc(&dpool, pool.size() * 4);
-        if (e != cudaSuccess) {
-            cudaFree(dimg);
-            return fail(QX_ERR_OOM, "image pool: %s", cudaGetErrorString(e));
-        }
-        e = cudaMemcpyAsync(dimg, img.data(), img.size() * sizeof(QxImage), cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(dpool, pool.data(), pool.size() * 4, cudaMemcpyHostToDevice, st);
+        const size_t bytes = (size_t)cn * sizeof(QxImage) + (size_t)w * 4;
+        QxImage *dimg = static_cast<QxImage *>(ex->dstage[k]);
+        uint32_t *dpool = reinterpret_cast<uint32_t *>(dimg + cn);
+        cudaError_t e = cudaMemcpyAsync(dimg, img, bytes, cudaMemcpyHostToDevice, st);
         for (int i = 0; i < ex->n_hl && e == cudaSuccess; i++) {
             size_t per = (size_t)ex->d.V[i] * QX_HD * QX_HD * 4;
             e = cudaMemsetAsync(reinterpret_cast<uint8_t *>(ex->d.S[i]) + per * (row0 + c0), 0, per * cn, st);
         }
         if (e == cudaSuccess) {
-            qx_predecode_kernel<<<dim3(4, cn), 256, 0, st>>>(static_cast<QxImage *>(dimg),
-                                                            static_cast<uint32_t *>(dpool), cn);
-            qx_load_kernel<<<dim3(64, cn), 256, 0, st>>>(ex->d, static_cast<QxImage *>(dimg),
-                                                        static_cast<uint32_t *>(dpool), row0 + c0, cn);
+            qx_predecode_kernel<<<dim3(4, cn), 256, 0, st>>>(dimg, dpool, cn);
+            qx_load_kernel<<<dim3(64, cn), 256, 0, st>>>(ex->d, dimg, dpool, row0 + c0, cn);
             e = cudaGetLastError();
         }
-        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-        cudaFree(dimg);
-        cudaFree(dpool);
+        if (e == cudaSuccess) e = cudaEventRecord(ex->staged[k], st);
         if (e != cudaSuccess) return fail(QX_ERR_CUDA, "qx_load_machines: %s", cudaGetErrorString(e));
     }
+    CU(cudaStreamSynchronize(st));
     return QX_OK;
 }
 

@@ -239,7 +239,8 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             case QX_PH_FORMS: {
-                // pieces [dst, 0, 0, n | flags] + n quads [row, w, row, w]: F = sum w * X[row]
+                // two forms a record: pieces [dst A, dst B, 0, n | flags] + n quads [row, w of A,
+                // row, w of B]: F = sum w * X[row], two independent sums a warp
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream st;
@@ -257,7 +258,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         continue;
                     }
                     const uint4 *q = st.rp + 1;
-                    if (fl & QX_R_FIRST) a0 = a1 = a2 = a3 = 0.0f;
+                    if (fl & QX_R_FIRST) a0 = a1 = a2 = a3 = 0.0f;  // a0, a2: form A; a1, a3: B
                     uint32_t j = 0;
                     for (; j + 2 <= n; j += 2) {
                         const uint4 e0 = q[j], e1 = q[j + 1];
@@ -273,7 +274,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
                         a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
                     }
-                    if (fl & QX_R_LAST) put_all(&QX_AT(sml, h.x), (a0 + a1) + (a2 + a3), C);
+                    if (fl & QX_R_LAST) {
+                        put_all(&QX_AT(sml, h.x), a0 + a2, C);
+                        put_all(&QX_AT(sml, h.y), a1 + a3, C);
+                    }
                     st.rp += 1 + n;
                     st.left -= 1 + (int)n;
                 }
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 if (b0 == b1) break;
                 Stream st;
                 st.start(d.stream, ring, b0, b1, lane);
-                float acc0 = 0.0f, acc1 = 0.0f;
+                float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
                 while (true) {
                     if (st.left == 0) {
                         if (!st.more()) break;
@@ -302,19 +306,21 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         continue;
                     }
                     const uint4 *q = st.rp + 1;
-                    if (fl & QX_R_FIRST) acc0 = acc1 = 0.0f;
+                    if (fl & QX_R_FIRST) acc0 = acc1 = acc2 = acc3 = 0.0f;
                     const uint32_t nc = h.y;
                     uint32_t j = 0;
-                    for (; j + 2 <= nc; j += 2) {
-                        const uint4 u0 = q[j], u1 = q[j + 1];
-                        const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x);
+                    for (; j + 4 <= nc; j += 4) {
+                        const uint4 u0 = q[j], u1 = q[j + 1], u2 = q[j + 2], u3 = q[j + 3];
+                        const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x), f2 = QX_AT(sml, u2.x),
+                                    f3 = QX_AT(sml, u3.x);
                         acc0 = fmaf(__uint_as_float(u0.y), relu(f0 + __uint_as_float(u0.z)), acc0);
                         acc1 = fmaf(__uint_as_float(u1.y), relu(f1 + __uint_as_float(u1.z)), acc1);
+                        acc2 = fmaf(__uint_as_float(u2.y), relu(f2 + __uint_as_float(u2.z)), acc2);
+                        acc3 = fmaf(__uint_as_float(u3.y), relu(f3 + __uint_as_float(u3.z)), acc3);
                     }
-                    if (j < nc) {
+                    for (; j < nc; j++) {
                         const uint4 u0 = q[j];
                         acc0 = fmaf(__uint_as_float(u0.y), relu(QX_AT(sml, u0.x) + __uint_as_float(u0.z)), acc0);
-                        j++;
                     }
                     for (; j < n; j += 2) {
                         const uint4 u = q[j], u2 = q[j + 1];
@@ -323,7 +329,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         acc1 += __fmul_rn(__fmul_rn(__uint_as_float(u.z), av), relu(bv));
                     }
                     if (fl & QX_R_LAST) {
-                        const float tot = acc0 + acc1;
+                        const float tot = (acc0 + acc1) + (acc2 + acc3);
                         if (fl & QX_R_STORE)
                             put_all(&QX_AT(sml, h.x), QX_AT(sml, h.x) + tot, C);  // the row's only record
                         else
@@ -577,12 +583,40 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         ref = __shfl_sync(0xFFFFFFFFu, ref, 0);  // (uniform: the batch's records are)
                         const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
                         const float oc[4] = {o.x, o.y, o.z, o.w};
+                        if (vh.nout != QX_OUT_DIRECT) {
+                            // at most 4 output rows: per-row sums over the warp, one add per row
+                            float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
 #pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            if (orow[k] == QX_NONE32) continue;
-                            const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
-                            const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
-                            atomicAdd(&QX_AT(obase + mmv[b], orow[k]), __fmul_rn(__fmul_rn(out, z), ow[k]));
+                            for (int k = 0; k < 4; k++) {
+                                if (orow[k] == QX_NONE32) continue;
+                                const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
+                                const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
+                                const float val = __fmul_rn(__fmul_rn(out, z), ow[k]);
+                                p0 += orow[k] == 0 ? val : 0.0f;
+                                p1 += orow[k] == 1 ? val : 0.0f;
+                                p2 += orow[k] == 2 ? val : 0.0f;
+                                p3 += orow[k] == 3 ? val : 0.0f;
+                            }
+#pragma unroll
+                            for (int off = 16; off > 0; off >>= 1) {
+                                p0 += __shfl_xor_sync(0xFFFFFFFFu, p0, off);
+                                p1 += __shfl_xor_sync(0xFFFFFFFFu, p1, off);
+                                p2 += __shfl_xor_sync(0xFFFFFFFFu, p2, off);
+                                p3 += __shfl_xor_sync(0xFFFFFFFFu, p3, off);
+                            }
+                            if ((uint32_t)lane < vh.nout) {
+                                const uint32_t r = lane == 0 ? vh.out4[0] : lane == 1 ? vh.out4[1] : lane == 2 ? vh.out4[2] : vh.out4[3];
+                                const float pr = lane == 0 ? p0 : lane == 1 ? p1 : lane == 2 ? p2 : p3;
+                                atomicAdd(&QX_AT(obase + mmv[b], r), pr);
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 4; k++) {
+                                if (orow[k] == QX_NONE32) continue;
+                                const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
+                                const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
+                                atomicAdd(&QX_AT(obase + mmv[b], orow[k]), __fmul_rn(__fmul_rn(out, z), ow[k]));
+                            }
                         }
                     }
                     if (lane == 0) atomicAdd(touched, rows);
@@ -641,10 +675,21 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     } else {
                         const float *bits = d.emb_bits + (size_t)fid * d.n_pay * d.n_feat;
                         for (int f = lane; f < d.n_feat; f += 32) {
-                            float acc = 0.0f;
-                            for (int i = 0; i < d.n_pay; i++)
-                                acc = __fadd_rn(acc, __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
-                            QX_AT(smw, d.feat_row[f]) = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), acc);
+                            // four partial sums (exact values: any order) so the loads of the
+                            // payload bits' rows are in flight together
+                            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                            int i = 0;
+                            for (; i + 4 <= d.n_pay; i += 4) {
+                                float w[4];
+#pragma unroll
+                                for (int u = 0; u < 4; u++) w[u] = __ldg(bits + (size_t)(i + u) * d.n_feat + f);
+#pragma unroll
+                                for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(dec_pay[(i + u) * 32 + mm], w[u]));
+                            }
+                            for (; i < d.n_pay; i++)
+                                acc[0] = __fadd_rn(acc[0], __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
+                            const float tot = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+                            QX_AT(smw, d.feat_row[f]) = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), tot);
                         }
                     }
                 }

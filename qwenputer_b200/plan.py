@@ -57,7 +57,7 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 10
+VERSION = 11
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -89,7 +89,7 @@ DT = {
                        ("s1", "<u4"), ("s2", "<u4")]),
     "vhead": np.dtype([("hl", "<u4"), ("vh", "<u4"), ("col", "<u4"), ("slot", "<u2"),
                        ("nrows", "<u2"), ("a_row", "<u4"), ("b_row", "<u4"), ("ca", "<f4"),
-                       ("cb", "<f4"), ("bconst", "<f4")]),
+                       ("cb", "<f4"), ("bconst", "<f4"), ("nout", "<u4"), ("out4", "<u4", (4,))]),
     "colform": np.dtype([("row", "<u4"), ("pad", "<u2"), ("live", "<u2"), ("c", "<f4")]),
 }
 HEADER = struct.Struct("<QII" + "I" * 16 + "32Q32Q")
@@ -353,12 +353,23 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         prog.append((kind, a, b, wp))
 
     def forms_phase(form_list: list[tuple], dst_rows: list[int], rowmap, prog):
+        """Forms in pairs of similar length: pieces [dst A, dst B, 0, n | flags] + n quads
+        [row, w of A, row, w of B] (the shorter padded with the zero row times +0), so a warp
+        runs two independent sums; an odd last form pairs with an empty one into the zero row."""
         recs, costs = [], []
-        for terms, dst in zip(form_list, dst_rows):
-            qs = entry_quads(terms, rowmap)
-            recs.append(pieces(W(dst), 0, 0, qs))
-            costs.append(5 * len(qs) + 12 * len(recs[-1]))
-            stats["form_nnz"] += len(terms)
+        items = sorted(zip(form_list, dst_rows), key=lambda fd: -len(fd[0]))
+        for i in range(0, len(items), 2):
+            ta, da = items[i]
+            tb, db = items[i + 1] if i + 1 < len(items) else ((), None)
+            ea = [(W(rowmap(t)), _fbits(w)) for t, w in ta]
+            eb = [(W(rowmap(t)), _fbits(w)) for t, w in tb]
+            n = max(len(ea), len(eb))
+            ea += [(ZW, 0)] * (n - len(ea))
+            eb += [(ZW, 0)] * (n - len(eb))
+            body = [(ea[j][0], ea[j][1], eb[j][0], eb[j][1]) for j in range(n)]
+            recs.append(pieces(W(da), W(db) if db is not None else ZW, 0, body))
+            costs.append(4 * n + 14 * len(recs[-1]))
+            stats["form_nnz"] += len(ta) + len(tb)
         stream_phase(PH["FORMS"], recs, costs, prog)
 
     def xrow(lv, d):
@@ -558,14 +569,12 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 frow = {f: W(ffree[i]) for f, i in gforms.items()}
                 if flist:
                     forms_phase(flist, [ffree[i] for i in range(len(flist))], rowmap, body)
-                # a key head: key pieces [slot | qhot << 16, common row, lag-ONE row, n | flags]
-                # then query pieces (R_QUERY), channel quads [row, c0, c1, 1.0 if the common
-                # form applies else 0]
+                # a key head is two records, on any warps: key pieces [slot | qhot << 16, common
+                # row, lag-ONE row, n | flags] and query pieces (R_QUERY); channel quads [row, c0,
+                # c1, 1.0 if the common form applies else 0]
                 recs, costs = [], []
                 one_f = _fbits(1.0)
                 for sl, h in enumerate(gheads):
-                    rec = []
-                    nkq = 0
                     for nm, qf_flag in (("k", 0), ("q", R_QUERY)):
                         com, lag, res = hf[h][nm]
                         com_row = frow[com] if com else ZW
@@ -578,11 +587,10 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                                     chans.append((frow[t] if t else ZW, _fbits(c0), _fbits(c1), one_f if com else 0))
                                 else:
                                     chans.append((ZW, 0, 0, 0))
-                        nkq += len(chans)
-                        rec += pieces(sl | int(g.head_qhot[h]) << 16, com_row, one_row, chans, qf_flag)
-                    recs.append(rec)
-                    costs.append(15 * nkq + 12 * len(rec))
-                    stats["kq_channels"] += nkq
+                        rec = pieces(sl | int(g.head_qhot[h]) << 16, com_row, one_row, chans, qf_flag)
+                        recs.append(rec)
+                        costs.append((12 if nm == "k" else 18) * len(chans) + 12 * len(rec))
+                        stats["kq_channels"] += len(chans)
                 stream_phase(PH["KSEL"], recs, costs, body)
                 v0 = len(vheads_l)
                 for sl, h in enumerate(gheads):
@@ -680,7 +688,21 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     s["VHSUM_ROWS"] = np.asarray(vhsum_l or [0], np.uint32)
     s["WARP_PTR"] = np.asarray(warp_ptr_l or [0], np.uint32)
     s["STAGES"] = arr(stages_l, "stage")
-    s["VHEADS"] = arr(vheads_l, "vhead")
+    # value heads with at most 4 distinct output rows: OUT_ROW holds indices into out4, and the
+    # kernel sums each row's columns across the warp before one add per row
+    vh_full = []
+    for v in vheads_l:
+        col = v[2]
+        rows = [r for r in dict.fromkeys(out_row_l[col:col + HD]) if r != NONE32]
+        if len(rows) <= 4:
+            for c in range(col, col + HD):
+                if out_row_l[c] != NONE32:
+                    out_row_l[c] = rows.index(out_row_l[c])
+            vh_full.append(tuple(v) + (len(rows), tuple(rows + [0] * (4 - len(rows)))))
+            stats["vh_out4"] += 1
+        else:
+            vh_full.append(tuple(v) + (0xFF, (0, 0, 0, 0)))
+    s["VHEADS"] = arr(vh_full, "vhead")
     s["VFORM"] = arr(vform_l, "colform")
     s["ZFORM"] = arr(zform_l, "colform")
     s["OUT_ROW"] = np.asarray(out_row_l, np.uint32)

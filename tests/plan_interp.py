@@ -73,7 +73,7 @@ class PlanInterp:
                     continue
                 cur.append((h, st[i + 1:i + 1 + n]))
                 i += 1 + n
-                if fl & R_LAST and not (k == PH["KSEL"] and not fl & 8):
+                if fl & R_LAST:
                     recs.append(cur)
                     cur = []
             assert not cur
@@ -124,10 +124,17 @@ class PlanInterp:
                     if ml >= 3:
                         H[2, e] = h[1]
             elif k == PH["FORMS"]:
+                f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
                     for pcs in recs:
                         body = np.concatenate([q for _, q in pcs])
-                        self.X[pcs[0][0][0]] = self.entries(body.reshape(-1))
+                        fa = np.zeros(self.B, np.float32)
+                        fb = np.zeros(self.B, np.float32)
+                        for e in body:
+                            fa = fa + f32(e[1]) * self.X[e[0]]
+                            fb = fb + f32(e[3]) * self.X[e[2]]
+                        self.X[pcs[0][0][0]] = fa
+                        self.X[pcs[0][0][1]] = fb
             elif k == PH["UNITS"]:
                 f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
@@ -147,23 +154,26 @@ class PlanInterp:
                 f32 = lambda v: np.uint32(v).view(np.float32)
                 for recs in self.warp_records(c, k):
                     for pcs in recs:
+                        # a key part or a query part of a key head
                         slot, qhot = int(pcs[0][0][0]) & 0xFFFF, int(pcs[0][0][0]) >> 16
-                        vals = {0: [], 8: []}
+                        query = bool(int(pcs[0][0][3]) >> 24 & 8)
+                        vals = []
                         for h, q in pcs:
                             com, x1 = self.X[h[1]], self.X[h[2]]
                             for qq in q:
                                 v = f32(qq[2]) * x1 + (f32(qq[1]) + (f32(qq[3]) * com + self.X[qq[0]]))
-                                vals[int(h[3]) >> 24 & 8].append(np.maximum(v, 0))
-                        kv = np.stack(vals[0]) if vals[0] else np.zeros((1, self.B), np.float32)
-                        qv = np.stack(vals[8]) if vals[8] else np.zeros((1, self.B), np.float32)
-                        km, ka = kv.max(0), kv.argmax(0)
-                        self.ksel[slot] = np.where(km > 0, ka, -1)
-                        sel = []
-                        for j in range(qhot):
-                            qm, qa = qv.max(0), qv.argmax(0)
-                            sel.append(np.where(qm > 0, qa, -1))
-                            qv[qa, np.arange(self.B)] = 0
-                        self.qsel[slot] = sel
+                                vals.append(np.maximum(v, 0))
+                        vv = np.stack(vals) if vals else np.zeros((1, self.B), np.float32)
+                        if not query:
+                            km, ka = vv.max(0), vv.argmax(0)
+                            self.ksel[slot] = np.where(km > 0, ka, -1)
+                        else:
+                            sel = []
+                            for j in range(qhot):
+                                qm, qa = vv.max(0), vv.argmax(0)
+                                sel.append(np.where(qm > 0, qa, -1))
+                                vv[qa, np.arange(self.B)] = 0
+                            self.qsel[slot] = sel
             elif k == PH["VHRUN"]:
                 pass  # the row work a VH phase lists is done here while it is listed
             elif k == PH["VHSUM"]:
@@ -205,6 +215,8 @@ class PlanInterp:
                             orow = int(s["OUT_ROW"][col + cc])
                             if orow == NONE:
                                 continue
+                            if int(vh["nout"]) != 0xFF:
+                                orow = int(vh["out4"][orow])  # an index into the head's 4 rows
                             zf = s["ZFORM"][col + cc]
                             z = max(self.X[int(zf["row"]), m] + zf["c"] * x0[m], 0) if zf["live"] else 0
                             out = o[cc] / norm if ref > 0 else np.float32(0)

@@ -72,7 +72,7 @@ def test_plan_is_consistent(graph, cluster):
     wp = s["WARP_PTR"].astype(np.int64)
     # walk every stream piece of every phase: rows in range, pieces inside one ring chunk,
     # records complete, ranges end on their warp's range
-    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_QUERY, R_SKIP
+    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_SKIP
 
     for ph in s["RUN_PROG"]:
         k = int(ph["kind"]) & 0xFF
@@ -91,10 +91,10 @@ def test_plan_is_consistent(graph, cluster):
                     continue
                 assert 1 + n <= PIECE_MAX
                 assert (i - start) // RING_QUADS == (i + n - start) // RING_QUADS, "piece crosses a chunk"
-                assert bool(fl & R_FIRST) != open_rec or (k == PH["KSEL"] and fl & R_QUERY and fl & R_FIRST)
+                assert bool(fl & R_FIRST) != open_rec
                 body = st[i + 1:i + 1 + n]
                 if k == PH["FORMS"]:
-                    assert h[0] < rows and h[0] % 132 == 0
+                    assert h[0] < rows and h[0] % 132 == 0 and h[1] < rows and h[1] % 132 == 0
                     assert np.all(body[:, 0] < rows) and np.all(body[:, 2] < rows)
                 elif k == PH["UNITS"]:
                     nc = int(h[1])
