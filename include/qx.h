@@ -53,9 +53,9 @@ enum { /* phase kinds of the per-token program */
     QX_PH_UNITS = 5,    /* FFN node records of the stream; warp ranges at warp_ptr[c] */
     QX_PH_KSEL = 6,     /* key-head records of the stream: key argmax, query top-k per machine */
     QX_PH_VH = 7,       /* value heads [a, b): list every (value head, machine) with row work;
-                           c: output delta rows of the phase (cluster plans, else 0) */
+                           c: output delta rows of the phase (at most QX_DELTA_ROWS) */
     QX_PH_VHRUN = 12,   /* value heads [a, b): serve the listed work: decay, write, read, output */
-    QX_PH_VHSUM = 13,   /* cluster plans: rows VHSUM_ROWS[a, a + b) += every CTA's delta row */
+    QX_PH_VHSUM = 13,   /* rows VHSUM_ROWS[a, a + b) += the group's output delta rows 0..b-1 */
     QX_PH_APPLY = 8,    /* X[dst] += X[src] for pairs [a, a + b) */
     QX_PH_WRITEOUT = 9, /* step mode: x[machine][dim] = X[row] for pairs [a, a + b) */
     QX_PH_DECODE = 10,  /* run mode: output code -> token; next embedding into X */
@@ -101,6 +101,7 @@ typedef struct {        /* value head task */
     uint32_t out4[4];   /* the output rows (byte offsets) */
 } qx_vhead;
 #define QX_OUT_DIRECT 0xFFu
+#define QX_DELTA_ROWS 128  /* output delta rows a value-head phase may use (per group, in HBM) */
 
 typedef struct {        /* a value head column's v or z: relu(F[row] + c x0) (F from the FORMS phase) */
     uint32_t row;       /* shared-memory byte offset of the form's row (the zero row if none) */
@@ -160,7 +161,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 11
+#define QX_PLAN_VERSION 12
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

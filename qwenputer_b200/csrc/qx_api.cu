@@ -175,11 +175,10 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
                             (unsigned long long)i);
             if ((kind == QX_PH_VH || kind == QX_PH_VHRUN) &&
                 (p[i].b < p[i].a || p[i].b - p[i].a > QX_VH_CHUNK || p[i].b > h.cnt[QX_S_VHEADS] ||
-                 (p[i].c > 0 && h.cluster == 1) ||
-                 qx_vh_worklist_offset(p[i].c) + (size_t)(p[i].b - p[i].a) * 32 * 8 > QX_RING_BYTES))
-                return fail(QX_ERR_INVALID_PLAN, "value-head phase [%u, %u) with %u delta rows exceeds the rings",
+                 p[i].c > QX_DELTA_ROWS || (size_t)(p[i].b - p[i].a) * 32 * 8 > QX_RING_BYTES))
+                return fail(QX_ERR_INVALID_PLAN, "value-head phase [%u, %u) with %u delta rows exceeds its buffers",
                             p[i].a, p[i].b, p[i].c);
-            if (kind == QX_PH_VHSUM && (h.cluster == 1 || (uint64_t)p[i].a + p[i].b > h.cnt[QX_S_VHSUM_ROWS]))
+            if (kind == QX_PH_VHSUM && (p[i].b > QX_DELTA_ROWS || (uint64_t)p[i].a + p[i].b > h.cnt[QX_S_VHSUM_ROWS]))
                 return fail(QX_ERR_INVALID_PLAN, "delta-sum phase beyond its rows");
         }
         if (!ended) return fail(QX_ERR_INVALID_PLAN, "program without an END phase");
@@ -302,6 +301,12 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     ex->dtok = static_cast<int32_t *>(p);
     if ((s = dev_alloc(ex, &p, 64)) != QX_OK) return bail(s);
     d.state_bytes = static_cast<unsigned long long *>(p);
+    {
+        const size_t vb = (size_t)(ex->Bpad / 32) * 2 * QX_DELTA_ROWS * 32 * 4;
+        if ((s = dev_alloc(ex, &p, vb)) != QX_OK) return bail(s);
+        d.vdelta = static_cast<float *>(p);
+        if (cudaMemset(p, 0, vb) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "delta init"));
+    }
     if (cudaMemset(p, 0, 64) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "counter init"));
     if (cudaMemset(d.x, 0, xb) != cudaSuccess || cudaMemset(d.err, 0, (size_t)batch * 4) != cudaSuccess ||
         cudaMemset(d.count, 0, (size_t)batch * 8) != cudaSuccess ||

@@ -163,10 +163,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
     float *sml = sm + lane;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
     unsigned int *wcount = touched + 1;  // [2] value-head worklist lengths, used in turn
     int vpar = 0;                        // which of the two the next VH phase appends to
-    // value-head phases reuse the stream rings: the CTA's output delta rows (cluster plans) and
-    // then the worklist
+    // value-head phases reuse the stream rings for their worklist; their outputs are summed in
+    // the group's delta rows in global memory (two buffers used in turn: the one a VHSUM phase
+    // read is cleared by the next serving phase, dprev rows of it)
     char *rings = reinterpret_cast<char *>(sm) + qx_ring_offset(d);
-    float *delta = reinterpret_cast<float *>(rings);
+    float *const D0 = d.vdelta + (size_t)(blockIdx.x / d.cluster) * (2 * QX_DELTA_ROWS * 32);
+    int dpar = 0;
+    uint32_t dprev = 0;
     if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
     if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; }
     const int grp = blockIdx.x / C;
@@ -434,8 +437,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // read touches a state row (record: value head, machine, decay factor, write row,
                 // query rows) in the CTA's worklist, which lives in the idle stream rings
                 const uint32_t n = ph.b - ph.a;
-                uint2 *wl = reinterpret_cast<uint2 *>(rings + qx_vh_worklist_offset(ph.c));
-                for (uint32_t j = warp; j < ph.c; j += QX_NW) delta[j * QX_RP + lane] = 0.0f;
+                uint2 *wl = reinterpret_cast<uint2 *>(rings);
                 for (uint32_t i = gw; i < n; i += nwv) {
                     const qx_vhead vh = d.vheads[ph.a + i];
                     const float x0 = QX_AT(sml, d.one_row);
@@ -481,8 +483,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // (decay, then write, then read, as the reference orders them).
                 // the other length was last read by the previous serve phase, a barrier ago
                 const uint32_t cnt = wcount[vpar];
-                const uint2 *wl = reinterpret_cast<const uint2 *>(rings + qx_vh_worklist_offset(ph.c));
-                float *obase = C > 1 ? delta : sm;  // outputs: the CTA's deltas, or the rows
+                const uint2 *wl = reinterpret_cast<const uint2 *>(rings);
+                float *const Dp = D0 + dpar * (QX_DELTA_ROWS * 32);  // this phase's output deltas
+                {
+                    float *const Dq = D0 + (dpar ^ 1) * (QX_DELTA_ROWS * 32);  // read by the last VHSUM
+                    for (uint32_t j = gw; j < dprev; j += nwv) Dq[j * 32 + lane] = 0.0f;
+                }
                 if (threadIdx.x == 0) wcount[vpar ^ 1] = 0;
                 vpar ^= 1;
                 for (uint32_t r0 = warp * 4; r0 < cnt; r0 += QX_NW * 4) {
@@ -607,7 +613,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             if ((uint32_t)lane < vh.nout) {
                                 const uint32_t r = lane == 0 ? vh.out4[0] : lane == 1 ? vh.out4[1] : lane == 2 ? vh.out4[2] : vh.out4[3];
                                 const float pr = lane == 0 ? p0 : lane == 1 ? p1 : lane == 2 ? p2 : p3;
-                                atomicAdd(&QX_AT(obase + mmv[b], r), pr);
+                                atomicAdd(Dp + (r >> 2) + mmv[b], pr);  // an L2 reduction
                             }
                         } else {
 #pragma unroll
@@ -615,7 +621,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                                 if (orow[k] == QX_NONE32) continue;
                                 const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
                                 const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
-                                atomicAdd(&QX_AT(obase + mmv[b], orow[k]), __fmul_rn(__fmul_rn(out, z), ow[k]));
+                                atomicAdd(Dp + (orow[k] >> 2) + mmv[b], __fmul_rn(__fmul_rn(out, z), ow[k]));
                             }
                         }
                     }
@@ -623,18 +629,15 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 }
                 break;
             }
-            case QX_PH_VHSUM:
-                // every CTA's output deltas, in rank order, into this copy's rows
-                for (uint32_t j = warp; j < ph.b; j += QX_NW) {
-                    float v = 0.0f;
-                    for (int r = 0; r < C; r++) {
-                        float pv;
-                        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(pv) : "r"(peer_addr(delta + j * QX_RP + lane, r)) : "memory");
-                        v += pv;
-                    }
-                    QX_AT(sml, d.vhsum_rows[ph.a + j]) += v;
-                }
+            case QX_PH_VHSUM: {
+                // the phase's output deltas into this copy's rows (L2 reads: the adds bypassed L1)
+                const float *Dp = D0 + dpar * (QX_DELTA_ROWS * 32);
+                for (uint32_t j = warp; j < ph.b; j += QX_NW)
+                    QX_AT(sml, d.vhsum_rows[ph.a + j]) += __ldcg(Dp + j * 32 + lane);
+                dprev = ph.b;
+                dpar ^= 1;
                 break;
+            }
             case QX_PH_DECODE: {
                 if (warp == 0) {
                     float fam = 0.0f, psum = 0.0f;
@@ -712,6 +715,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
             d.count[m] = count;
             d.halt_at[m] = halt_at;
         }
+    }
+    // the delta rows the last VHSUM read are cleared for the next launch (every copy has read
+    // them: the last phase ended with a barrier)
+    {
+        float *const Dq = D0 + (dpar ^ 1) * (QX_DELTA_ROWS * 32);
+        for (uint32_t j = gw; j < dprev; j += nwv) Dq[j * 32 + lane] = 0.0f;
     }
     if (C > 1) phase_sync(C);  // no CTA leaves while a peer may still address its rows
 }

@@ -21,6 +21,7 @@ struct QxDev {
     const uint2 *pairs;
     const uint4 *stream;
     const uint32_t *vhsum_rows;  // residual rows the cluster's output deltas add into
+    float *vdelta;  // [groups][2][QX_DELTA_ROWS][32] value-head output deltas (L2-resident)
     const uint32_t *warp_ptr;
     const qx_stage *stages;
     const qx_vhead *vheads;
@@ -66,8 +67,7 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
 // key-select slots, the decode area ([2][32] ints, [16][32] payload floats), a 64-byte counter
 // block and the per-warp stream rings ([NW][2][32] quads)
 // value heads one VH phase may list (the record packs the phase-local index in 8 bits); its
-// 8-byte (value head, machine) records live in the stream rings, after the phase's output delta
-// rows when the group runs on a cluster
+// 8-byte (value head, machine) records live in the stream rings
 #define QX_VH_CHUNK 64
 // stream piece flags (header quad .w >> 24)
 #define QX_R_FIRST 1u
@@ -76,9 +76,6 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
 #define QX_R_QUERY 8u
 #define QX_R_SKIP 0x80u
 #define QX_RING_BYTES (QX_NW * 2 * QX_RING_QUADS * 16)
-__host__ __device__ inline size_t qx_vh_worklist_offset(uint32_t delta_rows) {
-    return ((size_t)delta_rows * QX_RP * 4 + 15) / 16 * 16;
-}
 
 __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
     // rows (plus the zero row), key-select slots, decode area, counters

@@ -57,7 +57,7 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 11
+VERSION = 12
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -72,6 +72,7 @@ R_FIRST, R_LAST, R_STORE, R_QUERY, R_SKIP = 1, 2, 4, 8, 0x80
 # lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps); with a
 # cluster the rings also hold the CTA's output deltas (one row per output row of the phase)
 VH_CHUNK = 64
+DELTA_ROWS = 128  # output rows one value-head phase may sum into (the group's delta buffer)
 UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most this many
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
@@ -617,40 +618,36 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         vheads_l.append((hi, vhs_level.index(j), col, sl, int(g.vh_nrows[j]),
                                          frow[ta] if ta else ZW, frow[tb] if tb else ZW,
                                          ca, cb, 0.0 if g.vh_has_beta[j] else 1.0))
-                if cluster == 1:
-                    for c0 in range(v0, len(vheads_l), VH_CHUNK):
-                        c1 = min(c0 + VH_CHUNK, len(vheads_l))
-                        body.append((PH["VH"], c0, c1, 0))  # list the machines' row work
-                        body.append((PH["VHRUN"], c0, c1, 0))  # serve it
-                else:
-                    # each CTA sums its outputs into delta rows in its rings (worklist after
-                    # them); a VHSUM phase adds every CTA's deltas into each copy's rows
-                    def fits(nh, nr):
-                        return nh <= VH_CHUNK and (nr * ROW_PAD * 4 + 15) // 16 * 16 + nh * 32 * 8 <= ring_bytes
+                # value-head outputs are summed into the group's delta rows in global memory
+                # (one row per distinct output row of the phase, DELTA_ROWS at most, byte offset
+                # j * 128: 32 machines x fp32) by L2 atomic adds; a VHSUM phase adds them into
+                # the residual rows (of every copy, on a cluster)
+                def fits(nh, nr):
+                    return nh <= VH_CHUNK and nh * 32 * 8 <= ring_bytes and nr <= DELTA_ROWS
 
-                    c0 = v0
-                    while c0 < len(vheads_l):
-                        rows: list[int] = []
-                        c1 = c0
-                        while c1 < len(vheads_l):
-                            col = vheads_l[c1][2]
-                            new = [r for r in dict.fromkeys(out_row_l[col:col + HD]) if r != NONE32 and r not in rows]
-                            if not fits(c1 - c0 + 1, len(rows) + len(new)):
-                                break
-                            rows += new
-                            c1 += 1
-                        assert c1 > c0, "one value head's outputs exceed the rings"
-                        dpos = {r: i * ROW_PAD * 4 for i, r in enumerate(rows)}
-                        for v in range(c0, c1):
-                            col = vheads_l[v][2]
-                            for c in range(col, col + HD):
-                                if out_row_l[c] != NONE32:
-                                    out_row_l[c] = dpos[out_row_l[c]]
-                        body.append((PH["VH"], c0, c1, len(rows)))
-                        body.append((PH["VHRUN"], c0, c1, len(rows)))
-                        body.append((PH["VHSUM"], len(vhsum_l), len(rows), 0))
-                        vhsum_l.extend(rows)
-                        c0 = c1
+                c0 = v0
+                while c0 < len(vheads_l):
+                    rows: list[int] = []
+                    c1 = c0
+                    while c1 < len(vheads_l):
+                        col = vheads_l[c1][2]
+                        new = [r for r in dict.fromkeys(out_row_l[col:col + HD]) if r != NONE32 and r not in rows]
+                        if not fits(c1 - c0 + 1, len(rows) + len(new)):
+                            break
+                        rows += new
+                        c1 += 1
+                    assert c1 > c0, "one value head has more output rows than the delta buffer"
+                    dpos = {r: i * 128 for i, r in enumerate(rows)}
+                    for v in range(c0, c1):
+                        col = vheads_l[v][2]
+                        for c in range(col, col + HD):
+                            if out_row_l[c] != NONE32:
+                                out_row_l[c] = dpos[out_row_l[c]]
+                    body.append((PH["VH"], c0, c1, len(rows)))  # list the machines' row work
+                    body.append((PH["VHRUN"], c0, c1, len(rows)))  # serve it
+                    body.append((PH["VHSUM"], len(vhsum_l), len(rows), 0))
+                    vhsum_l.extend(rows)
+                    c0 = c1
             group_stats.append((lv, "head", len(groups)))
         apply_pairs = [(W(slot[d]), W(slot[k])) for (l2, d), k in temps.items() if l2 == lv]
         tail = []

@@ -47,10 +47,9 @@ class PlanInterp:
         self.H = [np.zeros((3, int(ne), B), np.float32) for ne in s["HL_NE"]]
         self.one = h["one_row"]
         self.ksel, self.qsel = {}, {}
-        # cluster plans: value-head outputs go to delta rows (in the stream rings), which VHSUM
-        # phases add into the residual rows
-        self.cluster = h["cluster"]
-        self.Dw = np.zeros((128 * 33, B), np.float32)
+        # value-head outputs go to delta rows (byte offset j * 128), which VHSUM phases add into
+        # the residual rows
+        self.Dw = np.zeros((128 * 32, B), np.float32)
         self.delta = _ByteIndexed(self.Dw)
 
     def warp_records(self, c, k):
@@ -178,10 +177,10 @@ class PlanInterp:
                 pass  # the row work a VH phase lists is done here while it is listed
             elif k == PH["VHSUM"]:
                 for jj in range(b):
-                    self.X[int(s["VHSUM_ROWS"][a + jj])] += self.delta[jj * 33 * 4]
+                    self.X[int(s["VHSUM_ROWS"][a + jj])] += self.delta[jj * 128]
             elif k == PH["VH"]:
-                self.Dw[:c * 33] = 0
-                out_rows = self.delta if self.cluster > 1 else self.X
+                self.Dw[:] = 0
+                out_rows = self.delta
                 x0 = self.X[self.one]
                 for vh in s["VHEADS"][a:b]:
                     hl, j, col, sl = int(vh["hl"]), int(vh["vh"]), int(vh["col"]), int(vh["slot"])
