@@ -588,6 +588,11 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         float ref = __fadd_rn(__fmul_rn(o.x, o.x), __fmul_rn(o.y, o.y));
                         ref = __shfl_sync(0xFFFFFFFFu, ref, 0);  // (uniform: the batch's records are)
                         const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
+                        // o / norm; when norm is a power of two (the usual read: the markers
+                        // give ref = 128 * 4^e), multiplying by its exact reciprocal rounds the same
+                        const uint32_t nb = __float_as_uint(norm);
+                        const bool pow2 = (nb & 0x7FFFFFu) == 0u && nb >= 0x01000000u && nb < 0x7E800000u;
+                        const float inv = pow2 ? __uint_as_float(0x7F000000u - nb) : 0.0f;
                         const float oc[4] = {o.x, o.y, o.z, o.w};
                         if (vh.nout != QX_OUT_DIRECT) {
                             // at most 4 output rows: per-row sums over the warp, one add per row
@@ -596,7 +601,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             for (int k = 0; k < 4; k++) {
                                 if (orow[k] == QX_NONE32) continue;
                                 const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
-                                const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
+                                const float out = ref > 0.0f ? (pow2 ? oc[k] * inv : __fdiv_rn(oc[k], norm)) : 0.0f;
                                 const float val = __fmul_rn(__fmul_rn(out, z), ow[k]);
                                 p0 += orow[k] == 0 ? val : 0.0f;
                                 p1 += orow[k] == 1 ? val : 0.0f;
@@ -620,7 +625,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             for (int k = 0; k < 4; k++) {
                                 if (orow[k] == QX_NONE32) continue;
                                 const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
-                                const float out = ref > 0.0f ? __fdiv_rn(oc[k], norm) : 0.0f;
+                                const float out = ref > 0.0f ? (pow2 ? oc[k] * inv : __fdiv_rn(oc[k], norm)) : 0.0f;
                                 atomicAdd(Dp + (orow[k] >> 2) + mmv[b], __fmul_rn(__fmul_rn(out, z), ow[k]));
                             }
                         }
