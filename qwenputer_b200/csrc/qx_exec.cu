@@ -312,18 +312,16 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     if (fl & QX_R_FIRST) acc0 = acc1 = acc2 = acc3 = 0.0f;
                     const uint32_t nc = h.y;
                     uint32_t j = 0;
-                    for (; j + 4 <= nc; j += 4) {
-                        const uint4 u0 = q[j], u1 = q[j + 1], u2 = q[j + 2], u3 = q[j + 3];
-                        const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x), f2 = QX_AT(sml, u2.x),
-                                    f3 = QX_AT(sml, u3.x);
+                    for (; j + 2 <= nc; j += 2) {
+                        const uint4 u0 = q[j], u1 = q[j + 1];
+                        const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x);
                         acc0 = fmaf(__uint_as_float(u0.y), relu(f0 + __uint_as_float(u0.z)), acc0);
                         acc1 = fmaf(__uint_as_float(u1.y), relu(f1 + __uint_as_float(u1.z)), acc1);
-                        acc2 = fmaf(__uint_as_float(u2.y), relu(f2 + __uint_as_float(u2.z)), acc2);
-                        acc3 = fmaf(__uint_as_float(u3.y), relu(f3 + __uint_as_float(u3.z)), acc3);
                     }
-                    for (; j < nc; j++) {
+                    if (j < nc) {
                         const uint4 u0 = q[j];
-                        acc0 = fmaf(__uint_as_float(u0.y), relu(QX_AT(sml, u0.x) + __uint_as_float(u0.z)), acc0);
+                        acc2 = fmaf(__uint_as_float(u0.y), relu(QX_AT(sml, u0.x) + __uint_as_float(u0.z)), acc2);
+                        j++;
                     }
                     for (; j < n; j += 2) {
                         const uint4 u = q[j], u2 = q[j + 1];
