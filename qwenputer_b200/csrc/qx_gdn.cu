@@ -143,17 +143,20 @@ __global__ void __launch_bounds__(128) qx_gdn_matrix_kernel(float *__restrict__ 
                 if (j == 0) atomicOr(&work[1], QX_ERR_DEVICE_FLAG);
                 return;
             }
-            for (int i = 0; i < GDN_D; i++) sS[i * GDN_D + j] = __fmul_rn(sS[i * GDN_D + j], a);
         } else {
             __syncthreads();
-            for (int i = 0; i < GDN_D; i++) sS[i * GDN_D + j] = 0.0f;
+            for (int i = 0; i < GDN_D; i++) sS[i * GDN_D + j] = 0.0f;  // 0 * S (no load needed)
         }
+        // two passes over the column: alpha * S is recomputed (the same rounding) instead of
+        // being written back first
         float kv = 0.0f;
-        for (int i = 0; i < GDN_D; i++) kv = __fadd_rn(kv, __fmul_rn(sS[i * GDN_D + j], sk[i]));
+#pragma unroll 8
+        for (int i = 0; i < GDN_D; i++) kv = __fadd_rn(kv, __fmul_rn(__fmul_rn(sS[i * GDN_D + j], a), sk[i]));
         const float delta = __fmul_rn(__fsub_rn(vj, kv), b);
         float oj = 0.0f;
+#pragma unroll 8
         for (int i = 0; i < GDN_D; i++) {
-            const float s2 = __fadd_rn(sS[i * GDN_D + j], __fmul_rn(sk[i], delta));
+            const float s2 = __fadd_rn(__fmul_rn(sS[i * GDN_D + j], a), __fmul_rn(sk[i], delta));
             sS[i * GDN_D + j] = s2;
             oj = __fadd_rn(oj, __fmul_rn(s2, sq[i]));
         }
