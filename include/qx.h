@@ -158,10 +158,12 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_EMB_TABLE,      /* float [n_emb_rows][n_feat] */
     QX_S_TABLES,         /* uint32 [99][2]: snapshot table -> (head level, first value head) */
     QX_S_REG_COLS,       /* int32 [32][8] */
+    QX_S_FAM_TOUCH_PTR,  /* uint32 [n_families + 1]: offsets into FAM_TOUCH */
+    QX_S_FAM_TOUCH,      /* uint32: per family, the features its payload-built embeddings touch */
     QX_S_COUNT
 };
 
-#define QX_PLAN_VERSION 12
+#define QX_PLAN_VERSION 13
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

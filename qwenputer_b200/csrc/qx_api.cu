@@ -147,11 +147,14 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
         {QX_S_VFORM, sizeof(qx_colform)}, {QX_S_ZFORM, sizeof(qx_colform)}, {QX_S_OUT_ROW, 4}, {QX_S_OUT_W, 4},
         {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 4}, {QX_S_PAY_ROW, 4}, {QX_S_FEAT_ROW, 4},
         {QX_S_FAM_IDS, 4}, {QX_S_FAM_SIZE, 4}, {QX_S_FAM_ROW0, 4}, {QX_S_EMB_BASE, 4}, {QX_S_EMB_BITS, 4},
-        {QX_S_EMB_TABLE, 4}, {QX_S_TABLES, 4}, {QX_S_REG_COLS, 4}};
+        {QX_S_EMB_TABLE, 4}, {QX_S_TABLES, 4}, {QX_S_REG_COLS, 4},
+        {QX_S_FAM_TOUCH_PTR, 4}, {QX_S_FAM_TOUCH, 4}};
     for (const SecSpec &s : specs) {
         if (h.off[s.id] % 16 || h.off[s.id] + h.cnt[s.id] * s.elem > bytes)
             return fail(QX_ERR_INVALID_PLAN, "section %d out of bounds", s.id);
     }
+    if (h.cnt[QX_S_FAM_TOUCH_PTR] != (uint64_t)h.n_families + 1)
+        return fail(QX_ERR_INVALID_PLAN, "touched-feature offsets missing");
     if (h.cnt[QX_S_TABLES] != 198 || h.cnt[QX_S_REG_COLS] != 256)
         return fail(QX_ERR_INVALID_PLAN, "snapshot tables missing");
     if (h.cnt[QX_S_HL_V] != h.n_head_levels || h.cnt[QX_S_FEAT_ROW] != h.n_feat ||
@@ -183,6 +186,13 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
         }
         if (!ended) return fail(QX_ERR_INVALID_PLAN, "program without an END phase");
     }
+    const uint32_t *tp = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FAM_TOUCH_PTR]);
+    const uint32_t *tf = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FAM_TOUCH]);
+    for (uint32_t f = 0; f < h.n_families; f++)
+        if (tp[f] > tp[f + 1] || tp[f + 1] > h.cnt[QX_S_FAM_TOUCH])
+            return fail(QX_ERR_INVALID_PLAN, "touched-feature offsets out of order");
+    for (uint32_t i = 0; i < tp[h.n_families]; i++)
+        if (tf[i] >= h.n_feat) return fail(QX_ERR_INVALID_PLAN, "touched feature beyond the features");
     return QX_OK;
 }
 
@@ -241,6 +251,8 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.fam_row0 = sec<int32_t>(ex, QX_S_FAM_ROW0);
     d.emb_base = sec<float>(ex, QX_S_EMB_BASE);
     d.emb_bits = sec<float>(ex, QX_S_EMB_BITS);
+    d.fam_touch_ptr = sec<uint32_t>(ex, QX_S_FAM_TOUCH_PTR);
+    d.fam_touch = sec<uint32_t>(ex, QX_S_FAM_TOUCH);
     d.emb_table = sec<float>(ex, QX_S_EMB_TABLE);
     d.tables = sec<uint32_t>(ex, QX_S_TABLES);
     d.reg_cols = sec<int32_t>(ex, QX_S_REG_COLS);

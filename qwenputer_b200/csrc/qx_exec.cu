@@ -679,10 +679,14 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         for (int f = lane; f < d.n_feat; f += 32)
                             QX_AT(smw, d.feat_row[f]) = __ldg(d.emb_table + (size_t)r * d.n_feat + f);
                     } else {
+                        // every feature 0, then the family's touched ones: base + the payload
+                        // bits' rows (four partial sums: exact values, any order)
                         const float *bits = d.emb_bits + (size_t)fid * d.n_pay * d.n_feat;
-                        for (int f = lane; f < d.n_feat; f += 32) {
-                            // four partial sums (exact values: any order) so the loads of the
-                            // payload bits' rows are in flight together
+                        for (int f = lane; f < d.n_feat; f += 32) QX_AT(smw, d.feat_row[f]) = 0.0f;
+                        __syncwarp();
+                        const uint32_t t1 = d.fam_touch_ptr[fid + 1];
+                        for (uint32_t t = d.fam_touch_ptr[fid] + lane; t < t1; t += 32) {
+                            const int f = (int)d.fam_touch[t];
                             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                             int i = 0;
                             for (; i + 4 <= d.n_pay; i += 4) {

@@ -31,6 +31,7 @@ struct QxDev {
     const uint32_t *fam_row, *pay_row, *feat_row;
     const int32_t *fam_ids, *fam_size, *fam_row0;
     const float *emb_base, *emb_bits, *emb_table;
+    const uint32_t *fam_touch_ptr, *fam_touch;  // per family: the features its embeddings touch
     const uint32_t *tables;     // [99][2]
     const int32_t *reg_cols;    // [32][8]
     // executor buffers

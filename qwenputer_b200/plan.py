@@ -57,7 +57,7 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 12
+VERSION = 13
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -77,7 +77,7 @@ UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most t
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
        "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
-       "TABLES", "REG_COLS"]
+       "TABLES", "REG_COLS", "FAM_TOUCH_PTR", "FAM_TOUCH"]
 TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
                + [f"quo{i}" for i in range(4)] + [f"rom{i}" for i in range(32)]
                + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
@@ -722,6 +722,17 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         tabs.append((hl_index[lv], vh0))
     s["TABLES"] = np.asarray(tabs, np.uint32).reshape(-1)
     s["REG_COLS"] = np.asarray(g.reg_cols, np.int32).reshape(-1)
+    # per family built from payload bits: the feature indices its embeddings can make nonzero
+    # (the base row's or any bit row's nonzeros); every other feature of such a token is 0
+    eb = np.asarray(g.emb_bits, np.float32).reshape(len(g.fam_ids), -1, len(feat))
+    ebase = np.asarray(g.emb_base, np.float32).reshape(len(g.fam_ids), len(feat))
+    tptr, touch = [0], []
+    for f in range(len(g.fam_ids)):
+        nz = np.flatnonzero((ebase[f] != 0) | (eb[f] != 0).any(axis=0))
+        touch.extend(int(x) for x in nz)
+        tptr.append(len(touch))
+    s["FAM_TOUCH_PTR"] = np.asarray(tptr, np.uint32)
+    s["FAM_TOUCH"] = np.asarray(touch or [0], np.uint32)
     P.hdr = dict(D=D, n_slots=n_slots, n_scratch=n_scratch, nw=nw, n_head_levels=len(head_levels),
                  one_row=one_w, n_ksel_slots=ksel_slots, qhot_max=qhot,
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
