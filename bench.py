@@ -39,8 +39,8 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "rv32im_trace_tokens_per_s"
 # DRAM bytes per machine-token of the token kernel: an ncu capture of 256 machines x 4 tokens
-# (dram__bytes_read.sum + dram__bytes_write.sum = 10.84 MB + 0 B), per machine-token
-DRAM_BYTES_PER_MACHINE_TOKEN = 10.84e6 / 1024
+# (dram__bytes_read.sum + dram__bytes_write.sum = 11.62 MB + 8 KB), per machine-token
+DRAM_BYTES_PER_MACHINE_TOKEN = (11.62368e6 + 8192) / 1024
 WORKLOAD = "rv32im free-run, bignum mix (40% MUL/MULH/DIVU chains, 20% LW/SW over 16 KB)"
 UNIT = "tokens/s"
 GO_TOKEN = 230322  # the run-start control (families then controls: NT .. HALT, GO, SC)
