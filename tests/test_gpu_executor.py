@@ -189,3 +189,43 @@ def test_gdn_two_steps_and_beta(qx):
         assert np.array_equal(od.cpu().numpy(), ow), step
         assert np.array_equal(Sd.cpu().numpy(), So), step
         q = q.roll(1, 0)
+
+
+@pytest.mark.parametrize("cluster", [1, 4])
+def test_step_in_cuda_graph(qx, graph, programs, cluster):
+    """Executor.step captured in a CUDA graph (as ExecRow captures Executor2.step) replays the
+    same residuals and head states as eager steps."""
+    names = ["gen_small_7", "div_fuzz_0", "mul_fuzz_1"]
+    progs = [programs[n]["prog"] for n in names]
+    traces = [programs[n]["trace"] for n in names]
+    eager = qx.Executor(None, batch=3, cluster=cluster)
+    capt = qx.Executor(None, batch=3, cluster=cluster)
+    for ex in (eager, capt):
+        ex.load_machines(0, progs)
+    xbuf = torch.zeros(3, graph.D, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        capt.step(xbuf.clone())  # warm-up outside the graph on the capture stream
+    torch.cuda.current_stream().wait_stream(s)
+    # the warm-up step moved capt one token ahead: restart both from the same state
+    for ex in (eager, capt):
+        ex.load_machines(0, progs)
+        ex.reset()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        capt.step(xbuf)
+    for t in range(20):
+        toks = [int(tr[min(t, len(tr) - 1)]) for tr in traces]
+        emb = torch.from_numpy(graph.embed(toks)).cuda()
+        xe = emb.clone()
+        eager.step(xe)
+        xbuf.copy_(emb)
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(xe, xbuf), t
+    for a, b in zip([s_["S"] for s_ in eager.steps if s_["kind"] == "head"],
+                    [s_["S"] for s_ in capt.steps if s_["kind"] == "head"]):
+        assert torch.equal(a, b)
+    del g
