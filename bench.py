@@ -231,7 +231,7 @@ def reference_arm(args) -> None:
     dt = time.perf_counter() - t0
     val = B * tps * args.steps / dt
     sample = f"{B} machines x {tps} free-running tokens per step on {cores} host threads"
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
@@ -241,10 +241,24 @@ def reference_arm(args) -> None:
                    "tokens_per_step": tps, "sample_machines": B},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
+
+
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """The one JSON line, on the process's original stdout."""
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(line) + "\n").encode())
 
 
 def main() -> None:
+    global _JSON_FD
+    # stdout carries only the JSON line: anything else written to fd 1 (library banners such as
+    # NCCL's version line) goes to stderr
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
@@ -393,7 +407,7 @@ def main() -> None:
             "e2e": e2e, "cpu_baseline": cpu, "gdn_step": gdn,
             "checksum_xor": f"{combined:016x}", "device_errors": errs,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
