@@ -4,7 +4,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "qx.h"
@@ -22,6 +24,7 @@ __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, i
 __global__ void qx_predecode_kernel(const QxImage *img, uint32_t *pool, int32_t n);
 __global__ void qx_load_kernel(const __grid_constant__ QxDev d, const QxImage *img, const uint32_t *pool,
                                int32_t row0, int32_t n);
+__global__ void qx_load_cover_kernel(const __grid_constant__ QxDev d, uint8_t *cover);
 __global__ void qx_readback_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, qx_state *out);
 __global__ void qx_checksum_kernel(const qx_state *st, int32_t n, uint64_t *out);
 __global__ void qx_reset_kernel(float *H, uint32_t ne, uint32_t bpad, int32_t row0, int32_t n);
@@ -70,6 +73,10 @@ struct qx_executor {
     void *dstage[2] = {nullptr, nullptr};
     size_t stage_bytes = 0;
     cudaEvent_t staged[2] = {nullptr, nullptr};
+    // the image copies run on their own stream, so that chunk k+1 crosses PCIe while the loader
+    // kernels build chunk k
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t copied[2] = {nullptr, nullptr};
     ~qx_executor() {
         for (void *p : allocs) cudaFree(p);
         if (dplan) cudaFree(dplan);
@@ -79,7 +86,9 @@ struct qx_executor {
             if (pin[i]) cudaFreeHost(pin[i]);
             if (dstage[i]) cudaFree(dstage[i]);
             if (staged[i]) cudaEventDestroy(staged[i]);
+            if (copied[i]) cudaEventDestroy(copied[i]);
         }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
     }
 };
 
@@ -163,8 +172,19 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     return QX_OK;
 }
 
-// every program ends, and every value-head phase names at most QX_VH_CHUNK heads of the section
+// every snapshot table names head state, every program ends, and every value-head phase names at most QX_VH_CHUNK heads of the section
 qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
+    {
+        // every snapshot table names a head sublayer and value heads inside it (tables 0-6, the
+        // counter and register heads, use their first value head; the rest use two)
+        const uint32_t *tab = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_TABLES]);
+        const uint32_t *hlv = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_HL_V]);
+        for (int t = 0; t < 99; t++) {
+            const uint32_t hl = tab[2 * t], vh0 = tab[2 * t + 1], need = t < 7 ? 1 : 2;
+            if (hl >= h.n_head_levels || hl >= QX_MAX_HL || vh0 > hlv[hl] || hlv[hl] - vh0 < need)
+                return fail(QX_ERR_INVALID_PLAN, "snapshot table %d names no head state", t);
+        }
+    }
     for (int id : {QX_S_RUN_PROG, QX_S_STEP_PROG}) {
         const qx_phase *p = reinterpret_cast<const qx_phase *>(plan + h.off[id]);
         bool ended = false;
@@ -194,6 +214,35 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
     for (uint32_t i = 0; i < tp[h.n_families]; i++)
         if (tf[i] >= h.n_feat) return fail(QX_ERR_INVALID_PLAN, "touched feature beyond the features");
     return QX_OK;
+}
+
+}  // namespace
+
+namespace {
+
+// Runs pack(lo, hi) over [0, n) split into contiguous ranges on up to 8 threads (one copy stream
+// into pinned memory does not reach the host's memory bandwidth); serially when n is small or a
+// thread cannot be started.
+template <class F>
+void pack_parallel(int n, const F &pack) {
+    const unsigned hw = std::thread::hardware_concurrency();
+    const int T = n < 64 ? 1 : (int)std::min(8u, std::max(1u, hw));
+    if (T == 1) {
+        pack(0, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    int done = 0;  // ranges below this index run on threads
+    try {
+        for (int t = 1; t < T; t++) {
+            th.emplace_back([&pack, n, T, t] { pack((int)((int64_t)n * t / T), (int)((int64_t)n * (t + 1) / T)); });
+            done = t;
+        }
+    } catch (...) {
+    }
+    pack(0, (int)((int64_t)n / T));
+    if (done + 1 < T) pack((int)((int64_t)n * (done + 1) / T), n);  // ranges no thread took
+    for (std::thread &x : th) x.join();
 }
 
 }  // namespace
@@ -325,6 +374,41 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
         cudaMemset(d.halt_at, 0xFF, (size_t)batch * 8) != cudaSuccess ||
         cudaMemset(d.hash, 0, (size_t)batch * 8) != cudaSuccess)
         return bail(fail(QX_ERR_CUDA, "buffer init"));
+    {
+        // the head-state rows of a machine that no load task writes: qx_load_machines writes zeros
+        // there, so that a load leaves every row of the machine's state written once
+        size_t rows = 0;
+        for (int i = 0; i < ex->n_hl; i++) rows += (size_t)d.V[i] * QX_HD;
+        uint8_t *cover = nullptr;
+        if (cudaMalloc(&cover, rows) != cudaSuccess) {
+            cudaGetLastError();
+            return bail(fail(QX_ERR_OOM, "row coverage scratch"));
+        }
+        std::vector<uint8_t> hc(rows);
+        cudaError_t e = cudaMemset(cover, 0, rows);
+        if (e == cudaSuccess) {
+            qx_load_cover_kernel<<<32, 256>>>(d, cover);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaMemcpy(hc.data(), cover, rows, cudaMemcpyDeviceToHost);
+        cudaFree(cover);
+        if (e != cudaSuccess) return bail(fail(QX_ERR_CUDA, "row coverage: %s", cudaGetErrorString(e)));
+        std::vector<uint32_t> zl;
+        size_t base = 0;
+        for (int i = 0; i < ex->n_hl; i++) {
+            for (uint32_t r = 0; r < d.V[i] * QX_HD; r++)
+                if (!hc[base + r]) { zl.push_back((uint32_t)i); zl.push_back(r); }
+            base += (size_t)d.V[i] * QX_HD;
+        }
+        d.n_zero_rows = (int32_t)(zl.size() / 2);
+        d.zero_rows = nullptr;
+        if (d.n_zero_rows) {
+            if ((s = dev_alloc(ex, &p, zl.size() * 4)) != QX_OK) return bail(s);
+            if (cudaMemcpy(p, zl.data(), zl.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+                return bail(fail(QX_ERR_CUDA, "zero-row list"));
+            d.zero_rows = static_cast<const uint2 *>(p);
+        }
+    }
     if (cudaMallocHost(&ex->err_host, (size_t)batch * 4) != cudaSuccess)
         return bail(fail(QX_ERR_OOM, "pinned error buffer"));
     ex->smem = qx_smem_bytes(d);
@@ -422,6 +506,7 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
         for (int i = 0; i < cn; i++) b += 4 * pool_words(images[c0 + i]);
         need = b > need ? b : need;
     }
+    if (!ex->copy_stream) CU(cudaStreamCreateWithFlags(&ex->copy_stream, cudaStreamNonBlocking));
     if (need > ex->stage_bytes) {
         for (int i = 0; i < 2; i++) {
             if (ex->staged[i]) CU(cudaEventSynchronize(ex->staged[i]));
@@ -435,6 +520,7 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
                 cudaMalloc(&ex->dstage[i], need) != cudaSuccess)
                 return fail(QX_ERR_OOM, "qx_load_machines: %zu B of staging", need);
             if (!ex->staged[i]) CU(cudaEventCreateWithFlags(&ex->staged[i], cudaEventDisableTiming));
+            if (!ex->copied[i]) CU(cudaEventCreateWithFlags(&ex->copied[i], cudaEventDisableTiming));
         }
         ex->stage_bytes = need;
     }
@@ -444,43 +530,49 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
         QxImage *img = static_cast<QxImage *>(ex->pin[k]);
         uint32_t *pool = reinterpret_cast<uint32_t *>(img + cn);
         uint32_t w = 0;
-        for (int i = 0; i < cn; i++) {
-            const qx_machine &m = images[c0 + i];
-            QxImage &q = img[i];
-            q.rom_off = w;
-            q.rom_len = m.rom_words;
-            if (m.rom_words) memcpy(pool + w, m.rom, (size_t)m.rom_words * 4);
-            w += m.rom_words;
-            q.drom_off = w;
-            q.drom_words = (m.drom_bytes + 3) / 4;
-            if (q.drom_words) {
-                pool[w + q.drom_words - 1] = 0;
-                memcpy(pool + w, m.drom, m.drom_bytes);  // little-endian words of the bytes
-            }
-            w += q.drom_words;
-            q.ram_off = w;
-            memcpy(pool + w, m.ram, 8192 * 4);
-            w += 8192;
-            if (m.bn) {
-                q.bn_off = w;
-                memcpy(pool + w, m.bn, 1024);
-                w += 256;
-            } else {
-                q.bn_off = 0xFFFFFFFFu;
-            }
-            memcpy(q.x, m.x, sizeof(q.x));
-            q.x[0] = 0;
-            q.anchor = m.anchor;
-            q.n = m.n;
+        for (int i = 0; i < cn; i++) {  // the pool offsets first, then the copies (several threads)
+            img[i].rom_off = w;
+            w += (uint32_t)pool_words(images[c0 + i]);
         }
+        auto pack = [&](int lo, int hi) {
+            for (int i = lo; i < hi; i++) {
+                const qx_machine &m = images[c0 + i];
+                QxImage &q = img[i];
+                uint32_t o = q.rom_off;
+                q.rom_len = m.rom_words;
+                if (m.rom_words) memcpy(pool + o, m.rom, (size_t)m.rom_words * 4);
+                o += m.rom_words;
+                q.drom_off = o;
+                q.drom_words = (m.drom_bytes + 3) / 4;
+                if (q.drom_words) {
+                    pool[o + q.drom_words - 1] = 0;
+                    memcpy(pool + o, m.drom, m.drom_bytes);  // little-endian words of the bytes
+                }
+                o += q.drom_words;
+                q.ram_off = o;
+                memcpy(pool + o, m.ram, 8192 * 4);
+                o += 8192;
+                if (m.bn) {
+                    q.bn_off = o;
+                    memcpy(pool + o, m.bn, 1024);
+                } else {
+                    q.bn_off = 0xFFFFFFFFu;
+                }
+                memcpy(q.x, m.x, sizeof(q.x));
+                q.x[0] = 0;
+                q.anchor = m.anchor;
+                q.n = m.n;
+            }
+        };
+        pack_parallel(cn, pack);
         const size_t bytes = (size_t)cn * sizeof(QxImage) + (size_t)w * 4;
         QxImage *dimg = static_cast<QxImage *>(ex->dstage[k]);
         uint32_t *dpool = reinterpret_cast<uint32_t *>(dimg + cn);
-        cudaError_t e = cudaMemcpyAsync(dimg, img, bytes, cudaMemcpyHostToDevice, st);
-        for (int i = 0; i < ex->n_hl && e == cudaSuccess; i++) {
-            size_t per = (size_t)ex->d.V[i] * QX_HD * QX_HD * 4;
-            e = cudaMemsetAsync(reinterpret_cast<uint8_t *>(ex->d.S[i]) + per * (row0 + c0), 0, per * cn, st);
-        }
+        // the loader writes every head-state row of the machines, so nothing is cleared first; the
+        // staging buffer's last reader (the loader two chunks back) has finished (staged[k])
+        cudaError_t e = cudaMemcpyAsync(dimg, img, bytes, cudaMemcpyHostToDevice, ex->copy_stream);
+        if (e == cudaSuccess) e = cudaEventRecord(ex->copied[k], ex->copy_stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ex->copied[k], 0);
         if (e == cudaSuccess) {
             qx_predecode_kernel<<<dim3(4, cn), 256, 0, st>>>(dimg, dpool, cn);
             qx_load_kernel<<<dim3(64, cn), 256, 0, st>>>(ex->d, dimg, dpool, row0 + c0, cn);

@@ -34,6 +34,7 @@ struct QxDev {
     const uint32_t *fam_touch_ptr, *fam_touch;  // per family: the features its embeddings touch
     const uint32_t *tables;     // [99][2]
     const int32_t *reg_cols;    // [32][8]
+    const uint2 *zero_rows;     // [n_zero_rows] (head sublayer, row) of the rows no load task writes
     // executor buffers
     float *S[QX_MAX_HL];        // [B][V][128][128]
     float *hist[QX_MAX_HL];     // [3][NE][Bpad]
@@ -50,6 +51,7 @@ struct QxDev {
     int32_t qhot_max, ksel_slots, n_hl, halt_tok;
     uint32_t zero_row;  // byte offset of the row kept at zero
     int32_t cluster;    // CTAs sharing one group of 32 machines (a thread-block cluster)
+    int32_t n_zero_rows;
 };
 
 // per-machine error bits

@@ -119,99 +119,202 @@ __device__ __forceinline__ float *row_ptr(const QxDev &d, int t, int x, int r, i
     return d.S[hl] + (((size_t)m * d.V[hl] + vh0 + x) * QX_HD + r) * QX_HD;
 }
 
+#define QX_LOAD_TASKS 22636  // content rows a machine's load writes (the zero-row list follows)
+
+// The state row load task `task` writes for machine m (the same map serves the loader and the
+// coverage kernel that finds the rows no task writes)
+__device__ __forceinline__ float *task_row(const QxDev &d, int task, int m) {
+    if (task == 0) return row_ptr(d, T_PC, 0, 0, m);
+    if (task < 7) return row_ptr(d, T_COUNT + (task - 1) / 2, 0, (task - 1) % 2, m);
+    if (task < 100) return row_ptr(d, T_REGS + (task - 7) / 31, 0, 1 + (task - 7) % 31, m);
+    if (task < 108) return row_ptr(d, T_QUO + (task - 100) / 2, (task - 100) % 2, 0, m);
+    if (task < 12396) {
+        const bool rom = task < 8300;
+        const int k0 = rom ? task - 108 : task - 8300;
+        return row_ptr(d, (rom ? T_ROM : T_DROM) + k0 / 256, (k0 / 128) % 2, k0 % 128, m);
+    }
+    if (task < 14444) {
+        const int k0 = task - 12396;
+        return row_ptr(d, (k0 / 1024 ? T_BN2 : T_BN1) + (k0 / 256) % 4, (k0 / 128) % 2, k0 % 128, m);
+    }
+    const uint32_t wi = (uint32_t)(task - 14444);
+    return row_ptr(d, T_RAM + ((wi & 15) | (wi >> 12) << 4), wi >> 4 & 1, wi >> 5 & 127, m);
+}
+
 }  // namespace
+
+// Marks, in cover[hl][row] (machine 0's rows), every state row a load task writes.
+__global__ void qx_load_cover_kernel(const __grid_constant__ QxDev d, uint8_t *cover) {
+    for (int task = blockIdx.x * blockDim.x + threadIdx.x; task < QX_LOAD_TASKS; task += gridDim.x * blockDim.x) {
+        const float *row = task_row(d, task, 0);
+        size_t base = 0;
+        for (int hl = 0; hl < d.n_hl; hl++) {
+            const size_t rows = (size_t)d.V[hl] * QX_HD;
+            if (row >= d.S[hl] && row < d.S[hl] + rows * QX_HD) {
+                cover[base + (size_t)(row - d.S[hl]) / QX_HD] = 1;
+                break;
+            }
+            base += rows;
+        }
+    }
+}
 
 // Pre-decode every machine's ROM words in the pool, in place (zero words stay zero).
 __global__ void qx_predecode_kernel(const QxImage *img, uint32_t *pool, int32_t n) {
     const int i = blockIdx.y;
     if (i >= n) return;
-    const QxImage im = img[i];
+    const QxImage &im = img[i];  // read in place (a copy would live in local memory)
     for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < im.rom_len; k += gridDim.x * blockDim.x) {
         uint32_t w = pool[im.rom_off + k];
         pool[im.rom_off + k] = w ? rom_word(w, ROM_BASE + 4 * k) : 0;
     }
 }
 
-// One warp per state row; blockIdx.y = machine (row0 + y).  Row tasks of a machine:
+// The small content rows, task [0, 108) of a machine: this lane's four columns and the row.
 //   [0, 7) pc, count x2, j x2, vcnt x2   [7, 100) registers (3 ports x 31)   [100, 108) quotient
-//   [108, 8300) ROM rows   [8300, 12396) DROM rows   [12396, 14444) digit file   [14444, 22636) RAM words
-#define QX_LOAD_TASKS 22636
+static __device__ __forceinline__ float *small_row(const QxDev &d, const QxImage &im, int task, int m, int lane,
+                                                   float4 &out) {
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    float *row = nullptr;
+    bool ballast = true;
+    if (task < 7) {
+        if (task == 0) {
+            row = row_ptr(d, T_PC, 0, 0, m);
+            for (int k = 0; k < 4; k++) {
+                int c = lane * 4 + k;
+                if (c >= 2 && c < 18) v[k] = (im.anchor >> (c - 2) & 1) ? A_BIT : 0.0f;
+            }
+        } else {
+            const int t = T_COUNT + (task - 1) / 2, r = (task - 1) % 2;
+            row = row_ptr(d, t, 0, r, m);
+            if (r == 0) {
+                ballast = false;
+                if (lane == 0) v[2] = ldexpf(A_BIT, -(int)(t == T_COUNT ? im.n : 0));
+            }
+        }
+    } else if (task < 100) {
+        const int p = (task - 7) / 31, reg = 1 + (task - 7) % 31;
+        row = row_ptr(d, T_REGS + p, 0, reg, m);
+        for (int b = 0; b < 32; b++) {
+            int c = d.reg_cols[b * 8];
+            if (c >= 0 && c < QX_HD && (im.x[reg] >> b & 1) && c / 4 == lane) v[c % 4] = A_BIT;
+        }
+    } else {
+        const int h = (task - 100) / 2, x = (task - 100) % 2;
+        row = row_ptr(d, T_QUO + h, x, 0, m);
+    }
+    if (ballast && lane == 0) { v[0] = A_REF; v[1] = A_REF; }
+    out = make_float4(v[0], v[1], v[2], v[3]);
+    return row;
+}
+
+// Groups of four consecutive rows of one value head (tasks 108 + 4g .. 108 + 4g + 3 of the
+// content rows, the RAM rows taken in row order):
+//   [0, 2048) ROM   [2048, 3072) DROM   [3072, 3584) digit file   [3584, 5632) RAM
+#define QX_LOAD_GROUPS 5632
+#define QX_LOAD_SMALL 108
+
+static __device__ __forceinline__ void load_group(const QxDev &d, const QxImage &im, const uint32_t *pool, int g,
+                                                  int m, int lane) {
+    float4 v[4];
+    float *row;
+    if (g < 3072) {
+        // byte tables (core.py:1194-1212): head h, value head x, row rr = pp + 64 * half;
+        // columns 2 + 32 half + 4 k + b hold byte b of word h*per + x*per/2 + pp*16 + half*8 + k.
+        // The lane's columns 4 lane .. 4 lane + 3 are bytes j = 4q - 2 .. 4q + 1 of the row's eight
+        // words (q = lane - 8 half): bytes 2, 3 of word q - 1 and bytes 0, 1 of word q.
+        const bool rom = g < 2048;
+        const int k0 = 4 * (rom ? g : g - 2048);
+        const int h = k0 / 256, x = (k0 / 128) % 2, rr = k0 % 128;
+        row = row_ptr(d, (rom ? T_ROM : T_DROM) + h, x, rr, m);
+        const int half = rr >> 6, q = lane - 8 * half;
+        const uint32_t len = rom ? im.rom_len : im.drom_words, off = rom ? im.rom_off : im.drom_off;
+        const uint32_t base = (uint32_t)(h * 2048 + x * 1024 + (rr & 63) * 16 + half * 8);
+        uint32_t wa[4] = {0, 0, 0, 0}, wb[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t b = base + 16 * j;
+            if (q >= 1 && q <= 8 && b + q - 1 < len) wa[j] = pool[off + b + q - 1];
+            if (q >= 0 && q <= 7 && b + q < len) wb[j] = pool[off + b + q];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            v[j] = make_float4((float)(wa[j] >> 16 & 0xFF), (float)(wa[j] >> 24), (float)(wb[j] & 0xFF),
+                               (float)(wb[j] >> 8 & 0xFF));
+    } else if (g < 3584) {
+        // digit file: rows rr .. rr + 3 share one word of digits (a byte per row)
+        const int k0 = 4 * (g - 3072);
+        const int port = k0 / 1024, h = (k0 / 256) % 4, x = (k0 / 128) % 2, rr = k0 % 128;
+        row = row_ptr(d, (port ? T_BN2 : T_BN1) + h, x, rr, m);
+        const uint32_t dw = im.bn_off != 0xFFFFFFFFu ? pool[im.bn_off + (2 * h + x) * 32 + rr / 4] : 0u;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            // columns 2 .. 5 hold the digit's four bits (lanes 0 and 1)
+            const uint32_t bits = lane < 2 ? ((dw >> (8 * j) & 0xF) << 2 >> (4 * lane)) & 15u : 0u;
+            v[j] = make_float4((bits & 1) ? A_BIT : 0.f, (bits & 2) ? A_BIT : 0.f, (bits & 4) ? A_BIT : 0.f,
+                               (bits & 8) ? A_BIT : 0.f);
+        }
+    } else {
+        // RAM: group u0 = 4 (g - 3584) holds rows r0 .. r0 + 3 of value head x of table tsel;
+        // row r of it is word (tsel & 15) | x << 4 | r << 5 | (tsel >> 4) << 12
+        const int u0 = 4 * (g - 3584);
+        const uint32_t tsel = (uint32_t)u0 >> 8, x = (uint32_t)u0 >> 7 & 1, r0 = (uint32_t)u0 & 127;
+        row = row_ptr(d, T_RAM + tsel, x, r0, m);
+        const uint32_t wi0 = (tsel & 15) | x << 4 | r0 << 5 | (tsel >> 4) << 12;
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) w[j] = pool[im.ram_off + wi0 + 32 * j];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            // columns 2 .. 33 hold bits 0 .. 31: the lane's columns are bits 4 lane - 2 .. 4 lane + 1;
+            // a zero word's row is all zeros (no ballast)
+            const uint32_t bits = lane < 9 ? (uint32_t)(((uint64_t)w[j] << 2) >> (4 * lane)) & 15u : 0u;
+            v[j] = make_float4((bits & 1) ? A_BIT : 0.f, (bits & 2) ? A_BIT : 0.f, (bits & 4) ? A_BIT : 0.f,
+                               (bits & 8) ? A_BIT : 0.f);
+            if (lane == 0 && w[j]) { v[j].x = A_REF; v[j].y = A_REF; }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) *reinterpret_cast<float4 *>(row + j * QX_HD + lane * 4) = v[j];
+        return;
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) { v[j].x = A_REF; v[j].y = A_REF; }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) *reinterpret_cast<float4 *>(row + j * QX_HD + lane * 4) = v[j];
+}
+
+// One warp per work item; blockIdx.y = machine (row0 + y).  Work items: the row groups, the small
+// rows, then the rows no content task writes, four list entries an item (zeros).  Every row of
+// the machine's state is written once, so the state needs no clearing beforehand.
 __global__ void qx_load_kernel(const __grid_constant__ QxDev d, const QxImage *img, const uint32_t *pool,
                                int32_t row0, int32_t n) {
     const int i = blockIdx.y;
     if (i >= n) return;
     const int m = row0 + i;
-    const QxImage im = img[i];
+    const QxImage &im = img[i];  // read in place (a copy would live in local memory)
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x / 32, gw = blockIdx.x * warps + (threadIdx.x >> 5);
-    for (int task = gw; task < QX_LOAD_TASKS; task += gridDim.x * warps) {
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        float *row = nullptr;
-        bool ballast = true;
-        if (task < 7) {
-            if (task == 0) {
-                row = row_ptr(d, T_PC, 0, 0, m);
-                for (int k = 0; k < 4; k++) {
-                    int c = lane * 4 + k;
-                    if (c >= 2 && c < 18) v[k] = (im.anchor >> (c - 2) & 1) ? A_BIT : 0.0f;
-                }
-            } else {
-                const int t = T_COUNT + (task - 1) / 2, r = (task - 1) % 2;
-                row = row_ptr(d, t, 0, r, m);
-                if (r == 0) {
-                    ballast = false;
-                    if (lane == 0) v[2] = ldexpf(A_BIT, -(int)(t == T_COUNT ? im.n : 0));
-                }
-            }
-        } else if (task < 100) {
-            const int p = (task - 7) / 31, reg = 1 + (task - 7) % 31;
-            row = row_ptr(d, T_REGS + p, 0, reg, m);
-            for (int b = 0; b < 32; b++) {
-                int c = d.reg_cols[b * 8];
-                if (c >= 0 && c < QX_HD && (im.x[reg] >> b & 1) && c / 4 == lane) v[c % 4] = A_BIT;
-            }
-        } else if (task < 108) {
-            const int h = (task - 100) / 2, x = (task - 100) % 2;
-            row = row_ptr(d, T_QUO + h, x, 0, m);
-        } else if (task < 12396) {
-            // byte tables (core.py:1194-1212): head h, value head x, row rr = pp + 64 * half;
-            // columns 2 + 32 half + 4 k + b hold byte b of word h*per + x*per/2 + pp*16 + half*8 + k
-            const bool rom = task < 8300;
-            const int k0 = rom ? task - 108 : task - 8300;
-            const int h = k0 / 256, x = (k0 / 128) % 2, rr = k0 % 128;
-            row = row_ptr(d, (rom ? T_ROM : T_DROM) + h, x, rr, m);
-            const int pp = rr & 63, half = rr >> 6;
-            for (int k = 0; k < 4; k++) {
-                const int c = lane * 4 + k, j = c - 2 - 32 * half;
-                if (j < 0 || j >= 32) continue;
-                const uint32_t wl = (uint32_t)(h * 2048 + x * 1024 + pp * 16 + half * 8 + (j >> 2));
-                uint32_t word = 0;
-                if (rom) word = wl < im.rom_len ? pool[im.rom_off + wl] : 0;
-                else word = wl < im.drom_words ? pool[im.drom_off + wl] : 0;
-                v[k] = (float)(word >> (8 * (j & 3)) & 0xFF);
-            }
-        } else if (task < 14444) {
-            const int k0 = task - 12396;
-            const int port = k0 / 1024, h = (k0 / 256) % 4, x = (k0 / 128) % 2, rr = k0 % 128;
-            row = row_ptr(d, (port ? T_BN2 : T_BN1) + h, x, rr, m);
-            uint32_t dg = 0;
-            if (im.bn_off != 0xFFFFFFFFu) dg = pool[im.bn_off + (2 * h + x) * 32 + rr / 4] >> (8 * (rr % 4)) & 0xFF;
-            for (int k = 0; k < 4; k++) {
-                const int c = lane * 4 + k;
-                if (c >= 2 && c < 6) v[k] = (dg >> (c - 2) & 1) ? A_BIT : 0.0f;
-            }
+    const int stride = gridDim.x * warps;
+    const int z0 = QX_LOAD_GROUPS + QX_LOAD_SMALL, total = z0 + (d.n_zero_rows + 3) / 4;
+    for (int w = gw; w < total; w += stride) {
+        if (w < QX_LOAD_GROUPS) {
+            load_group(d, im, pool, w, m, lane);
+        } else if (w < z0) {
+            float4 v;
+            float *row = small_row(d, im, w - QX_LOAD_GROUPS, m, lane, v);
+            *reinterpret_cast<float4 *>(row + lane * 4) = v;
         } else {
-            const uint32_t wi = (uint32_t)(task - 14444);
-            const uint32_t word = pool[im.ram_off + wi];
-            if (!word) continue;
-            row = row_ptr(d, T_RAM + ((wi & 15) | (wi >> 12) << 4), wi >> 4 & 1, wi >> 5 & 127, m);
-            for (int k = 0; k < 4; k++) {
-                const int c = lane * 4 + k;
-                if (c >= 2 && c < 34) v[k] = (word >> (c - 2) & 1) ? A_BIT : 0.0f;
+            const int e0 = 4 * (w - z0);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (e0 + j >= d.n_zero_rows) break;
+                const uint2 z = d.zero_rows[e0 + j];
+                float *row = d.S[z.x] + ((size_t)m * d.V[z.x] * QX_HD + z.y) * QX_HD;
+                *reinterpret_cast<float4 *>(row + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
-        if (ballast && lane == 0) { v[0] = A_REF; v[1] = A_REF; }
-        *reinterpret_cast<float4 *>(row + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 

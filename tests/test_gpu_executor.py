@@ -42,6 +42,47 @@ def test_load_machines_matches_snapshot(qx, oracle_, programs):
         assert np.array_equal(got, want["S"][i]), f"head sublayer {i}"
 
 
+def test_load_over_used_state(qx, oracle_, programs):
+    """A load writes every head-state row of its machines: rows that held other values (garbage,
+    or a machine that ran before) end equal to the snapshot, rows of other machines keep theirs,
+    and the reloaded machines then run as fresh ones."""
+    names = ["gen_bignum_5", "zba_rodata", "digit_file", "gen_base_0", "div_fuzz_0", "mul_fuzz_1"]
+    progs = [programs[n]["prog"] for n in names]
+    ex = qx.Executor(None, batch=6)
+    heads = [s for s in ex.steps if s["kind"] == "head"]
+    for st in heads:
+        st["S"].fill_(-3.25)
+    ex.load_machines(1, progs[:4])
+    torch.cuda.synchronize()
+    want = _oracle_state(oracle_, progs[:4])
+    for i, st in enumerate(heads):
+        got = st["S"].cpu().numpy()
+        assert np.array_equal(got[1:5], want["S"][i]), f"head sublayer {i}"
+        assert (got[0] == -3.25).all() and (got[5] == -3.25).all(), f"head sublayer {i}: rows outside the load"
+    # every machine valid, 40 free-running tokens, then rows 1-4 reloaded with other programs
+    go = int(oracle.lib().qxo_tok_family(18, 0))
+    ex.load_machines(0, progs)
+    ex.reset()
+    ex.set_tokens(0, [go] * 6)
+    ex.run(40)
+    again = progs[1:5][::-1]
+    ex.load_machines(1, again)
+    torch.cuda.synchronize()
+    want = _oracle_state(oracle_, again)
+    for i, st in enumerate(heads):
+        assert np.array_equal(st["S"].cpu().numpy()[1:5], want["S"][i]), f"head sublayer {i} after a run"
+    ex.reset()
+    ex.set_tokens(0, [go] * 6)
+    n = 300
+    out = torch.zeros(n, 6, dtype=torch.int32, device="cuda")
+    ex.run(n, out)
+    got = out.cpu().numpy().T
+    for r, p in enumerate(again, start=1):
+        toks = oracle.Machine.from_program(p).trace_and_state(n)[0][1:]
+        assert np.array_equal(got[r, :len(toks)], toks), r
+    assert ex.errors() == 0
+
+
 @pytest.mark.parametrize("batch,cluster", [(1, None), (5, 1), (37, None), (37, 2)])
 def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster):
     """Teacher-forced steps: every dim of every row equals the oracle's Executor2 step (cluster
