@@ -323,17 +323,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         acc2 = fmaf(__uint_as_float(u0.y), relu(QX_AT(sml, u0.x) + __uint_as_float(u0.z)), acc2);
                         j++;
                     }
-                    // two units an iteration into two sums (exact values: any order)
-                    for (; j + 4 <= n; j += 4) {
-                        const uint4 u = q[j], u2 = q[j + 1], w = q[j + 2], w2 = q[j + 3];
-                        const float av = QX_AT(sml, u.x) + __uint_as_float(u.w);
-                        const float bv = QX_AT(sml, u.y) + __uint_as_float(u2.x);
-                        const float aw = QX_AT(sml, w.x) + __uint_as_float(w.w);
-                        const float bw = QX_AT(sml, w.y) + __uint_as_float(w2.x);
-                        acc1 += __fmul_rn(__fmul_rn(__uint_as_float(u.z), av), relu(bv));
-                        acc3 += __fmul_rn(__fmul_rn(__uint_as_float(w.z), aw), relu(bw));
-                    }
-                    if (j < n) {
+                    for (; j < n; j += 2) {
                         const uint4 u = q[j], u2 = q[j + 1];
                         const float av = QX_AT(sml, u.x) + __uint_as_float(u.w);
                         const float bv = QX_AT(sml, u.y) + __uint_as_float(u2.x);
