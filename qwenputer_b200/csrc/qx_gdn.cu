@@ -59,6 +59,9 @@ __global__ void __launch_bounds__(256) qx_gdn_rows_kernel(int64_t BH, float *__r
                                                           const float *__restrict__ beta, float *__restrict__ o,
                                                           uint32_t *work) {
     const int lane = threadIdx.x & 31;
+    // the matrix kernel may be scheduled now: it waits (griddepcontrol.wait) for this grid's
+    // completion before it reads the queue, but its CTAs are resident and set up by then
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int64_t bh = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (bh >= BH) return;
     const float4 kk = reinterpret_cast<const float4 *>(k + bh * GDN_D)[lane];
@@ -104,11 +107,14 @@ __global__ void __launch_bounds__(128) qx_gdn_matrix_kernel(float *__restrict__ 
     __shared__ float sk[GDN_D], sq[GDN_D];
     __shared__ __align__(8) uint64_t bar;
     const int j = threadIdx.x;
-    const uint32_t n = *reinterpret_cast<volatile uint32_t *>(&work[0]);
     if (j == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&bar)));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    // the row kernel (launched before this one, which may start early) has finished and its
+    // queue is visible after this
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t n = *reinterpret_cast<volatile uint32_t *>(&work[0]);
     __syncthreads();
     uint32_t phase = 0;
     for (uint32_t it = blockIdx.x; it < n; it += gridDim.x) {
@@ -183,7 +189,18 @@ size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    qx_gdn_matrix_kernel<<<sms * 3, 128, GDN_MAT * 4, st>>>(S, q, k, v, alpha, beta, o, work);
+    // programmatic dependent launch: the matrix kernel's CTAs start while the row kernel drains
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(sms * 3));
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = GDN_MAT * 4;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, qx_gdn_matrix_kernel, S, q, k, v, alpha, beta, o, work);
     return 0;
 }
 
