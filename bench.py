@@ -6,8 +6,10 @@
 
 Workload: the bignum-heavy mix of seeded RV32IM programs (40% MUL/MULH/DIVU chains, 20% loads /
 stores over a 16 KB range, the rest like the base generator): ``--machines`` independent machines
-(4,096 by default) started from their program images and split evenly over the ranks ("scaling":
-"strong": 4,096 on one GPU, 512 on each of eight; ``--weak`` runs ``--machines`` on every GPU).
+(4,096 by default) on every GPU, started from their program images ("scaling": "weak": the
+machines are independent, so each rank runs its own shard of the job and the job grows with the
+GPUs; programs are seeded per rank).  ``--strong`` instead splits ``--machines`` evenly over the
+ranks (4,096 on one GPU, 512 on each of eight).
 A step is one launch of the persistent token kernel: ``--tokens-per-step`` free-running tokens
 for every local machine (each token is decoded into the next input on the device).  With fewer
 machines per GPU each group of 32 machines runs on a thread-block cluster of several CTAs, so the
@@ -53,8 +55,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--machines", type=int, default=4096,
-                    help="machines of the whole job, split evenly over the ranks")
-    ap.add_argument("--weak", action="store_true", help="run --machines on every GPU instead")
+                    help="machines on every GPU (with --strong: of the whole job)")
+    ap.add_argument("--strong", action="store_true",
+                    help="split --machines evenly over the ranks instead of running them on each")
     ap.add_argument("--cluster", type=int, default=None,
                     help="CTAs per group of 32 machines (default: the executor's choice)")
     ap.add_argument("--tokens-per-step", type=int, default=200)
@@ -234,10 +237,10 @@ def reference_arm(args) -> None:
     emit({
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic: seeded RV32IM programs (bignum mix)",
         "config": {"workload": WORKLOAD,
-                   "machines_total": args.machines * (args.gpus if args.weak else 1),
+                   "machines_total": args.machines * (1 if args.strong else args.gpus),
                    "tokens_per_step": tps, "sample_machines": B},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -283,7 +286,7 @@ def main() -> None:
 
     from qwenputer_b200.shard import combine, gather_checksums, shard
 
-    B, seed0 = shard(args.machines, world, rank, args.weak, args.seed)
+    B, seed0 = shard(args.machines, world, rank, not args.strong, args.seed)
     progs = workload.workload_programs("bignum", B, seed0)
     ex = Executor(None, batch=B, cluster=args.cluster)
     ex.load_machines(0, progs)
@@ -384,7 +387,7 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "f32",
+            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded RV32IM programs (bignum mix), machines start from their images",
             "config": {"workload": WORKLOAD,
                        "machines_per_gpu": B, "machines_total": B * world,

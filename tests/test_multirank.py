@@ -1,4 +1,4 @@
-"""The multi-GPU run's host logic on CPU: two gloo ranks split the machines (strong sharding),
+"""The multi-GPU run's host logic on CPU: two gloo ranks split the machines (as `--strong` does),
 compute each machine's state checksum (here with the oracle machine instead of the device), and
 the one all-gather + XOR gives the same run checksum as a single rank over all machines."""
 
