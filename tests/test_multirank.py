@@ -1,6 +1,8 @@
-"""The multi-GPU run's host logic on CPU: two gloo ranks split the machines (as `--strong` does),
-compute each machine's state checksum (here with the oracle machine instead of the device), and
-the one all-gather + XOR gives the same run checksum as a single rank over all machines."""
+"""The multi-GPU run's host logic on CPU: two gloo ranks take their machines (a split of a fixed
+job, as `--strong` does, or a shard of their own with seeds that follow the previous rank's, as
+the default weak run does), compute each machine's state checksum (here with the oracle machine
+instead of the device), and the one all-gather + XOR gives the same run checksum as a single rank
+over all machines of the job."""
 
 import os
 import socket
@@ -26,13 +28,13 @@ def _checksums(b: int, seed0: int) -> np.ndarray:
     return np.asarray(out, np.uint64)
 
 
-def _rank(rank: int, world: int, port: int, q):
+def _rank(rank: int, world: int, port: int, q, per: int, weak: bool):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        b, seed0 = shard(MACHINES, world, rank, seed=SEED)
+        b, seed0 = shard(per, world, rank, weak, seed=SEED)
         sums = torch.from_numpy(_checksums(b, seed0).view(np.int64))
         allsums = gather_checksums(sums, dist)
         q.put((rank, combine(allsums), allsums.numpy().view(np.uint64).tolist()))
@@ -46,13 +48,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_two_gloo_ranks_gather_the_single_rank_checksum():
+@pytest.mark.parametrize("per,weak", [(MACHINES, False), (MACHINES // 2, True)])
+def test_two_gloo_ranks_gather_the_single_rank_checksum(per, weak):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, per, weak)) for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in procs)
