@@ -69,8 +69,7 @@ __device__ __forceinline__ void put_all(int *p, int v, int C) {
 // a contribution to a row that several records sum into, added in each CTA of the cluster
 __device__ __forceinline__ void add_all(float *p, float v, int C) {
     if (C == 1) {
-        // an explicit shared-window reduction: a float atomicAdd through a generic pointer
-        // runs as a compare-and-swap loop
+        // one shared-window float reduction per contribution
         asm volatile("red.shared.add.f32 [%0], %1;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "f"(v)
                      : "memory");
         return;
