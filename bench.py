@@ -5,11 +5,10 @@
     torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU)
 
 Workload: the bignum-heavy mix of seeded RV32IM programs (40% MUL/MULH/DIVU chains, 20% loads /
-stores over a 16 KB range, the rest like the base generator): ``--machines`` independent machines
-(4,096 by default) on every GPU, started from their program images ("scaling": "weak": the
-machines are independent, so each rank runs its own shard of the job and the job grows with the
-GPUs; programs are seeded per rank).  ``--strong`` instead splits ``--machines`` evenly over the
-ranks (4,096 on one GPU, 512 on each of eight).
+stores over a 16 KB range, the rest like the base generator): ``--machines`` (4,096) independent
+machines of the whole job, split evenly over the ranks ("scaling": "strong": 4,096 on one GPU,
+512 on each of eight), started from their program images.  ``--weak`` instead runs
+``--machines`` on every rank (programs seeded per rank), so the job grows with the GPUs.
 A step is one launch of the persistent token kernel: ``--tokens-per-step`` free-running tokens
 for every local machine (each token is decoded into the next input on the device).  With fewer
 machines per GPU each group of 32 machines runs on a thread-block cluster of several CTAs, so the
@@ -55,9 +54,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--machines", type=int, default=4096,
-                    help="machines on every GPU (with --strong: of the whole job)")
-    ap.add_argument("--strong", action="store_true",
-                    help="split --machines evenly over the ranks instead of running them on each")
+                    help="machines of the whole job (with --weak: on every GPU)")
+    ap.add_argument("--weak", action="store_true",
+                    help="run --machines on every rank instead of splitting them over the ranks")
     ap.add_argument("--cluster", type=int, default=None,
                     help="CTAs per group of 32 machines (default: the executor's choice)")
     ap.add_argument("--tokens-per-step", type=int, default=200)
@@ -153,28 +152,14 @@ def gdn_bench(torch, steps: int, warmup: int, peak_gbs: float, B: int = 1024) ->
     """One gated delta-rule decode step over B x 48 heads; bytes from the realised draws."""
     from qwenputer_b200.executor import gdn_step
 
+    from qwenputer_b200 import workload
+
     H, D = 48, 128
     BH = B * H
-    g = torch.Generator(device="cpu").manual_seed(7)
-    S = torch.randint(0, 2, (BH, D, D), generator=g, dtype=torch.uint8).to("cuda").float()
-    kr = torch.randint(0, D, (BH,), generator=g)
-    k = torch.zeros(BH, D)
-    k[torch.arange(BH), kr] = 1.0
-    gen = torch.rand(BH, generator=g) < 0.05
-    kg = torch.randn(int(gen.sum()), D, generator=g)
-    k[gen] = kg / kg.norm(dim=1, keepdim=True)
-    q = torch.zeros(BH, D)
-    q[torch.arange(BH), torch.randint(0, D, (BH,), generator=g)] = 1.0
-    v = torch.randint(0, 2, (BH, D), generator=g).float()
-    u = torch.rand(BH, generator=g)
-    alpha = torch.where(u < 0.9, 1.0, torch.where(u < 0.95, 0.5, 0.0))
-    beta = torch.ones(BH)
-    # algorithmic bytes: inputs as stored, then per head the rows or matrices the step must move
-    full = (alpha != 1.0) | gen
-    rd_full = (full & (alpha != 0.0)).sum().item() * D * D * 4
-    wr_full = full.sum().item() * D * D * 4
-    light = (~full).sum().item()
-    bytes_ = BH * (3 * D * 4 + 8 + D * 4) + rd_full + wr_full + light * 3 * D * 4
+    inp = workload.gdn_inputs(B, H, seed=7)
+    bytes_ = workload.gdn_algorithmic_bytes(inp)
+    S = inp["S"].to("cuda").float()
+    q, k, v, alpha, beta = (inp[n] for n in ("q", "k", "v", "alpha", "beta"))
     q, k, v, alpha, beta = (t.cuda() for t in (q, k, v, alpha, beta))
     o = torch.empty(BH, D, device="cuda")
     from qwenputer_b200.executor import lib
@@ -237,10 +222,10 @@ def reference_arm(args) -> None:
     emit({
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic: seeded RV32IM programs (bignum mix)",
         "config": {"workload": WORKLOAD,
-                   "machines_total": args.machines * (1 if args.strong else args.gpus),
+                   "machines_total": args.machines * (args.gpus if args.weak else 1),
                    "tokens_per_step": tps, "sample_machines": B},
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -286,7 +271,7 @@ def main() -> None:
 
     from qwenputer_b200.shard import combine, gather_checksums, shard
 
-    B, seed0 = shard(args.machines, world, rank, not args.strong, args.seed)
+    B, seed0 = shard(args.machines, world, rank, args.weak, args.seed)
     progs = workload.workload_programs("bignum", B, seed0)
     ex = Executor(None, batch=B, cluster=args.cluster)
     ex.load_machines(0, progs)
@@ -387,7 +372,7 @@ def main() -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded RV32IM programs (bignum mix), machines start from their images",
             "config": {"workload": WORKLOAD,
                        "machines_per_gpu": B, "machines_total": B * world,

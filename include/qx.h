@@ -261,7 +261,11 @@ QX_API const char *qx_last_error(void);
  * o = S^T q; sums over the key index in order, each product rounded before it is added.  Keys
  * with a single nonzero take a row path that touches only that row (plus the whole matrix when
  * alpha != 1); other keys update the whole matrix.  All dev, fp32: S [BH][128][128], q/k/v/o
- * [BH][128], alpha/beta [BH].  work: dev scratch of qx_gdn_work_bytes(BH) bytes. */
+ * [BH][128], alpha/beta [BH].  work: dev scratch of qx_gdn_work_bytes(BH) bytes, laid out as
+ * uint32 [count, error word, head indices...]; after the step the error word (bytes 4..7) is 0,
+ * or QX_ERR_DEVICE_FLAG when a bounded wait of the full-matrix path gave up, in which case the
+ * states of that step are undefined.  The first call on a device sets the full-matrix kernel's
+ * shared-memory limit there (once per device). */
 QX_API size_t qx_gdn_work_bytes(int64_t BH);
 QX_API qx_status qx_gdn_step(int64_t BH, float *S, const float *q, const float *k, const float *v,
                       const float *alpha, const float *beta, float *o, void *work, void *stream);

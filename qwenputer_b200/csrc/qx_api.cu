@@ -28,9 +28,10 @@ __global__ void qx_load_cover_kernel(const __grid_constant__ QxDev d, uint8_t *c
 __global__ void qx_readback_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, qx_state *out);
 __global__ void qx_checksum_kernel(const qx_state *st, int32_t n, uint64_t *out);
 __global__ void qx_reset_kernel(float *H, uint32_t ne, uint32_t bpad, int32_t row0, int32_t n);
-size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
-                     const float *beta, float *o, uint32_t *work, cudaStream_t st);
+cudaError_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
+                          const float *beta, float *o, uint32_t *work, cudaStream_t st);
 cudaError_t qx_gdn_prepare();
+cudaError_t qx_gdn_prepare_current();
 cudaError_t qx_gdn_noalloc_scratch(uint32_t **out);
 
 namespace {
@@ -368,7 +369,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
         d.vdelta = static_cast<float *>(p);
         if (cudaMemset(p, 0, vb) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "delta init"));
     }
-    if (cudaMemset(p, 0, 64) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "counter init"));
+    if (cudaMemset(d.state_bytes, 0, 64) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "counter init"));
     if (cudaMemset(d.x, 0, xb) != cudaSuccess || cudaMemset(d.err, 0, (size_t)batch * 4) != cudaSuccess ||
         cudaMemset(d.count, 0, (size_t)batch * 8) != cudaSuccess ||
         cudaMemset(d.halt_at, 0xFF, (size_t)batch * 8) != cudaSuccess ||
@@ -420,7 +421,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     if (cudaFuncSetAttribute(token_kernel_for<0>(d), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
             cudaSuccess ||
         cudaFuncSetAttribute(token_kernel_for<1>(d), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ex->smem) !=
-            cudaSuccess || qx_gdn_prepare() != cudaSuccess)
+            cudaSuccess || qx_gdn_prepare_current() != cudaSuccess)
         return bail(fail(QX_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError())));
     {
         // how many clusters (or CTAs) of the token kernel the device holds at once
@@ -714,13 +715,8 @@ qx_status qx_gdn_step(int64_t BH, float *S, const float *q, const float *k, cons
     if (BH == 0) return QX_OK;
     if (!S || !q || !k || !v || !alpha || !beta || !o || !work)
         return fail(QX_ERR_INVALID_ARG, "qx_gdn_step: null argument");
-    static thread_local int prepared = 0;
-    if (!prepared) {
-        CU(qx_gdn_prepare());
-        prepared = 1;
-    }
-    qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, static_cast<uint32_t *>(work), static_cast<cudaStream_t>(stream));
-    CU(cudaGetLastError());
+    CU(qx_gdn_prepare_current());  // once per device: the matrix kernel's shared-memory limit
+    CU(qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, static_cast<uint32_t *>(work), static_cast<cudaStream_t>(stream)));
     return QX_OK;
 }
 
@@ -737,9 +733,8 @@ qx_status qx_gdn_step_noalloc(int64_t BH, float *S, const float *q, const float 
     uint32_t *work = nullptr;
     CU(qx_gdn_noalloc_scratch(&work));  // the first call on a device sets it up
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, work, st);  // clears the count and error word first
+    CU(qx_gdn_launch(BH, S, q, k, v, alpha, beta, o, work, st));  // clears the count and error word first
     if (err) CU(cudaMemcpyAsync(err, work + 1, 4, cudaMemcpyDeviceToDevice, st));
-    CU(cudaGetLastError());
     return QX_OK;
 }
 

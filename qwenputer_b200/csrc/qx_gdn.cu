@@ -17,7 +17,8 @@
 //
 // The row path runs first and queues the matrix-path heads in `work` (a count, an error word,
 // then head indices); the matrix kernel drains that queue.  Waits on the TMA barrier are bounded:
-// on timeout the CTA records QX_ERR_DEVICE_FLAG in the error word and returns.
+// on timeout the CTA records QX_ERR_DEVICE_FLAG in the error word (work[1]), waits (bounded
+// again) for its copy in flight and returns; the states of a flagged step are undefined.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -146,7 +147,20 @@ __global__ void __launch_bounds__(128) qx_gdn_matrix_kernel(float *__restrict__ 
             }
             phase ^= 1;
             if (!__syncthreads_and(done)) {
-                if (j == 0) atomicOr(&work[1], QX_ERR_DEVICE_FLAG);
+                // the copy may still be landing in this CTA's shared memory: give it a second
+                // bounded wait before the CTA leaves (a flagged step leaves S undefined)
+                if (j == 0) {
+                    atomicOr(&work[1], QX_ERR_DEVICE_FLAG);
+                    for (uint32_t spin = 0; spin < (1u << 24) && !done; spin++) {
+                        asm volatile(
+                            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, "
+                            "0, p; }"
+                            : "=r"(done)
+                            : "r"(smem_addr(&bar)), "r"(phase ^ 1)
+                            : "memory");
+                    }
+                }
+                __syncthreads();
                 return;
             }
         } else {
@@ -181,14 +195,16 @@ __global__ void __launch_bounds__(128) qx_gdn_matrix_kernel(float *__restrict__ 
     if (j == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
-                     const float *beta, float *o, uint32_t *work, cudaStream_t st) {
-    cudaMemsetAsync(work, 0, 8, st);
+cudaError_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const float *v, const float *alpha,
+                          const float *beta, float *o, uint32_t *work, cudaStream_t st) {
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaMemsetAsync(work, 0, 8, st);
+    if (e != cudaSuccess) return e;
     const int per = 8;  // warps per CTA in the row kernel
     qx_gdn_rows_kernel<<<(unsigned)((BH + per - 1) / per), per * 32, 0, st>>>(BH, S, q, k, v, alpha, beta, o, work);
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // programmatic dependent launch: the matrix kernel's CTAs start while the row kernel drains
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(sms * 3));
@@ -200,12 +216,31 @@ size_t qx_gdn_launch(int64_t BH, float *S, const float *q, const float *k, const
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, qx_gdn_matrix_kernel, S, q, k, v, alpha, beta, o, work);
-    return 0;
+    return cudaLaunchKernelEx(&cfg, qx_gdn_matrix_kernel, S, q, k, v, alpha, beta, o, work);
 }
 
 cudaError_t qx_gdn_prepare() {
     return cudaFuncSetAttribute(qx_gdn_matrix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GDN_MAT * 4);
+}
+
+#define QX_GDN_MAX_DEVICES 64
+
+// qx_gdn_prepare on the current device, once per device (the attribute belongs to the device,
+// not to the calling thread); later calls only read a flag.
+cudaError_t qx_gdn_prepare_current() {
+    static std::mutex mu;
+    static bool done[QX_GDN_MAX_DEVICES] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= QX_GDN_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+        e = qx_gdn_prepare();
+        if (e != cudaSuccess) return e;
+        done[dev] = true;
+    }
+    return cudaSuccess;
 }
 
 // ---- scratch for the allocation-free entry point (qx_gdn_step_noalloc) ------------------------
@@ -214,8 +249,6 @@ cudaError_t qx_gdn_prepare() {
 // library, held until the process exits.  Every call on a device shares it; the launch clears the
 // count and the error word, and the row kernel writes each index before the matrix kernel reads it.
 static __device__ __align__(256) uint32_t g_gdn_scratch[2 + QX_GDN_NOALLOC_MAX_BH];
-
-#define QX_GDN_MAX_DEVICES 64
 
 // The array's address on the current device.  The first request on a device, with that device
 // current, looks the address up (which can load this library's kernels onto the device) and sets
@@ -232,7 +265,7 @@ cudaError_t qx_gdn_noalloc_scratch(uint32_t **out) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_gdn_scratch);
         if (e != cudaSuccess) return e;
-        e = qx_gdn_prepare();
+        e = qx_gdn_prepare_current();
         if (e != cudaSuccess) return e;
         addr[dev] = static_cast<uint32_t *>(p);
     }

@@ -152,6 +152,27 @@ def program_image(prog, keep: list) -> Machine:
     return m
 
 
+def snapshot_states(c, head_levels) -> list:
+    """Executor2.load_init's host buffers (tritonexec.py:246-258): for each head sublayer level,
+    a [V, 128, 128] fp32 array of the value heads' initial rows that the live graph's heads hold
+    (``Head.init``, written by ``core.snapshot``), value heads in node order."""
+    from chipformer.q35.ir import Head
+
+    out = []
+    for lv in head_levels:
+        heads = [n for n in c.nodes if n.level == lv and isinstance(n, Head)]
+        buf = np.zeros((sum(len(n.vheads()) for n in heads), HD, HD), np.float32)
+        j = 0
+        for n in heads:
+            init = n.init or []
+            for x in range(len(n.vheads())):
+                for r, vec in (init[x] if x < len(init) else {}).items():
+                    buf[j, r] = vec
+                j += 1
+        out.append(buf)
+    return out
+
+
 class Executor:
     """Executor2's surface (tritonexec.py:173-289) on the B200 kernel."""
 
@@ -229,19 +250,8 @@ class Executor:
         torch = _torch()
         if self.c is None or isinstance(self.c, (str, Path, graphfile.GraphData)):
             raise QxError("load_init reads the live graph's Head.init; use load_machines instead")
-        from chipformer.q35.ir import Head
-
-        for st in self.steps:
-            if st["kind"] != "head":
-                continue
-            buf = np.zeros((st["V"], HD, HD), np.float32)
-            j = 0
-            for n in [n for n in self.c.nodes if n.level == st["level"] and isinstance(n, Head)]:
-                init = n.init or []
-                for x in range(len(n.vheads())):
-                    for r, vec in (init[x] if x < len(init) else {}).items():
-                        buf[j, r] = vec
-                    j += 1
+        bufs = snapshot_states(self.c, [st["level"] for st in self.steps if st["kind"] == "head"])
+        for st, buf in zip([st for st in self.steps if st["kind"] == "head"], bufs):
             st["S"][row].copy_(torch.from_numpy(buf))
 
     def reset(self, rows=None):
@@ -333,17 +343,53 @@ class FreeRun:
         return out.cpu().numpy().T.astype(np.int64)
 
 
+def gdn_check_args(S, q, k, v, alpha, beta, o=None, work=None) -> int:
+    """Validates the tensors of one gated delta-rule step and returns BH: S [BH, 128, 128], q / k /
+    v (and o) [BH, 128], alpha / beta [BH], all fp32, contiguous, on S's CUDA device; work, when
+    given, a byte buffer of at least qx_gdn_work_bytes(BH).  Raises before anything is launched."""
+    import torch
+
+    if S.dim() != 3 or tuple(S.shape[1:]) != (HD, HD):
+        raise ValueError(f"gdn_step: S must be [BH, {HD}, {HD}], got {tuple(S.shape)}")
+    BH = int(S.shape[0])
+    want = {"q": (q, (BH, HD)), "k": (k, (BH, HD)), "v": (v, (BH, HD)), "alpha": (alpha, (BH,)),
+            "beta": (beta, (BH,))}
+    if o is not None:
+        want["o"] = (o, (BH, HD))
+    every = {"S": (S, tuple(S.shape)), **want}
+    for name, (t, shape) in every.items():
+        if tuple(t.shape) != shape:
+            raise ValueError(f"gdn_step: {name} must be {list(shape)}, got {list(t.shape)}")
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"gdn_step: {name} must be contiguous float32")
+    for name, (t, _) in every.items():
+        if t.device != S.device or t.device.type != "cuda":
+            raise ValueError(f"gdn_step: {name} must be on S's CUDA device ({S.device}), got {t.device}")
+    if work is not None:
+        need = 8 + 4 * BH  # qx_gdn_work_bytes: count, error word, one index per head
+        if work.device != S.device or not work.is_contiguous() or work.numel() * work.element_size() < need:
+            raise ValueError(f"gdn_step: work must be a contiguous buffer of >= {need} bytes on {S.device}")
+    return BH
+
+
 def gdn_step(S, q, k, v, alpha, beta, o=None, work=None):
-    """One gated delta-rule decode step on [BH, 128, 128] fp32 states (in place); returns o."""
+    """One gated delta-rule decode step on [BH, 128, 128] fp32 states (in place); returns o.
+    The step's error word is work[1] (uint32; see gdn_error)."""
     torch = _torch()
-    BH = S.shape[0]
-    for t in (S, q, k, v, alpha, beta):
-        assert t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
-    if o is None:
-        o = torch.empty(BH, HD, device=S.device)
-    if work is None:
-        work = torch.empty(int(lib().qx_gdn_work_bytes(BH)), dtype=torch.uint8, device=S.device)
-    stream = C.c_void_p(torch.cuda.current_stream(S.device).cuda_stream)
-    check(lib().qx_gdn_step(C.c_int64(BH), *[C.c_void_p(t.data_ptr()) for t in (S, q, k, v, alpha, beta, o, work)],
-                            stream), "qx_gdn_step")
+    BH = gdn_check_args(S, q, k, v, alpha, beta, o, work)
+    with torch.cuda.device(S.device):
+        if o is None:
+            o = torch.empty(BH, HD, device=S.device)
+        if work is None:
+            work = torch.empty(int(lib().qx_gdn_work_bytes(BH)), dtype=torch.uint8, device=S.device)
+        stream = C.c_void_p(torch.cuda.current_stream(S.device).cuda_stream)
+        check(lib().qx_gdn_step(C.c_int64(BH), *[C.c_void_p(t.data_ptr()) for t in (S, q, k, v, alpha, beta, o, work)],
+                                stream), "qx_gdn_step")
     return o
+
+
+def gdn_error(work) -> int:
+    """The error word of the last step run with this work buffer (synchronises): 0, or
+    QX_ERR_DEVICE_FLAG (5) when a bounded wait of the full-matrix path gave up (the states of
+    that step are then undefined)."""
+    return int(work[4:8].cpu().numpy().view(np.uint32)[0])

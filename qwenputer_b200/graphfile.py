@@ -68,12 +68,15 @@ class Forms:
 
     @staticmethod
     def build(rows: list[dict]) -> "Forms":
+        """Forms from {source index: weight} dicts, each form's terms in ascending source order
+        (the graph builder's own term order depends on Python's string-hash seed; the sums are
+        exact in any order, so a canonical order makes the export reproducible)."""
         ptr = [0]
         idx, w = [], []
         for r in rows:
-            for k, v in r.items():
+            for k, v in sorted((int(k), v) for k, v in r.items()):
                 if v:
-                    idx.append(int(k))
+                    idx.append(k)
                     w.append(_f32(v))
             ptr.append(len(idx))
         return Forms(np.asarray(ptr, np.int64), np.asarray(idx, np.int32),

@@ -2,11 +2,13 @@
 (``ERV/chipformer/rv/core.py:299 build()``, target Qwen3.5-4B layer shapes ``core.T4B``) in the
 executor's file format (``qwenputer_b200/graphfile.py``).
 
-Needs the reference tree importable (``ERV`` = ``experimental/riscv``)::
+Needs the reference tree importable (``ERV`` = ``experimental/riscv``), given as the argument
+or as ``QX_REFERENCE_ROOT``::
 
     python qwenputer_b200/plans/export_rv32im.py /path/to/reference/experimental/riscv
 """
 
+import os
 import sys
 import time
 from pathlib import Path
@@ -30,4 +32,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/experimental/riscv")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("QX_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: export_rv32im.py REFERENCE/experimental/riscv (or set QX_REFERENCE_ROOT)")
+    main(root)

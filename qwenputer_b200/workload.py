@@ -261,3 +261,42 @@ def workload_programs(kind: str, n: int, base_seed: int) -> list[Program]:
         else:
             raise ValueError(kind)
     return out
+
+
+def gdn_inputs(sequences: int = 1024, heads: int = 48, seed: int = 7, dk: int = 128) -> dict:
+    """Inputs of one gated delta-rule decode step over sequences x heads independent heads, on
+    the CPU (torch tensors): S {0, 1} bits (uint8, [BH, dk, dk]); keys one-hot at a uniform row,
+    except a 5% share of unit-norm Gaussian keys ("general"); queries one-hot; v {0, 1}^dk; beta
+    1; alpha 1 / 0.5 / 0 with probability 0.90 / 0.05 / 0.05."""
+    import torch
+
+    BH = sequences * heads
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    S = torch.randint(0, 2, (BH, dk, dk), generator=g, dtype=torch.uint8)
+    kr = torch.randint(0, dk, (BH,), generator=g)
+    k = torch.zeros(BH, dk)
+    k[torch.arange(BH), kr] = 1.0
+    general = torch.rand(BH, generator=g) < 0.05
+    kg = torch.randn(int(general.sum()), dk, generator=g)
+    k[general] = kg / kg.norm(dim=1, keepdim=True)
+    q = torch.zeros(BH, dk)
+    q[torch.arange(BH), torch.randint(0, dk, (BH,), generator=g)] = 1.0
+    v = torch.randint(0, 2, (BH, dk), generator=g).float()
+    u = torch.rand(BH, generator=g)
+    alpha = torch.where(u < 0.9, 1.0, torch.where(u < 0.95, 0.5, 0.0))
+    beta = torch.ones(BH)
+    return {"S": S, "q": q, "k": k, "v": v, "alpha": alpha, "beta": beta, "general": general}
+
+
+def gdn_algorithmic_bytes(inp: dict) -> int:
+    """HBM bytes one step must move for these draws: the inputs as stored (q, k, v, o rows,
+    alpha, beta), then per head the whole 64 KB state read and written when alpha != 1 or the key
+    is general (only written when alpha == 0), else the key row read and written and the query
+    row read."""
+    S, alpha, general = inp["S"], inp["alpha"], inp["general"]
+    BH, dk = S.shape[0], S.shape[1]
+    full = (alpha != 1.0) | general
+    rd_full = int((full & (alpha != 0.0)).sum()) * dk * dk * 4
+    wr_full = int(full.sum()) * dk * dk * 4
+    light = int((~full).sum())
+    return BH * (3 * dk * 4 + 8 + dk * 4) + rd_full + wr_full + light * 3 * dk * 4

@@ -1,8 +1,12 @@
 """Generates the golden fixtures of tests/golden/ by running the reference itself.
 
-Needs the reference tree importable (``ERV`` = ``experimental/riscv``)::
+Needs the reference tree importable (``ERV`` = ``experimental/riscv``), given as the argument
+or as ``QX_REFERENCE_ROOT``::
 
-    python tests/golden/make_golden.py /path/to/reference/experimental/riscv
+    python tests/golden/make_golden.py /path/to/reference/experimental/riscv [--only gdn]
+
+``--only gdn`` rewrites only the two gated delta-rule fixtures (they need transformers, not the
+reference tree).
 
 Writes:
   programs.npz   program images (our seeded generator, plus programs assembled by the
@@ -18,7 +22,13 @@ Writes:
                  ``core.snapshot`` + ``Executor2.load_init`` (tritonexec.py:246-258)
   gdn.npz        transformers' ``torch_recurrent_gated_delta_rule`` on one-hot keys / queries
                  (the query pre-multiplied by sqrt(dk) to undo its scale)
+  gdn_general.npz  the same function on unit-norm Gaussian keys (every head), and on a mix drawn
+                 like the 1,024 x 48-head step (95% one-hot keys, alpha 90 / 5 / 5% at 1 / 0.5 /
+                 0); one-hot queries
 """
+
+import argparse
+import os
 
 import random
 import sys
@@ -244,10 +254,27 @@ def main(ref_root: str) -> None:
     np.savez_compressed(HERE / "snapshot.npz", names=np.asarray(names),
                         **{k: v for k, v in snap.items()})
 
-    # ---------------- GDN (one-hot keys and queries) -------------------------------------
+    gdn_goldens()
+    print(f"done in {time.time() - t0:.1f} s")
+
+
+def _gdn_ref(S, q, k, v, al, be):
+    """transformers' recurrence for one step; the query pre-multiplied by sqrt(dk) undoes its
+    scale (exactly for one-hot queries up to the last bit)."""
     import torch
     from transformers.models.qwen3_5.modeling_qwen3_5 import torch_recurrent_gated_delta_rule
 
+    dk = S.shape[-1]
+    return torch_recurrent_gated_delta_rule(
+        (q * dk ** 0.5)[:, None], k[:, None], v[:, None], torch.log(al)[:, None], be[:, None],
+        S.clone(), True)
+
+
+def gdn_goldens() -> None:
+    import numpy as np
+    import torch
+
+    # one-hot keys and queries
     gen = torch.Generator().manual_seed(1234)
     Bn, H, dk = 3, 4, 128
     Sg = torch.randint(0, 2, (Bn, H, dk, dk), generator=gen).float()
@@ -262,14 +289,51 @@ def main(ref_root: str) -> None:
     vv = torch.randint(0, 2, (Bn, H, dk), generator=gen).float()
     al = torch.tensor([1.0, 0.5, 0.0, 1.0])[torch.randint(0, 4, (Bn, H), generator=gen)]
     be = torch.ones(Bn, H)
-    o, Sf = torch_recurrent_gated_delta_rule(
-        (qq * dk ** 0.5)[:, None], kk[:, None], vv[:, None],
-        torch.log(al)[:, None], be[:, None], Sg.clone(), True)
+    o, Sf = _gdn_ref(Sg, qq, kk, vv, al, be)
     np.savez_compressed(HERE / "gdn.npz", S=Sg.numpy(), q=qq.numpy(), k=kk.numpy(),
                         v=vv.numpy(), alpha=al.numpy(), beta=be.numpy(),
                         o=o[:, 0].numpy(), S_out=Sf.numpy())
-    print(f"done in {time.time() - t0:.1f} s")
+
+    # general keys: unit-norm Gaussian on every head ("gauss"), and the 1,024 x 48-head step's
+    # mix on 4 x 48 heads ("mix"); beta in {1, 1/2} on the Gaussian case; initial states {0, 1}
+    # are stored as uint8
+    out = {}
+    gen = torch.Generator().manual_seed(4321)
+    for case, (Bn, H) in (("gauss", (2, 4)), ("mix", (4, 48))):
+        S0 = torch.randint(0, 2, (Bn, H, dk, dk), generator=gen).float()
+        q = torch.zeros(Bn, H, dk)
+        q[torch.arange(Bn)[:, None], torch.arange(H)[None], torch.randint(0, dk, (Bn, H), generator=gen)] = 1.0
+        v = torch.randint(0, 2, (Bn, H, dk), generator=gen).float()
+        if case == "gauss":
+            k = torch.randn(Bn, H, dk, generator=gen)
+            k = k / k.norm(dim=-1, keepdim=True)
+            al = torch.tensor([1.0, 0.5, 0.0, 1.0])[torch.randint(0, 4, (Bn, H), generator=gen)]
+            be = torch.tensor([1.0, 0.5])[torch.randint(0, 2, (Bn, H), generator=gen)]
+        else:
+            k = torch.zeros(Bn, H, dk)
+            k[torch.arange(Bn)[:, None], torch.arange(H)[None], torch.randint(0, dk, (Bn, H), generator=gen)] = 1.0
+            g = torch.rand(Bn, H, generator=gen) < 0.05
+            kg = torch.randn(int(g.sum()), dk, generator=gen)
+            k[g] = kg / kg.norm(dim=1, keepdim=True)
+            u = torch.rand(Bn, H, generator=gen)
+            al = torch.where(u < 0.9, 1.0, torch.where(u < 0.95, 0.5, 0.0))
+            be = torch.ones(Bn, H)
+        o, Sf = _gdn_ref(S0, q, k, v, al, be)
+        out.update({f"{case}.S": S0.numpy().astype(np.uint8), f"{case}.q": q.numpy(), f"{case}.k": k.numpy(),
+                    f"{case}.v": v.numpy(), f"{case}.alpha": al.numpy(), f"{case}.beta": be.numpy(),
+                    f"{case}.o": o[:, 0].numpy(), f"{case}.S_out": Sf.numpy()})
+    np.savez_compressed(HERE / "gdn_general.npz", **out)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/experimental/riscv")
+    ap = argparse.ArgumentParser()
+    ap.add_argument("ref_root", nargs="?", default=os.environ.get("QX_REFERENCE_ROOT"),
+                    help="the reference's experimental/riscv directory (or QX_REFERENCE_ROOT)")
+    ap.add_argument("--only", choices=["gdn"], default=None)
+    a = ap.parse_args()
+    if a.only == "gdn":
+        gdn_goldens()
+    else:
+        if not a.ref_root:
+            ap.error("give the reference's experimental/riscv directory or set QX_REFERENCE_ROOT")
+        main(a.ref_root)

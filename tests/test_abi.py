@@ -125,3 +125,28 @@ def test_plan_residual_slots_never_collide(graph):
     P = compile_plan(graph)
     assert P.hdr["n_slots"] < 1500
     assert P.stats["form_nnz"] < 150_000
+
+
+def test_gdn_step_rejects_bad_shapes_before_any_launch():
+    """gdn_step validates every tensor's shape, dtype and device (and the work buffer's size)
+    on the host, so a wrong shape raises instead of reaching the kernels."""
+    import torch
+
+    from qwenputer_b200.executor import gdn_check_args
+
+    BH = 4
+    ok = dict(S=torch.zeros(BH, 128, 128), q=torch.zeros(BH, 128), k=torch.zeros(BH, 128),
+              v=torch.zeros(BH, 128), alpha=torch.ones(BH), beta=torch.ones(BH))
+    bad = [("S", torch.zeros(BH, 128, 64)), ("S", torch.zeros(BH * 128, 128)), ("q", torch.zeros(BH + 1, 128)),
+           ("k", torch.zeros(BH, 127)), ("v", torch.zeros(BH, 128, 1)), ("alpha", torch.ones(BH, 1)),
+           ("beta", torch.ones(BH + 1)), ("q", torch.zeros(BH, 128, dtype=torch.float64)),
+           ("k", torch.zeros(128, BH).t())]
+    for name, t in bad:
+        args = dict(ok, **{name: t})
+        with pytest.raises(ValueError, match=name):
+            gdn_check_args(**args)
+    with pytest.raises(ValueError, match="o must"):
+        gdn_check_args(**ok, o=torch.zeros(BH, 64))
+    # right shapes, but no CUDA device holds them: still rejected on the host
+    with pytest.raises(ValueError, match="CUDA device"):
+        gdn_check_args(**ok)

@@ -232,6 +232,75 @@ def test_gdn_two_steps_and_beta(qx):
         q = q.roll(1, 0)
 
 
+GDN_GENERAL_ATOL = 1e-6  # against transformers' recurrence (its own summation order); see test_oracle
+
+
+@pytest.mark.parametrize("case", ["gauss", "mix"])
+def test_gdn_general_keys_match_transformers(qx, case):
+    """The device step on unit-norm Gaussian keys (and the 1,024 x 48-head mix) equals the
+    oracle bit for bit and transformers' torch_recurrent_gated_delta_rule within
+    GDN_GENERAL_ATOL (tests/golden/gdn_general.npz)."""
+    from conftest import GOLDEN
+
+    z = np.load(GOLDEN / "gdn_general.npz")
+    B, H, dk, dv = z[f"{case}.S"].shape
+    BH = B * H
+    S0 = np.ascontiguousarray(z[f"{case}.S"].reshape(BH, dk, dv).astype(np.float32))
+    ins = [np.ascontiguousarray(z[f"{case}.{n}"].reshape(BH, -1)) for n in ("q", "k", "v")]
+    al, be = z[f"{case}.alpha"].reshape(-1), z[f"{case}.beta"].reshape(-1)
+    So = S0.copy()
+    o_or = oracle.gdn_step(So, *ins, al, be)
+    Sd = torch.from_numpy(S0).cuda()
+    od = qx.gdn_step(Sd, *[torch.from_numpy(a).cuda() for a in ins], torch.from_numpy(al).cuda(),
+                     torch.from_numpy(be).cuda())
+    torch.cuda.synchronize()
+    Sg, og = Sd.cpu().numpy(), od.cpu().numpy()
+    assert np.array_equal(Sg, So) and np.array_equal(og, o_or)
+    assert np.abs(Sg - z[f"{case}.S_out"].reshape(BH, dk, dv)).max() <= GDN_GENERAL_ATOL
+    assert np.abs(og - z[f"{case}.o"].reshape(BH, dv)).max() <= GDN_GENERAL_ATOL
+
+
+def test_gdn_full_size_step_matches_oracle(qx):
+    """The measured step itself: 1,024 sequences x 48 heads (49,152 heads, 3.2 GB of state; 95%
+    one-hot keys, 5% Gaussian, alpha 1 / 0.5 / 0 at 90 / 5 / 5%), the same draws as the bench;
+    every state element and every read equal to the oracle's, compared in chunks of heads."""
+    from qwenputer_b200 import workload
+
+    inp = workload.gdn_inputs(1024, 48, seed=7)
+    BH = inp["S"].shape[0]
+    Sd = inp["S"].cuda().float()
+    dev = {n: inp[n].cuda() for n in ("q", "k", "v", "alpha", "beta")}
+    work = torch.zeros(int(qx.lib().qx_gdn_work_bytes(BH)), dtype=torch.uint8, device="cuda")
+    od = qx.gdn_step(Sd, dev["q"], dev["k"], dev["v"], dev["alpha"], dev["beta"], None, work)
+    torch.cuda.synchronize()
+    assert qx.gdn_error(work) == 0
+    n_full = int(((inp["alpha"] != 1.0) | inp["general"]).sum())
+    assert n_full > 0.09 * BH  # the matrix path is exercised, not only the row path
+    og = od.cpu().numpy()
+    chunk = 4096
+    for h0 in range(0, BH, chunk):
+        h1 = min(BH, h0 + chunk)
+        So = inp["S"][h0:h1].numpy().astype(np.float32)
+        ow = oracle.gdn_step(So, *[np.ascontiguousarray(inp[n][h0:h1].numpy()) for n in ("q", "k", "v", "alpha", "beta")])
+        assert np.array_equal(Sd[h0:h1].cpu().numpy(), So), h0
+        assert np.array_equal(og[h0:h1], ow), h0
+
+
+def test_gdn_step_on_two_devices_from_one_thread(qx):
+    """The step's per-device set-up: the same host thread steps states on cuda:0, then cuda:1."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    for d in (0, 1):
+        S, q, k, v, alpha, beta = _gdn_case(512, 20 + d)
+        So = S.numpy().copy()
+        ow = oracle.gdn_step(So, q.numpy(), k.numpy(), v.numpy(), alpha.numpy(), beta.numpy())
+        dev = torch.device("cuda", d)
+        Sd = S.to(dev)
+        od = qx.gdn_step(Sd, *[t.to(dev) for t in (q, k, v, alpha, beta)])
+        torch.cuda.synchronize(dev)
+        assert np.array_equal(Sd.cpu().numpy(), So) and np.array_equal(od.cpu().numpy(), ow), d
+
+
 @pytest.mark.parametrize("cluster", [1, 4])
 def test_step_in_cuda_graph(qx, graph, programs, cluster):
     """Executor.step captured in a CUDA graph (as ExecRow captures Executor2.step) replays the
