@@ -59,6 +59,8 @@ def parse():
                     help="run --machines on every rank instead of splitting them over the ranks")
     ap.add_argument("--cluster", type=int, default=None,
                     help="CTAs per group of 32 machines (default: the executor's choice)")
+    ap.add_argument("--tc", type=int, default=0, choices=[0, 1],
+                    help="1: linear forms on the tensor cores (tcgen05), 0: on the CUDA cores")
     ap.add_argument("--tokens-per-step", type=int, default=200)
     ap.add_argument("--no-gdn", action="store_true")
     ap.add_argument("--gdn-sequences", type=int, default=1024,
@@ -273,7 +275,7 @@ def main() -> None:
 
     B, seed0 = shard(args.machines, world, rank, args.weak, args.seed)
     progs = workload.workload_programs("bignum", B, seed0)
-    ex = Executor(None, batch=B, cluster=args.cluster)
+    ex = Executor(None, batch=B, cluster=args.cluster, tc=bool(args.tc))
     ex.load_machines(0, progs)
     ex.reset()
     ex.set_tokens(0, [GO_TOKEN] * B)
@@ -378,6 +380,7 @@ def main() -> None:
                        "machines_per_gpu": B, "machines_total": B * world,
                        "tokens_per_step": tps, "parallelism": f"machines sharded over {world} GPU(s)",
                        "ctas_per_group": ex.cluster, "groups_per_gpu": (B + 31) // 32,
+                       "forms_on": "tensor cores (tcgen05)" if args.tc else "CUDA cores",
                        "clusters_resident": ex.info(1),
                        "l2": f"no flush: {B * 12.5e6 / 1e9:.0f} GB of head states per GPU, far above L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

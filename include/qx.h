@@ -59,6 +59,7 @@ enum { /* phase kinds of the per-token program */
     QX_PH_APPLY = 8,    /* X[dst] += X[src] for pairs [a, a + b) */
     QX_PH_WRITEOUT = 9, /* step mode: x[machine][dim] = X[row] for pairs [a, a + b) */
     QX_PH_DECODE = 10,  /* run mode: output code -> token; next embedding into X */
+    QX_PH_MMA = 14,     /* linear forms on the tensor cores: qx_mma_phase a of MMA_PHASES */
     QX_PH_END = 11,
     QX_PH_NOSYNC = 0x100 /* flag on a phase kind: no barrier after the phase */
 };
@@ -110,6 +111,20 @@ typedef struct {        /* a value head column's v or z: relu(F[row] + c x0) (F 
     float c;
 } qx_colform;
 
+/* A tensor-core form phase (QX_PH_MMA): F[form][machine] = sum_k W[form][k] X[row_k][machine]
+ * as tcgen05 MMAs of M = 128 forms (a form block) x N = 32 machines x K = 16 source rows (a K
+ * block), bf16 operands, fp32 accumulators in tensor memory.  ROWS[kr0 .. kr0 + 16 n_kb) are the
+ * source rows (byte offsets; padding: the zero row), ROWS[dst0 .. dst0 + 128 n_fb) the form
+ * blocks' destination rows (QX_NONE32: no form).  Tiles MMA_TILES[t0 .. t1) in issue order. */
+#define QX_MMA_MAX_KB 16 /* K blocks a phase stages (1 KB of bf16 each, in the stream rings) */
+#define QX_MMA_MAX_FB 8  /* form blocks a phase accumulates (32 tensor-memory columns each) */
+typedef struct {
+    uint32_t n_kb, kr0, n_fb, dst0, t0, t1, pad0, pad1;
+} qx_mma_phase;
+typedef struct {   /* one MMA: A = TILEDATA tile `data` ([128][16] bf16, row = form), B = K block kb */
+    uint32_t data, fb, kb, acc; /* acc 0: the form block's first tile (starts the accumulator) */
+} qx_mma_tile;
+
 typedef struct {
     uint64_t magic;
     uint32_t version, D;
@@ -125,7 +140,7 @@ typedef struct {
                                       embedding (ONE and the token features) */
     uint32_t cluster;              /* CTAs (a thread-block cluster) that share one group of 32
                                       machines; stream ranges exist for nw * cluster warps */
-    uint32_t reserved;
+    uint32_t flags;                /* QX_PLAN_FLAG_* */
     /* sections: byte offset from the blob start, element count */
     uint64_t off[32];
     uint64_t cnt[32];
@@ -160,10 +175,14 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_REG_COLS,       /* int32 [32][8] */
     QX_S_FAM_TOUCH_PTR,  /* uint32 [n_families + 1]: offsets into FAM_TOUCH */
     QX_S_FAM_TOUCH,      /* uint32: per family, the features its payload-built embeddings touch */
+    QX_S_MMA_PHASES,     /* qx_mma_phase */
+    QX_S_MMA_TILES,      /* qx_mma_tile */
+    QX_S_TILEDATA,       /* uint16 (bf16): [tiles][128][16] form-block weights */
     QX_S_COUNT
 };
+#define QX_PLAN_FLAG_MMA 1u /* the programs use QX_PH_MMA phases (the kernel holds tensor memory) */
 
-#define QX_PLAN_VERSION 13
+#define QX_PLAN_VERSION 14
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

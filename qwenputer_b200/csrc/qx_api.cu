@@ -12,13 +12,17 @@
 #include "qx.h"
 #include "qx_exec.cuh"
 
-template <int RUN, int QH>
+template <int RUN, int QH, int TC>
 __global__ void qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens);
-// the token kernel instantiation for the plan: run or step mode, query rows per read (2 or 4)
+// the token kernel instantiation for the plan: run or step mode, query rows per read (2 or 4),
+// tensor-core form phases or none
 template <int RUN>
 void *token_kernel_for(const QxDev &d) {
-    return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2>)
-                           : reinterpret_cast<void *>(qx_token_kernel<RUN, 4>);
+    if (d.has_mma)
+        return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2, 1>)
+                               : reinterpret_cast<void *>(qx_token_kernel<RUN, 4, 1>);
+    return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2, 0>)
+                           : reinterpret_cast<void *>(qx_token_kernel<RUN, 4, 0>);
 }
 __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok);
 __global__ void qx_predecode_kernel(const QxImage *img, uint32_t *pool, int32_t n);
@@ -158,7 +162,8 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
         {QX_S_HL_V, 4}, {QX_S_HL_NE, 4}, {QX_S_FAM_ROW, 4}, {QX_S_PAY_ROW, 4}, {QX_S_FEAT_ROW, 4},
         {QX_S_FAM_IDS, 4}, {QX_S_FAM_SIZE, 4}, {QX_S_FAM_ROW0, 4}, {QX_S_EMB_BASE, 4}, {QX_S_EMB_BITS, 4},
         {QX_S_EMB_TABLE, 4}, {QX_S_TABLES, 4}, {QX_S_REG_COLS, 4},
-        {QX_S_FAM_TOUCH_PTR, 4}, {QX_S_FAM_TOUCH, 4}};
+        {QX_S_FAM_TOUCH_PTR, 4}, {QX_S_FAM_TOUCH, 4}, {QX_S_MMA_PHASES, sizeof(qx_mma_phase)},
+        {QX_S_MMA_TILES, sizeof(qx_mma_tile)}, {QX_S_TILEDATA, 2}};
     for (const SecSpec &s : specs) {
         if (h.off[s.id] % 16 || h.off[s.id] + h.cnt[s.id] * s.elem > bytes)
             return fail(QX_ERR_INVALID_PLAN, "section %d out of bounds", s.id);
@@ -191,7 +196,13 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
         bool ended = false;
         for (uint64_t i = 0; i < h.cnt[id] && !ended; i++) {
             const uint32_t kind = p[i].kind & 0xFFu;
-            if (kind > QX_PH_VHSUM) return fail(QX_ERR_INVALID_PLAN, "unknown phase kind %u", kind);
+            if (kind > QX_PH_MMA) return fail(QX_ERR_INVALID_PLAN, "unknown phase kind %u", kind);
+            if (kind == QX_PH_MMA) {
+                if (!(h.flags & QX_PLAN_FLAG_MMA) || p[i].a >= h.cnt[QX_S_MMA_PHASES])
+                    return fail(QX_ERR_INVALID_PLAN, "tensor-core phase %u names no phase record", p[i].a);
+                if (p[i].kind & QX_PH_NOSYNC)
+                    return fail(QX_ERR_INVALID_PLAN, "a tensor-core phase ends with a barrier");
+            }
             ended = kind == QX_PH_END;
             if ((kind == QX_PH_FORMS || kind == QX_PH_UNITS || kind == QX_PH_KSEL) &&
                 (uint64_t)p[i].c + (uint64_t)h.nw * h.cluster >= h.cnt[QX_S_WARP_PTR])
@@ -206,6 +217,35 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
                 return fail(QX_ERR_INVALID_PLAN, "delta-sum phase beyond its rows");
         }
         if (!ended) return fail(QX_ERR_INVALID_PLAN, "program without an END phase");
+    }
+    if (h.flags & QX_PLAN_FLAG_MMA) {
+        // tensor-core phases: source and destination rows inside the rows (plus the zero row),
+        // K and form blocks within the staging area and the accumulator columns, every tile's
+        // data and blocks inside its phase
+        const qx_mma_phase *mp = reinterpret_cast<const qx_mma_phase *>(plan + h.off[QX_S_MMA_PHASES]);
+        const qx_mma_tile *mt = reinterpret_cast<const qx_mma_tile *>(plan + h.off[QX_S_MMA_TILES]);
+        const uint32_t *rows = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_ROWS]);
+        const uint64_t zero_row = (uint64_t)(h.n_slots + h.n_scratch) * QX_RP * 4;
+        const uint64_t n_tiles = h.cnt[QX_S_TILEDATA] / (128 * 16);
+        for (uint64_t i = 0; i < h.cnt[QX_S_MMA_PHASES]; i++) {
+            const qx_mma_phase &m = mp[i];
+            if (m.n_kb < 1 || m.n_kb > QX_MMA_MAX_KB || m.n_fb < 1 || m.n_fb > QX_MMA_MAX_FB ||
+                (uint64_t)m.kr0 + 16ull * m.n_kb > h.cnt[QX_S_ROWS] ||
+                (uint64_t)m.dst0 + 128ull * m.n_fb > h.cnt[QX_S_ROWS] || m.t0 > m.t1 ||
+                m.t1 > h.cnt[QX_S_MMA_TILES])
+                return fail(QX_ERR_INVALID_PLAN, "tensor-core phase %llu out of bounds", (unsigned long long)i);
+            for (uint32_t r = 0; r < 16 * m.n_kb; r++)
+                if (rows[m.kr0 + r] > zero_row || rows[m.kr0 + r] % (QX_RP * 4))
+                    return fail(QX_ERR_INVALID_PLAN, "tensor-core phase %llu: a source row outside the rows",
+                                (unsigned long long)i);
+            for (uint32_t r = 0; r < 128 * m.n_fb; r++)
+                if (rows[m.dst0 + r] != QX_NONE32 && (rows[m.dst0 + r] >= zero_row || rows[m.dst0 + r] % (QX_RP * 4)))
+                    return fail(QX_ERR_INVALID_PLAN, "tensor-core phase %llu: a destination outside the rows",
+                                (unsigned long long)i);
+            for (uint32_t t = m.t0; t < m.t1; t++)
+                if (mt[t].data >= n_tiles || mt[t].fb >= m.n_fb || mt[t].kb >= m.n_kb)
+                    return fail(QX_ERR_INVALID_PLAN, "tensor-core tile %u out of bounds", t);
+        }
     }
     const uint32_t *tp = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FAM_TOUCH_PTR]);
     const uint32_t *tf = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FAM_TOUCH]);
@@ -306,6 +346,10 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.emb_table = sec<float>(ex, QX_S_EMB_TABLE);
     d.tables = sec<uint32_t>(ex, QX_S_TABLES);
     d.reg_cols = sec<int32_t>(ex, QX_S_REG_COLS);
+    d.mma_phases = sec<qx_mma_phase>(ex, QX_S_MMA_PHASES);
+    d.mma_tiles = sec<qx_mma_tile>(ex, QX_S_MMA_TILES);
+    d.tiledata = sec<uint4>(ex, QX_S_TILEDATA);
+    d.has_mma = (h.flags & QX_PLAN_FLAG_MMA) ? 1 : 0;
     d.B = batch;
     d.Bpad = ex->Bpad;
     d.D = (int32_t)h.D;

@@ -95,6 +95,44 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// ---- tensor cores (tcgen05): the linear forms of a tensor-core phase ----------------------------
+// D[form][machine] (fp32, tensor memory: lane = form of the block, column = machine) +=
+// A[form][k] (bf16 weights, tensor memory: lane = form, 8 columns of two k each) x B[machine][k]
+// (bf16 source rows staged in shared memory, K-major, no swizzle: core matrices of 8 machines x
+// 16 bytes, the two 8-row halves of K 128 B apart, machine groups of 8 rows 256 B apart).
+// Tensor-memory columns: [0, 256) accumulators (32 per form block), [256, 384) A tiles (8 each).
+#define QX_TMEM_COLS 512
+#define QX_TMEM_A0 256
+__device__ __forceinline__ uint32_t su32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ uint64_t umma_desc_kmajor(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (uint64_t)(128u >> 4) << 16 | (uint64_t)(256u >> 4) << 32 |
+           (uint64_t)1 << 46;  // descriptor version of sm_100; base offset 0, no swizzle
+}
+// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, N = 32, M = 128
+constexpr uint32_t kMmaIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((32u >> 3) << 17) | ((128u >> 4) << 24);
+__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t acc) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(d), "r"(a), "l"(bdesc),
+                 "r"(kMmaIdesc), "r"(acc)
+                 : "memory");
+}
+// bounded wait (about 2^31 SM cycles, ~1 s) for the completion of phase `par` of a shared-memory
+// mbarrier (false: gave up)
+__device__ __forceinline__ bool mbar_wait(const uint64_t *bar, uint32_t par) {
+    uint32_t done = 0;
+    const long long t0 = clock64();
+    while (!done) {
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done)
+                     : "r"(su32(bar)), "r"(par)
+                     : "memory");
+        if (!done && clock64() - t0 > (1ll << 31)) return false;
+    }
+    return true;
+}
+
 // A warp's view of its range [begin, end) of the plan stream, read through a ring of QX_NCHUNK
 // chunks of QX_CHUNK quads: while the warp reads one chunk, the next QX_NCHUNK - 1 are in flight.
 #define QX_CHUNK 32
@@ -143,9 +181,129 @@ struct Stream {
     }
 };
 
+
+// One tensor-core form phase (QX_PH_MMA): a function of its own (not inlined), so that its
+// registers (a round's tile rows in flight) do not add to the pressure of the CUDA-core phases.
+__device__ __noinline__ void mma_forms_phase(const QxDev &d, uint32_t pi, int32_t t, float *sm, char *rings,
+                                             const uint32_t *tslot, const uint64_t *mbar, int warp, int lane,
+                                             bool act, int m) {
+    float *sml = sm + lane;
+    const qx_mma_phase mp = d.mma_phases[pi];
+    char *const stage = rings;  // K block j: 1 KB at j * 1024
+    // a wait for the tensor cores that gave up in an earlier phase (the CTA's machines carry
+    // QX_E_BUSY): no further tensor-core work in this launch
+    volatile uint32_t *dead = const_cast<uint32_t *>(tslot) + 1;
+    if (*dead) return;
+    const uint32_t tmem = *tslot;
+    // the mbarrier's phase parity: its commits so far (pad0: this token's before this
+    // phase; pad1: a token's, in total)
+    uint32_t mma_par = (mp.pad0 + (uint32_t)t * mp.pad1) & 1u;
+    uint32_t inexact = 0;
+    bool tc_busy = false;
+    // 1. stage the source rows as bf16 (exact: the circuit's values are bf16 numbers,
+    //    checked here), warp w the K blocks w, w + 16, ...; lane = machine = B row
+    for (uint32_t j = warp; j < mp.n_kb; j += QX_NW) {
+        const uint4 *ro = reinterpret_cast<const uint4 *>(d.rows + mp.kr0 + 16 * j);
+        uint32_t pk[8];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) {
+            const uint4 o = __ldg(ro + q4);
+            const uint32_t a0 = __float_as_uint(QX_AT(sml, o.x)), a1 = __float_as_uint(QX_AT(sml, o.y)),
+                           a2 = __float_as_uint(QX_AT(sml, o.z)), a3 = __float_as_uint(QX_AT(sml, o.w));
+            inexact |= (a0 | a1 | a2 | a3) & 0xFFFFu;
+            pk[2 * q4] = (a0 >> 16) | (a1 & 0xFFFF0000u);
+            pk[2 * q4 + 1] = (a2 >> 16) | (a3 & 0xFFFF0000u);
+        }
+        char *dst = stage + j * 1024 + (lane >> 3) * 256 + (lane & 7) * 16;
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4 *>(dst + 128) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    }
+    if (inexact && act) atomicOr(&d.err[m], QX_E_INEXACT);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the MMAs
+    // 2. the tiles in rounds of up to 16 A slots: team warp / 4 loads tiles team,
+    //    team + 4, ... of the round (lane quarter warp % 4 = tile rows 32q .. 32q + 31),
+    //    one thread issues the round's MMAs and commits them to the mbarrier
+    const int team = warp >> 2, q = warp & 3;
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    for (uint32_t r0 = mp.t0; r0 < mp.t1; r0 += 16) {
+        const uint32_t nt = min(16u, mp.t1 - r0);
+        uint4 a[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t t = team + 4 * i;
+            if (t < nt) {
+                const uint4 *src = d.tiledata + (size_t)__ldg(&d.mma_tiles[r0 + t].data) * 256 + (q * 32 + lane) * 2;
+                a[i][0] = __ldg(src);
+                a[i][1] = __ldg(src + 1);
+            }
+        }
+        if (r0 > mp.t0) {  // the previous round's MMAs have read their A slots
+            tc_busy = !mbar_wait(mbar, mma_par);
+            mma_par ^= 1;
+            tc_after();
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t t = team + 4 * i;
+            if (t < nt)
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
+                                 tq + QX_TMEM_A0 + 8 * t),
+                             "r"(a[i][0].x), "r"(a[i][0].y), "r"(a[i][0].z), "r"(a[i][0].w), "r"(a[i][1].x),
+                             "r"(a[i][1].y), "r"(a[i][1].z), "r"(a[i][1].w)
+                             : "memory");
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_before();
+        tc_busy = __syncthreads_or(tc_busy);  // (one decision for the whole CTA)
+        tc_after();
+        if (tc_busy) break;
+        if (threadIdx.x == 0) {
+            for (uint32_t t = 0; t < nt; t++) {
+                const qx_mma_tile tl = d.mma_tiles[r0 + t];
+                mma_ts(tmem + 32 * tl.fb, tmem + QX_TMEM_A0 + 8 * t, umma_desc_kmajor(su32(stage + tl.kb * 1024)),
+                       tl.acc);
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             su32(mbar))
+                         : "memory");
+        }
+    }
+    if (!tc_busy) tc_busy = !mbar_wait(mbar, mma_par);  // the phase's accumulators are complete
+    tc_busy = __syncthreads_or(tc_busy);
+    tc_after();
+    if (tc_busy) {
+        *dead = 1u;
+        if (act) atomicOr(&d.err[m], QX_E_BUSY);
+        return;
+    }
+    // 3. team t reads form blocks t, t + 4, ...: its lane quarter holds forms 32q ..
+    //    32q + 31 of the block, 32 machines each, stored into their rows
+    for (uint32_t fb = team; fb < mp.n_fb; fb += 4) {
+        const uint32_t dst = __ldg(d.rows + mp.dst0 + fb * 128 + q * 32 + lane);
+        float *row = reinterpret_cast<float *>(reinterpret_cast<char *>(sm) + (dst != QX_NONE32 ? dst : 0));
+#pragma unroll
+        for (int h = 0; h < 2; h++) {  // machines 16h .. 16h + 15
+            uint32_t v[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+                "%12, %13, %14, %15}, [%16];"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                  "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                  "=r"(v[14]), "=r"(v[15])
+                : "r"(tq + 32 * fb + 16 * h)
+                : "memory");
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (dst != QX_NONE32) {
+#pragma unroll
+                for (int n = 0; n < 16; n++) row[16 * h + n] = __uint_as_float(v[n]);
+            }
+        }
+    }
+    tc_before();  // these reads precede the next phase's MMAs (across its barrier)
+}
 }  // namespace
 
-template <int RUN, int QH>
+template <int RUN, int QH, int TC>
 __global__ void __launch_bounds__(QX_NT, 1)
     qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens) {
     extern __shared__ __align__(16) float sm[];
@@ -173,7 +331,24 @@ __global__ void __launch_bounds__(QX_NT, 1)
     int dpar = 0;
     uint32_t dprev = 0;
     if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
-    if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; }
+    if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; touched[13] = 0; }
+    // tensor-core phases: the CTA's tensor memory (warp 0 allocates it; a CTA per SM) and the
+    // mbarrier its MMA commits arrive on, in the counter block
+    uint64_t *mbar = reinterpret_cast<uint64_t *>((reinterpret_cast<uintptr_t>(touched + 4) + 7) & ~(uintptr_t)7);
+    uint32_t *tslot = touched + 12;
+    if (TC) {
+        if (warp == 0) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tslot)),
+                         "r"(QX_TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+        if (threadIdx.x == 0) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(mbar)) : "memory");
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        tc_before();
+    }
     const int grp = blockIdx.x / C;
     const int m = grp * 32 + lane;  // this lane's machine
     const bool act = m < d.B;
@@ -194,6 +369,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
         }
     }
     phase_sync(C);  // (with C > 1, also: every CTA of the cluster runs before rows are shared)
+    if (TC) tc_after();
     const qx_phase *prog = RUN ? d.run_prog : d.step_prog;
     for (int32_t t = 0; t < n_tokens; t++) {
         for (int pc = 0;; pc++) {
@@ -289,6 +465,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 st.finish();
                 break;
             }
+            case QX_PH_MMA:
+                // linear forms on the tensor cores; every CTA of a cluster computes all of them
+                if (TC) mma_forms_phase(d, ph.a, t, sm, rings, tslot, mbar, warp, lane, act, m);
+                break;
             case QX_PH_UNITS: {
                 // pieces [out, n_const, 0, n | flags] + n_const quads [F[b] row, k, cb, 0]
                 // (k relu(F[b] + cb)) + two quads per unit with an a form, [F[a] row, F[b] row,
@@ -714,6 +894,26 @@ __global__ void __launch_bounds__(QX_NT, 1)
         }
     }
     if (threadIdx.x == 0 && d.state_bytes) atomicAdd(d.state_bytes, 512ull * *touched);
+    if (TC) {
+        // (the last phase ended with a barrier after tc_before)  After a wait that gave up, the
+        // issuing thread first waits, bounded again, for every MMA it issued: a fresh commit on a
+        // second mbarrier tracks them all
+        if (threadIdx.x == 0 && tslot[1]) {
+            uint64_t *bar2 = mbar + 1;
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(bar2)) : "memory");
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar2))
+                         : "memory");
+            mbar_wait(bar2, 0);
+        }
+        tc_before();
+        __syncthreads();
+        if (warp == 0) {
+            tc_after();
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tslot), "r"(QX_TMEM_COLS)
+                         : "memory");
+        }
+    }
     if (RUN && crank == 0) {
         for (int i = warp; i < d.n_born0; i += QX_NW) {
             uint2 p = d.pairs[i];
@@ -734,11 +934,17 @@ __global__ void __launch_bounds__(QX_NT, 1)
     if (C > 1) phase_sync(C);  // no CTA leaves while a peer may still address its rows
 }
 
-// QH: query rows a value head reads, at most (2 when the plan's heads read at most 2, else 4)
-template __global__ void qx_token_kernel<0, 2>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1, 2>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<0, 4>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1, 4>(const __grid_constant__ QxDev, int32_t, int32_t *);
+// QH: query rows a value head reads, at most (2 when the plan's heads read at most 2, else 4);
+// TC: the plan has tensor-core form phases (the CTA holds tensor memory); a plan without them
+// runs an instantiation that contains no tensor-core code at all
+template __global__ void qx_token_kernel<0, 2, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<1, 2, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<0, 4, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<1, 4, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<0, 2, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<1, 2, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<0, 4, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
+template __global__ void qx_token_kernel<1, 4, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
 
 // Sets rows [row0, row0 + n) of x to the embeddings of the given tokens (FreeRun.load).
 __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok) {

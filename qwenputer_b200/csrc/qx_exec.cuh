@@ -52,6 +52,11 @@ struct QxDev {
     uint32_t zero_row;  // byte offset of the row kept at zero
     int32_t cluster;    // CTAs sharing one group of 32 machines (a thread-block cluster)
     int32_t n_zero_rows;
+    // tensor-core form phases
+    const qx_mma_phase *mma_phases;
+    const qx_mma_tile *mma_tiles;
+    const uint4 *tiledata;  // [tiles][128 rows][2] (a row: 16 bf16 weights)
+    int32_t has_mma;        // the kernel allocates tensor memory
 };
 
 // per-machine error bits
@@ -59,6 +64,7 @@ struct QxDev {
 #define QX_E_KEY 2u         // a key with more than one positive channel
 #define QX_E_QUERY 4u       // a query with more positive channels than the head reads
 #define QX_E_BUSY 8u        // a bounded wait gave up
+#define QX_E_INEXACT 16u    // a value a tensor-core form phase read is not exact in bf16
 
 struct QxImage {  // one machine inside a packed image upload (offsets into the word pool)
     uint32_t rom_off, rom_len, drom_off, drom_words, ram_off, bn_off;  // bn_off: ~0 = none

@@ -105,10 +105,10 @@ def load_graph(c=None) -> graphfile.GraphData:
     return graphfile.export_graph(c)
 
 
-def plan_for(g: graphfile.GraphData, cluster: int = 1):
-    key = (id(g), cluster)
+def plan_for(g: graphfile.GraphData, cluster: int = 1, tc: bool = False):
+    key = (id(g), cluster, tc)
     if key not in _plans:
-        _plans[key] = (g, compile_plan(g, cluster=cluster))
+        _plans[key] = (g, compile_plan(g, cluster=cluster, tc=tc))
     return _plans[key][1]
 
 
@@ -176,7 +176,9 @@ def snapshot_states(c, head_levels) -> list:
 class Executor:
     """Executor2's surface (tritonexec.py:173-289) on the B200 kernel."""
 
-    def __init__(self, c=None, batch: int = 1, device="cuda", cluster: int | None = None):
+    def __init__(self, c=None, batch: int = 1, device="cuda", cluster: int | None = None, tc: bool = False):
+        """``tc``: run the linear forms on the tensor cores (tcgen05 MMA phases) instead of the
+        CUDA cores; the results are the same bits either way."""
         torch = _torch()
         self.g = load_graph(c)
         self.c = c
@@ -187,7 +189,8 @@ class Executor:
         if cluster is None:
             cluster = pick_cluster(self.B, self.g, self.dev.index)
         self.cluster = int(cluster)
-        self.plan = plan_for(self.g, self.cluster)
+        self.tc = bool(tc)
+        self.plan = plan_for(self.g, self.cluster, self.tc)
         self.D = int(self.g.D)
         blob = self.plan.blob()
         self._blob = C.create_string_buffer(blob, len(blob))

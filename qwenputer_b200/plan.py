@@ -57,11 +57,11 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 13
+VERSION = 14
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
-          DECODE=10, END=11, VHRUN=12, VHSUM=13)
+          DECODE=10, END=11, VHRUN=12, VHSUM=13, MMA=14)
 NOSYNC = 0x100  # phase kind flag: no barrier after the phase
 # stream pieces: a header quad [x, y, z, n | flags << 24] and n <= PIECE_MAX - 1 body quads, never
 # crossing a ring chunk of RING_QUADS quads (counted from the warp's range start); a record longer
@@ -77,12 +77,22 @@ UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most t
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
        "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
-       "TABLES", "REG_COLS", "FAM_TOUCH_PTR", "FAM_TOUCH"]
+       "TABLES", "REG_COLS", "FAM_TOUCH_PTR", "FAM_TOUCH", "MMA_PHASES", "MMA_TILES", "TILEDATA"]
 TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
                + [f"quo{i}" for i in range(4)] + [f"rom{i}" for i in range(32)]
                + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
                + [f"bn2.{i}" for i in range(4)] + [f"ram{i}" for i in range(32)])
 SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
+# tensor-core form phases (PH["MMA"]): F[form, machine] = sum W[form, k] X[k, machine] on tcgen05
+# as M = 128 forms (a form block) x N = 32 machines x K = 16 source rows (a K block) tiles, bf16
+# operands (every weight and every value a form reads is bf16-exact) and fp32 accumulators in
+# tensor memory; the phase's source rows are staged as bf16 into the stream rings (1 KB per K
+# block, so at most MMA_MAX_KB), the accumulators of at most MMA_MAX_FB form blocks live in
+# tensor-memory columns [0, 256)
+MMA_M, MMA_K = 128, 16
+MMA_MAX_KB = 16
+MMA_MAX_FB = 8
+FLAG_MMA = 1  # header flag: the plan has tensor-core form phases
 
 DT = {
     "phase": np.dtype([("kind", "<u4"), ("a", "<u4"), ("b", "<u4"), ("c", "<u4")]),
@@ -92,6 +102,9 @@ DT = {
                        ("nrows", "<u2"), ("a_row", "<u4"), ("b_row", "<u4"), ("ca", "<f4"),
                        ("cb", "<f4"), ("bconst", "<f4"), ("nout", "<u4"), ("out4", "<u4", (4,))]),
     "colform": np.dtype([("row", "<u4"), ("pad", "<u2"), ("live", "<u2"), ("c", "<f4")]),
+    "mma": np.dtype([("n_kb", "<u4"), ("kr0", "<u4"), ("n_fb", "<u4"), ("dst0", "<u4"), ("t0", "<u4"),
+                     ("t1", "<u4"), ("pad0", "<u4"), ("pad1", "<u4")]),
+    "tile": np.dtype([("data", "<u4"), ("fb", "<u4"), ("kb", "<u4"), ("acc", "<u4")]),
 }
 HEADER = struct.Struct("<QII" + "I" * 16 + "32Q32Q")
 
@@ -150,7 +163,7 @@ class Plan:
         head = HEADER.pack(MAGIC, VERSION, h["D"], h["n_slots"], h["n_scratch"], h["nw"],
                            h["n_head_levels"], h["one_row"], h["n_ksel_slots"], h["qhot_max"],
                            h["n_fam"], h["n_pay"], h["n_feat"], h["n_emb_rows"], h["n_families"],
-                           h["vocab"], h["n_born0"], h["cluster"], 0, *offs, *cnts)
+                           h["vocab"], h["n_born0"], h["cluster"], h.get("flags", 0), *offs, *cnts)
         out = bytearray(pos)
         out[:len(head)] = head
         for p, b in parts:
@@ -159,10 +172,11 @@ class Plan:
 
 
 def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAULT,
-                 ksel_slots: int = 16, cluster: int = 1) -> Plan:
+                 ksel_slots: int = 16, cluster: int = 1, tc: bool = False) -> Plan:
     """The phase program and stream of the graph, for CTAs of ``nw`` warps; one group of 32
     machines runs on a cluster of ``cluster`` CTAs, so stream records are balanced over
-    nw * cluster warps."""
+    nw * cluster warps.  ``tc``: linear forms run as tensor-core phases (tcgen05) instead of
+    stream records on the CUDA cores (every CTA of a cluster then computes all of them)."""
     assert 1 <= cluster <= 8, cluster
     # the kernel takes the ONE dim as 1 on every machine: no sublayer may write it
     assert ONE not in set(int(d) for d in g.ffn_out) and ONE not in set(int(d) for d in g.out_dim)
@@ -373,6 +387,73 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
             stats["form_nnz"] += len(ta) + len(tb)
         stream_phase(PH["FORMS"], recs, costs, prog)
 
+    mma_l: list[tuple] = []
+    tiles_l: list[tuple] = []
+    tiledata_l: list[np.ndarray] = []
+
+    def bf16_exact(w: float) -> bool:
+        return (int(np.float32(w).view(np.uint32)) & 0xFFFF) == 0
+
+    def mma_phase(form_list: list[tuple], dst_rows: list[int], rowmap, prog) -> None:
+        """Forms on the tensor cores: split (in the given order) into MMA phases of at most
+        MMA_MAX_KB K blocks of source rows and MMA_MAX_FB form blocks; per phase its source rows
+        (K blocks of MMA_K, padded with the zero row), the form blocks' destination rows (padded
+        with NONE32), and one bf16 A tile [MMA_M forms x MMA_K rows] per occupied (form block,
+        K block), the first tile of each form block starting its accumulator."""
+        if not all(bf16_exact(w) for ft in form_list for _, w in ft):
+            forms_phase(form_list, dst_rows, rowmap, prog)  # a weight bf16 cannot hold
+            return
+        subs, cur, cur_rows = [], [], set()
+        for ft, dr in zip(form_list, dst_rows):
+            rs = {rowmap(t) for t, _ in ft}
+            if cur and (len(cur_rows | rs) > MMA_MAX_KB * MMA_K or len(cur) >= MMA_MAX_FB * MMA_M):
+                subs.append(cur)
+                cur, cur_rows = [], set()
+            cur.append((ft, dr))
+            cur_rows |= rs
+        if cur:
+            subs.append(cur)
+        for sub in subs:
+            src = sorted({rowmap(t) for ft, _ in sub for t, _ in ft})
+            kidx = {r: i for i, r in enumerate(src)}
+            n_kb = -(-len(src) // MMA_K)
+            rows_l.extend([0] * (-len(rows_l) % 4))  # K blocks start 16-byte aligned (uint4 loads)
+            kr0 = len(rows_l)
+            rows_l.extend(W(r) for r in src)
+            rows_l.extend([ZW] * (n_kb * MMA_K - len(src)))
+            n_fb = -(-len(sub) // MMA_M)
+            dst0 = len(rows_l)
+            rows_l.extend(W(dr) for _, dr in sub)
+            rows_l.extend([NONE32] * (n_fb * MMA_M - len(sub)))
+            t0 = len(tiles_l)
+            for fb in range(n_fb):
+                blocks: dict[int, np.ndarray] = {}
+                for i, (ft, _) in enumerate(sub[fb * MMA_M:(fb + 1) * MMA_M]):
+                    for t, w in ft:
+                        k = kidx[rowmap(t)]
+                        tile = blocks.setdefault(k // MMA_K, np.zeros((MMA_M, MMA_K), np.uint16))
+                        assert tile[i, k % MMA_K] == 0, "two terms of one form on one row"
+                        tile[i, k % MMA_K] = _bf16_bits(w)
+                for j, kb in enumerate(sorted(blocks)):
+                    tiles_l.append((len(tiledata_l), fb, kb, 0 if j == 0 else 1))
+                    tiledata_l.append(blocks[kb])
+            mma_l.append((n_kb, kr0, n_fb, dst0, t0, len(tiles_l), 0, 0))
+            prog.append((PH["MMA"], len(mma_l) - 1, 0, 0))
+            stats["form_nnz"] += sum(len(ft) for ft, _ in sub)
+            stats["mma_tiles"] += len(tiles_l) - t0
+            stats["mma_phases"] += 1
+
+    def run_forms(form_list, dst_rows, rowmap, prog) -> None:
+        (mma_phase if tc else forms_phase)(form_list, dst_rows, rowmap, prog)
+
+    def tc_order(forms: dict, rowmap) -> dict:
+        """In tensor-core mode, forms ordered by their source rows (forms with like rows share
+        A tiles; consecutive forms get consecutive destination rows); else as given."""
+        if not tc:
+            return forms
+        order = sorted(forms, key=lambda f: tuple(sorted(rowmap(t) for t, _ in f)))
+        return {f: i for i, f in enumerate(order)}
+
     def xrow(lv, d):
         return slot[temps[(lv, d)]] if (lv, d) in temps else slot[d]
 
@@ -426,8 +507,9 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 groups.append((cur, cur_forms))
             for gnodes, gforms in groups:
                 assert len(gforms) <= len(free), f"sublayer {lv}: a node needs too many forms"
+                gforms = tc_order(gforms, lambda t: slot[t[1]])
                 flist = list(gforms)
-                forms_phase(flist, [free[i] for i in range(len(flist))], lambda t: slot[t[1]], body)
+                run_forms(flist, [free[i] for i in range(len(flist))], lambda t: slot[t[1]], body)
                 frow = {f: W(free[i]) for f, i in gforms.items()}
                 # units as flat quads (ONE is 1 for every machine: no sublayer writes it):
                 #   constant a:  [F[b] row, k, cb, 0]          k = coef * ca rounded as the
@@ -566,10 +648,11 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 groups.append((cur, cur_forms))
             for gheads, gforms in groups:
                 assert len(gforms) <= cap, f"sublayer {lv}: a key head needs too many forms"
+                gforms = tc_order(gforms, rowmap)
                 flist = list(gforms)
                 frow = {f: W(ffree[i]) for f, i in gforms.items()}
                 if flist:
-                    forms_phase(flist, [ffree[i] for i in range(len(flist))], rowmap, body)
+                    run_forms(flist, [ffree[i] for i in range(len(flist))], rowmap, body)
                 # a key head is two records, on any warps: key pieces [slot | qhot << 16, common
                 # row, lag-ONE row, n | flags] and query pieces (R_QUERY); channel quads [row, c0,
                 # c1, 1.0 if the common form applies else 0]
@@ -665,6 +748,15 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     run_prog.append((PH["DECODE"], 0, 0, 0))
     run_prog.append((PH["END"], 0, 0, 0))
     step_prog.append((PH["END"], 0, 0, 0))
+    # tensor-core phases commit once per round of up to 16 tiles to one mbarrier: record per phase
+    # the commits of a token before it (pad0) and a token's total (pad1), whose parities give the
+    # barrier phase the kernel waits on (both programs run the same MMA phases in the same order)
+    assert [p for p in run_prog if p[0] == PH["MMA"]] == [p for p in step_prog if p[0] == PH["MMA"]]
+    commits = 0
+    for i, mp in enumerate(mma_l):
+        mma_l[i] = mp[:6] + (commits, 0)
+        commits += -(-(mp[5] - mp[4]) // 16)
+    mma_l[:] = [mp[:7] + (commits,) for mp in mma_l]
 
     # ---- sections -----------------------------------------------------------------------------
     def arr(lst, dt):
@@ -733,18 +825,24 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         tptr.append(len(touch))
     s["FAM_TOUCH_PTR"] = np.asarray(tptr, np.uint32)
     s["FAM_TOUCH"] = np.asarray(touch or [0], np.uint32)
+    s["MMA_PHASES"] = arr(mma_l, "mma")
+    s["MMA_TILES"] = arr(tiles_l, "tile")
+    s["TILEDATA"] = (np.stack(tiledata_l).reshape(-1) if tiledata_l else np.zeros(MMA_M * MMA_K, np.uint16))
     P.hdr = dict(D=D, n_slots=n_slots, n_scratch=n_scratch, nw=nw, n_head_levels=len(head_levels),
                  one_row=one_w, n_ksel_slots=ksel_slots, qhot_max=qhot,
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
                  n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
-                 vocab=int(g.vocab), n_born0=len(born0), cluster=cluster)
+                 vocab=int(g.vocab), n_born0=len(born0), cluster=cluster,
+                 flags=FLAG_MMA if mma_l else 0)
     stats["n_slots"] = n_slots
     stats["n_scratch"] = n_scratch
     stats["phases_run"] = len(run_prog)
     stats["barriers_run"] = sum(1 for k, *_ in run_prog if not k & NOSYNC and k != PH["END"])
     stats["stream_quads"] = len(stream)
     stats["weight_bytes"] = int(s["STREAM"].nbytes + s["STAGES"].nbytes + s["VHEADS"].nbytes
-                                + s["RUN_PROG"].nbytes + s["WARP_PTR"].nbytes)
+                                + s["RUN_PROG"].nbytes + s["WARP_PTR"].nbytes
+                                + (s["TILEDATA"].nbytes + s["MMA_TILES"].nbytes + s["MMA_PHASES"].nbytes
+                                   if mma_l else 0))
     stats["imbalance"] = (stats["imbalance_sum"] / stats["balanced_sum"]) if stats["balanced_sum"] else 0
     stats["groups"] = group_stats
     P.stats = dict(stats)

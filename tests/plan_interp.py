@@ -173,6 +173,28 @@ class PlanInterp:
                                 sel.append(np.where(qm > 0, qa, -1))
                                 vv[qa, np.arange(self.B)] = 0
                             self.qsel[slot] = sel
+            elif k == PH["MMA"]:
+                # tensor-core forms: per form block, D = sum over its tiles of A (bf16 weights,
+                # [128 forms x 16 rows]) x the staged source rows (bf16-exact, checked); the sums
+                # are exact, so float64 accumulation cast to float32 is the kernel's result
+                mp = s["MMA_PHASES"][a]
+                n_kb, kr0, n_fb, dst0 = (int(mp[f]) for f in ("n_kb", "kr0", "n_fb", "dst0"))
+                src = s["ROWS"][kr0:kr0 + 16 * n_kb]
+                xs = np.stack([self.X[int(r)] for r in src]).astype(np.float32)
+                assert not (xs.view(np.uint32) & 0xFFFF).any(), "a staged value is not bf16-exact"
+                xs = xs.astype(np.float64)
+                data = s["TILEDATA"].reshape(-1, 128, 16)
+                acc = np.zeros((n_fb, 128, self.B))
+                for t in s["MMA_TILES"][int(mp["t0"]):int(mp["t1"])]:
+                    A = (data[int(t["data"])].astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+                    kb, fb = int(t["kb"]), int(t["fb"])
+                    part = A @ xs[16 * kb:16 * kb + 16]
+                    acc[fb] = part if int(t["acc"]) == 0 else acc[fb] + part
+                for fb in range(n_fb):
+                    for i in range(128):
+                        dst = int(s["ROWS"][dst0 + fb * 128 + i])
+                        if dst != NONE:
+                            self.X[dst] = acc[fb, i].astype(np.float32)
             elif k == PH["VHRUN"]:
                 pass  # the row work a VH phase lists is done here while it is listed
             elif k == PH["VHSUM"]:

@@ -59,11 +59,11 @@ def test_bad_plans_are_rejected():
     assert lib.qx_create(bytes(blob[:1000]), C.c_size_t(1000), 4, 0, C.byref(h)) == 1
 
 
-@pytest.mark.parametrize("cluster", [1, 4])
-def test_plan_is_consistent(graph, cluster):
+@pytest.mark.parametrize("cluster,tc", [(1, False), (4, False), (1, True), (4, True)])
+def test_plan_is_consistent(graph, cluster, tc):
     from qwenputer_b200.plan import PH, RING_QUADS, SMEM_MAX, compile_plan, smem_extra_bytes
 
-    P = compile_plan(graph, cluster=cluster)
+    P = compile_plan(graph, cluster=cluster, tc=tc)
     s = P.sec
     rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * 33 * 4  # byte offsets, zero row included
     assert P.hdr["cluster"] == cluster
@@ -110,6 +110,33 @@ def test_plan_is_consistent(graph, cluster):
             assert i == end
     kinds = [int(k) & 0xFF for k in s["RUN_PROG"]["kind"]]
     assert kinds[-2:] == [PH["DECODE"], PH["END"]] and kinds.count(PH["END"]) == 1
+    # tensor-core phases: staged rows and destinations inside the rows, blocks within the
+    # staging area and accumulator columns, every tile inside its phase, the first tile of each
+    # form block starting its accumulator, and the commit counts behind the barrier parity
+    from qwenputer_b200.plan import MMA_MAX_FB, MMA_MAX_KB
+
+    assert (PH["FORMS"] in kinds) != tc and (PH["MMA"] in kinds) == tc
+    if tc:
+        assert P.hdr["flags"] == 1
+        tiles, n_tiles = s["MMA_TILES"], len(s["TILEDATA"]) // (128 * 16)
+        commits = 0
+        for mp in s["MMA_PHASES"]:
+            n_kb, kr0, n_fb, dst0, t0, t1 = (int(mp[f]) for f in ("n_kb", "kr0", "n_fb", "dst0", "t0", "t1"))
+            assert 1 <= n_kb <= MMA_MAX_KB and 1 <= n_fb <= MMA_MAX_FB and kr0 % 4 == 0 and t0 < t1
+            src = s["ROWS"][kr0:kr0 + 16 * n_kb]
+            assert np.all(src < rows) and np.all(src % 132 == 0)
+            dst = s["ROWS"][dst0:dst0 + 128 * n_fb]
+            real = dst[dst != 0xFFFFFFFF]
+            assert np.all(real < rows - 132) and len(set(real.tolist())) == len(real)
+            seen = set()
+            for t in tiles[t0:t1]:
+                assert int(t["data"]) < n_tiles and int(t["fb"]) < n_fb and int(t["kb"]) < n_kb
+                assert int(t["acc"]) == (int(t["fb"]) in seen)
+                seen.add(int(t["fb"]))
+            assert seen == set(range(n_fb))
+            assert int(mp["pad0"]) == commits
+            commits += -(-(t1 - t0) // 16)
+        assert all(int(mp["pad1"]) == commits for mp in s["MMA_PHASES"])
     assert len(s["TABLES"]) == 198
     smem = (P.hdr["n_slots"] + P.hdr["n_scratch"]) * 33 * 4 + smem_extra_bytes(P.hdr["n_ksel_slots"], P.hdr["qhot_max"], P.hdr["nw"])
     assert smem <= SMEM_MAX, smem

@@ -33,12 +33,13 @@ def qx():
     return executor
 
 
-@pytest.mark.parametrize("kind,batch,n,seed", [("base", 1, 20000, 1000), ("many", 256, 50000, 2000)])
-def test_workload_parity(qx, kind, batch, n, seed):
+@pytest.mark.parametrize("kind,batch,n,seed,tc", [("base", 1, 20000, 1000, False), ("many", 256, 50000, 2000, False),
+                                                  ("many", 256, 50000, 2000, True)])
+def test_workload_parity(qx, kind, batch, n, seed, tc):
     from qwenputer_b200 import workload
 
     progs = workload.workload_programs(kind, batch, seed)
-    ex = qx.Executor(None, batch=batch)
+    ex = qx.Executor(None, batch=batch, tc=tc)
     ex.load_machines(0, progs)
     ex.reset()
     go = int(oracle.lib().qxo_tok_family(18, 0))  # GO: the seventh control after 12 families

@@ -83,16 +83,18 @@ def test_load_over_used_state(qx, oracle_, programs):
     assert ex.errors() == 0
 
 
-@pytest.mark.parametrize("batch,cluster", [(1, None), (5, 1), (37, None), (37, 2)])
-def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster):
+@pytest.mark.parametrize("batch,cluster,tc", [(1, None, False), (5, 1, False), (37, None, False), (37, 2, False),
+                                              (1, None, True), (37, 1, True), (37, 4, True)])
+def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster, tc):
     """Teacher-forced steps: every dim of every row equals the oracle's Executor2 step (cluster
-    None: the executor's own choice, 8 CTAs a group at these batches)."""
+    None: the executor's own choice, 8 CTAs a group at these batches; tc: linear forms on the
+    tensor cores)."""
     pool = ["gen_small_7", "div_fuzz_0", "mul_fuzz_1", "digit_file", "gen_base_1", "refresh_70",
             "zba_rodata", "gen_many_11", "csr_putchar"]
     names = [pool[i % len(pool)] for i in range(batch)]
     progs = [programs[n]["prog"] for n in names]
     traces = [programs[n]["trace"] for n in names]
-    ex = qx.Executor(None, batch=batch, cluster=cluster)
+    ex = qx.Executor(None, batch=batch, cluster=cluster, tc=tc)
     ex.load_machines(0, progs)
     ost = _oracle_state(oracle_, progs)
     T = 60 if batch > 8 else 120
@@ -110,8 +112,9 @@ def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster):
     assert ex.errors() == 0
 
 
-@pytest.mark.parametrize("batch,n,cluster", [(1, 3000, None), (40, 1500, None), (40, 1500, 1)])
-def test_free_run_matches_machine(qx, programs, batch, n, cluster):
+@pytest.mark.parametrize("batch,n,cluster,tc", [(1, 3000, None, False), (40, 1500, None, False),
+                                                (40, 1500, 1, False), (40, 1500, 1, True), (1, 3000, None, True)])
+def test_free_run_matches_machine(qx, programs, batch, n, cluster, tc):
     """Free-running generation: every token equals the traced machine's, and the machine state
     read back from the heads equals the traced state after the last complete record."""
     from qwenputer_b200 import workload
@@ -119,7 +122,7 @@ def test_free_run_matches_machine(qx, programs, batch, n, cluster):
     progs = [programs[k]["prog"] for k in sorted(programs)]
     progs += workload.workload_programs("many", max(0, batch - len(progs)), 500)
     progs = progs[:batch]
-    ex = qx.Executor(None, batch=batch, cluster=cluster)
+    ex = qx.Executor(None, batch=batch, cluster=cluster, tc=tc)
     ex.load_machines(0, progs)
     ex.reset()
     go = int(oracle.lib().qxo_tok_family(18, 0))  # GO: the seventh control after 12 families
@@ -143,15 +146,16 @@ def test_free_run_matches_machine(qx, programs, batch, n, cluster):
 
 
 def test_cluster_sizes_agree(qx):
-    """One group of 32 machines on 1, 2, 4 or 8 CTAs of a cluster: the same tokens, states and
-    checksums (96 machines of the bignum workload, 400 tokens)."""
+    """One group of 32 machines on 1, 2, 4 or 8 CTAs of a cluster, linear forms on the CUDA cores
+    or the tensor cores: the same tokens, states and checksums (96 machines of the bignum
+    workload, 400 tokens)."""
     from qwenputer_b200 import workload
 
     progs = workload.workload_programs("bignum", 96, 77)
     go = int(oracle.lib().qxo_tok_family(18, 0))
     outs = []
-    for cluster in (1, 2, 4, 8):
-        ex = qx.Executor(None, batch=96, cluster=cluster)
+    for cluster, tc in ((1, False), (2, False), (4, False), (8, False), (1, True), (2, True), (8, True)):
+        ex = qx.Executor(None, batch=96, cluster=cluster, tc=tc)
         assert ex.info(0) == cluster and ex.info(2) == 3 * cluster and ex.info(1) >= 1
         ex.load_machines(0, progs)
         ex.reset()
@@ -301,15 +305,15 @@ def test_gdn_step_on_two_devices_from_one_thread(qx):
         assert np.array_equal(Sd.cpu().numpy(), So) and np.array_equal(od.cpu().numpy(), ow), d
 
 
-@pytest.mark.parametrize("cluster", [1, 4])
-def test_step_in_cuda_graph(qx, graph, programs, cluster):
+@pytest.mark.parametrize("cluster,tc", [(1, False), (4, False), (1, True)])
+def test_step_in_cuda_graph(qx, graph, programs, cluster, tc):
     """Executor.step captured in a CUDA graph (as ExecRow captures Executor2.step) replays the
     same residuals and head states as eager steps."""
     names = ["gen_small_7", "div_fuzz_0", "mul_fuzz_1"]
     progs = [programs[n]["prog"] for n in names]
     traces = [programs[n]["trace"] for n in names]
-    eager = qx.Executor(None, batch=3, cluster=cluster)
-    capt = qx.Executor(None, batch=3, cluster=cluster)
+    eager = qx.Executor(None, batch=3, cluster=cluster, tc=tc)
+    capt = qx.Executor(None, batch=3, cluster=cluster, tc=tc)
     for ex in (eager, capt):
         ex.load_machines(0, progs)
     xbuf = torch.zeros(3, graph.D, device="cuda")

@@ -8,11 +8,14 @@ import oracle
 from plan_interp import PlanInterp
 
 
-@pytest.mark.parametrize("names,cluster", [(["gen_small_7", "div_fuzz_0"], 1), (["digit_file", "refresh_70"], 8)])
-def test_plan_program_matches_oracle(oracle_, graph, programs, names, cluster):
+@pytest.mark.parametrize("names,cluster,tc", [(["gen_small_7", "div_fuzz_0"], 1, False),
+                                               (["digit_file", "refresh_70"], 8, False),
+                                               (["gen_bignum_5", "mul_fuzz_1"], 1, True),
+                                               (["zba_rodata", "div_fuzz_1"], 4, True)])
+def test_plan_program_matches_oracle(oracle_, graph, programs, names, cluster, tc):
     from qwenputer_b200.plan import compile_plan
 
-    P = compile_plan(graph, cluster=cluster)
+    P = compile_plan(graph, cluster=cluster, tc=tc)
     B = len(names)
     it = PlanInterp(P, B)
     ost = oracle_.new_state(B)
