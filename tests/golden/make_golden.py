@@ -25,6 +25,11 @@ Writes:
   gdn_general.npz  the same function on unit-norm Gaussian keys (every head), and on a mix drawn
                  like the 1,024 x 48-head step (95% one-hot keys, alpha 90 / 5 / 5% at 1 / 0.5 /
                  0); one-hot queries
+  hf_residual.npz  the compiled stack emitted as stock transformers Qwen3_5ForCausalLM weights
+                 (the reference's ``hf.build_model``, bf16, torch kernels), the snapshot injected
+                 into its cache, decoded token by token: the residual of every IR dim after the
+                 last compiled layer at every position (ERV/chipformer/rv/hf.py:74-112), for
+                 programs of programs.npz (``--only hf`` rewrites only this file)
 """
 
 import argparse
@@ -325,14 +330,70 @@ def gdn_goldens() -> None:
     np.savez_compressed(HERE / "gdn_general.npz", **out)
 
 
+HF_CASES = {"div_fuzz_0": 40, "gen_small_7": 40}
+
+
+def hf_goldens(ref_root: str) -> None:
+    """Residuals of the stock HF modules (bf16) running the emitted compiled stack, decoded
+    token by token from the snapshot of each HF_CASES program (its first n trace tokens)."""
+    sys.path.insert(0, ref_root)
+    sys.path.insert(0, str(REPO))
+    import numpy as np
+    import torch
+    from chipformer.rv import core, hf, ref
+
+    t0 = time.time()
+    c = core.build()
+    z = np.load(HERE / "programs.npz")
+    out = {"names": np.asarray(sorted(HF_CASES))}
+    for name, n in sorted(HF_CASES.items()):
+        p = SimpleNamespace(text=[int(w) for w in z[f"{name}.text"]], data=z[f"{name}.data"].tobytes(),
+                            data_base=int(z[f"{name}.data_base"]), entry=int(z[f"{name}.entry"]),
+                            rodata=z[f"{name}.rodata"].tobytes())
+        core.snapshot(c, ref.Machine.from_program(p))
+        toks = [int(t) for t in ref.Machine.from_program(p).run(n + 1)[:n]]
+        model, lay, ids = hf.build_model(c, toks)
+        print(f"  hf model for {name}: hidden {lay.hidden}, {time.time() - t0:.0f} s", flush=True)
+        dims = list(range(1, len(c.dims)))
+        cols = [lay.dim(d) for d in dims]
+        r = c.target.value_heads // c.target.key_heads
+        with torch.no_grad():
+            o = model(input_ids=torch.tensor([[ids[None]]]), use_cache=True)  # the zero prefix
+            cache = o.past_key_values
+            # the snapshot into the linear-attention states (hf.inject's layout; this
+            # transformers keeps a layer's recurrent state as one [B, H, dk, dv] tensor)
+            for ni, (L, j) in hf.head_slots(c).items():
+                st = cache.layers[L].recurrent_states
+                init = c.nodes[ni].init or []
+                for x in range(len(c.nodes[ni].vheads())):
+                    S = st[0, j * r + x]
+                    S.zero_()
+                    for row, vec in (init[x] if x < len(init) else {}).items():
+                        S[row] = torch.tensor(vec, dtype=S.dtype)
+            hs = []
+            for t in range(n):
+                o = model(input_ids=torch.tensor([[ids[toks[t]]]]), past_key_values=cache, use_cache=True,
+                          output_hidden_states=True)
+                hs.append(o.hidden_states[c.n_layers()][0])
+        h = torch.cat(hs).float().numpy()[:, cols]
+        out[f"{name}.tokens"] = np.asarray(toks, np.int32)
+        out[f"{name}.resid"] = np.ascontiguousarray(h, np.float32)  # [n, D - 1]: dims 1 .. D - 1
+        print(f"  hf decode {name}: {n} positions, {time.time() - t0:.0f} s", flush=True)
+    np.savez_compressed(HERE / "hf_residual.npz", **out)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("ref_root", nargs="?", default=os.environ.get("QX_REFERENCE_ROOT"),
                     help="the reference's experimental/riscv directory (or QX_REFERENCE_ROOT)")
-    ap.add_argument("--only", choices=["gdn"], default=None)
+    ap.add_argument("--only", choices=["gdn", "hf"], default=None)
     a = ap.parse_args()
     if a.only == "gdn":
         gdn_goldens()
+    elif a.only == "hf":
+        if not a.ref_root:
+            ap.error("give the reference's experimental/riscv directory or set QX_REFERENCE_ROOT")
+        hf_goldens(a.ref_root)
     else:
         if not a.ref_root:
             ap.error("give the reference's experimental/riscv directory or set QX_REFERENCE_ROOT")

@@ -174,6 +174,28 @@ def test_cluster_sizes_agree(qx):
         assert np.array_equal(o[3], outs[0][3])
 
 
+@pytest.mark.parametrize("tc", [False, True])
+def test_step_matches_stock_hf_modules(qx, graph, programs, tc):
+    """Teacher-forced steps against the stock transformers Qwen3.5 modules running the emitted
+    compiled stack (bf16 torch kernels, tests/golden/hf_residual.npz): every dim at every
+    position, two programs as a batch of two."""
+    from conftest import GOLDEN
+
+    h = np.load(GOLDEN / "hf_residual.npz")
+    names = [str(n) for n in h["names"]]
+    ex = qx.Executor(None, batch=len(names), tc=tc)
+    ex.load_machines(0, [programs[n]["prog"] for n in names])
+    toks = np.stack([h[f"{n}.tokens"] for n in names], 1)
+    for t in range(toks.shape[0]):
+        x = torch.from_numpy(graph.embed([int(v) for v in toks[t]])).cuda()
+        ex.step(x)
+        got = x.cpu().numpy()
+        for r, n in enumerate(names):
+            bad = np.nonzero(got[r, 1:] != h[f"{n}.resid"][t])[0]
+            assert not len(bad), (n, t, bad[:5])
+    assert ex.errors() == 0
+
+
 def test_free_run_in_chunks_equals_one_run(qx, programs):
     """Two launches of n/2 tokens generate what one launch of n does (x, lag history and head
     states carry over between launches)."""

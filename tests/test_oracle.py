@@ -143,3 +143,20 @@ def test_gdn_general_keys_match_transformers(case):
     light = ((k != 0).sum(1) == 1) & (al == 1.0)
     if light.any():
         assert np.array_equal(S[light], S_ref[light])
+
+
+@pytest.mark.parametrize("name", ["div_fuzz_0", "gen_small_7"])
+def test_oracle_step_matches_stock_hf_modules(graph, oracle_, programs, name):
+    """A third witness for the compiled weights: the reference emits the stack as stock
+    transformers Qwen3_5ForCausalLM weights (bf16, torch kernels) and decodes the trace from the
+    injected snapshot (tests/golden/hf_residual.npz); the oracle's residual equals those modules'
+    on every dim at every position."""
+    h = np.load(GOLDEN / "hf_residual.npz")
+    st = oracle_.new_state(1)
+    oracle_.snapshot(st, 0, oracle.Machine.from_program(programs[name]["prog"]))
+    want = h[f"{name}.resid"]
+    for t, tok in enumerate(h[f"{name}.tokens"]):
+        x = graph.embed([int(tok)])
+        oracle_.step(st, x, nthreads=1)
+        bad = np.nonzero(x[0, 1:] != want[t])[0]
+        assert not len(bad), (t, bad[:5])
