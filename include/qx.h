@@ -142,8 +142,8 @@ typedef struct {
                                       machines; stream ranges exist for nw * cluster warps */
     uint32_t flags;                /* QX_PLAN_FLAG_* */
     /* sections: byte offset from the blob start, element count */
-    uint64_t off[32];
-    uint64_t cnt[32];
+    uint64_t off[48];
+    uint64_t cnt[48];
 } qx_plan_header;
 
 enum { /* section ids of qx_plan_header.off / cnt */
@@ -178,11 +178,25 @@ enum { /* section ids of qx_plan_header.off / cnt */
     QX_S_MMA_PHASES,     /* qx_mma_phase */
     QX_S_MMA_TILES,      /* qx_mma_tile */
     QX_S_TILEDATA,       /* uint16 (bf16): [tiles][128][16] form-block weights */
+    QX_S_FEAT_DIM,       /* uint32 [n_feat]: the feature dims (ONE first), FEAT_ROW's order */
+    QX_S_CODE_ROW,       /* uint32 [n_code]: rows of the output-code dims (merged readout) */
+    QX_S_TEXT_WORDS,     /* uint32 [n_text][5]: each text token's 152 bits (merged) */
+    QX_S_TEXT_BASE,      /* float [n_feat]: a text token's features with no bit set */
+    QX_S_TEXT_BITS,      /* float [n_text_bits][n_feat]: the features each text bit adds */
+    QX_S_PRINTABLE,      /* int32 [n_printable]: the text token of each Q payload */
+    QX_S_TEXT_TOUCH,     /* uint32: the features a text token can make nonzero */
+    QX_S_MERGED_INFO,    /* uint32 [8]: Q family id, n_text, n_printable, n_text_touch, n_code,
+                            n_text_bits, 0, 0 */
     QX_S_COUNT
 };
-#define QX_PLAN_FLAG_MMA 1u /* the programs use QX_PH_MMA phases (the kernel holds tensor memory) */
+#define QX_PLAN_FLAG_MMA 1u    /* the programs use QX_PH_MMA phases (the kernel holds tensor memory) */
+#define QX_PLAN_FLAG_MERGED 2u /* merged readout: the next token from the signs of the code dims,
+                                  a Q code naming the text token PRINTABLE[payload] */
+#define QX_FEAT_DEFERRED 0x80000000u /* FEAT_ROW: the feature goes to x[machine][low bits] and is
+                                        loaded where it is first used (a LOADX phase) */
+#define QX_TEXT_TOKEN (1 << 24) /* a text token in the machine's stream: QX_TEXT_TOKEN | qid */
 
-#define QX_PLAN_VERSION 14
+#define QX_PLAN_VERSION 15
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

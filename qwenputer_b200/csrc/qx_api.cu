@@ -153,7 +153,7 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     if (h.cluster < 1 || h.cluster > 8) return fail(QX_ERR_INVALID_PLAN, "cluster of %u CTAs (1 to 8)", h.cluster);
     if (h.n_head_levels > QX_MAX_HL) return fail(QX_ERR_INVALID_PLAN, "too many head sublayers");
     if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
-    if (h.n_born0 != h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
+    if (h.n_born0 > h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
     const SecSpec specs[] = {
         {QX_S_RUN_PROG, sizeof(qx_phase)}, {QX_S_STEP_PROG, sizeof(qx_phase)}, {QX_S_ROWS, 4},
         {QX_S_PAIRS, 8}, {QX_S_STREAM, 16}, {QX_S_VHSUM_ROWS, 4}, {QX_S_WARP_PTR, 4},
@@ -163,7 +163,9 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
         {QX_S_FAM_IDS, 4}, {QX_S_FAM_SIZE, 4}, {QX_S_FAM_ROW0, 4}, {QX_S_EMB_BASE, 4}, {QX_S_EMB_BITS, 4},
         {QX_S_EMB_TABLE, 4}, {QX_S_TABLES, 4}, {QX_S_REG_COLS, 4},
         {QX_S_FAM_TOUCH_PTR, 4}, {QX_S_FAM_TOUCH, 4}, {QX_S_MMA_PHASES, sizeof(qx_mma_phase)},
-        {QX_S_MMA_TILES, sizeof(qx_mma_tile)}, {QX_S_TILEDATA, 2}};
+        {QX_S_MMA_TILES, sizeof(qx_mma_tile)}, {QX_S_TILEDATA, 2}, {QX_S_FEAT_DIM, 4}, {QX_S_CODE_ROW, 4},
+        {QX_S_TEXT_WORDS, 4}, {QX_S_TEXT_BASE, 4}, {QX_S_TEXT_BITS, 4}, {QX_S_PRINTABLE, 4},
+        {QX_S_TEXT_TOUCH, 4}, {QX_S_MERGED_INFO, 4}};
     for (const SecSpec &s : specs) {
         if (h.off[s.id] % 16 || h.off[s.id] + h.cnt[s.id] * s.elem > bytes)
             return fail(QX_ERR_INVALID_PLAN, "section %d out of bounds", s.id);
@@ -172,6 +174,8 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
         return fail(QX_ERR_INVALID_PLAN, "touched-feature offsets missing");
     if (h.cnt[QX_S_TABLES] != 198 || h.cnt[QX_S_REG_COLS] != 256)
         return fail(QX_ERR_INVALID_PLAN, "snapshot tables missing");
+    if (h.cnt[QX_S_FEAT_DIM] != h.n_feat || h.cnt[QX_S_MERGED_INFO] != 8)
+        return fail(QX_ERR_INVALID_PLAN, "feature dims or merged-readout facts missing");
     if (h.cnt[QX_S_HL_V] != h.n_head_levels || h.cnt[QX_S_FEAT_ROW] != h.n_feat ||
         h.cnt[QX_S_FAM_ROW] != h.n_fam || h.cnt[QX_S_PAY_ROW] != h.n_pay)
         return fail(QX_ERR_INVALID_PLAN, "section counts disagree with the header");
@@ -245,6 +249,37 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
             for (uint32_t t = m.t0; t < m.t1; t++)
                 if (mt[t].data >= n_tiles || mt[t].fb >= m.n_fb || mt[t].kb >= m.n_kb)
                     return fail(QX_ERR_INVALID_PLAN, "tensor-core tile %u out of bounds", t);
+        }
+    }
+    {
+        // features: rows inside the rows, deferred ones naming dims below D; merged readout:
+        // code rows inside the rows, the text tables' sizes, printable tokens inside the vocabulary
+        const uint32_t *fr = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FEAT_ROW]);
+        const uint32_t *fd = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FEAT_DIM]);
+        const uint64_t zero_row = (uint64_t)(h.n_slots + h.n_scratch) * QX_RP * 4;
+        for (uint32_t f = 0; f < h.n_feat; f++) {
+            if (fd[f] >= h.D) return fail(QX_ERR_INVALID_PLAN, "feature %u names no dim", f);
+            if (fr[f] & QX_FEAT_DEFERRED ? (fr[f] & ~QX_FEAT_DEFERRED) != fd[f] : fr[f] >= zero_row)
+                return fail(QX_ERR_INVALID_PLAN, "feature %u: row out of range", f);
+        }
+        const uint32_t *mi = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_MERGED_INFO]);
+        if (h.flags & QX_PLAN_FLAG_MERGED) {
+            const uint32_t q_fid = mi[0], n_text = mi[1], n_pr = mi[2], n_touch = mi[3], n_code = mi[4],
+                           n_bits = mi[5];
+            if (n_code < 1 || n_code > 32 || n_code <= 16 || h.cnt[QX_S_CODE_ROW] < n_code || n_bits != 152 ||
+                h.cnt[QX_S_TEXT_WORDS] != 5ull * n_text || h.cnt[QX_S_TEXT_BASE] != h.n_feat ||
+                h.cnt[QX_S_TEXT_BITS] != (uint64_t)n_bits * h.n_feat || h.cnt[QX_S_PRINTABLE] < n_pr ||
+                h.cnt[QX_S_TEXT_TOUCH] < n_touch || n_text < 1 || n_pr < 1 || q_fid >= 32)
+                return fail(QX_ERR_INVALID_PLAN, "merged readout tables inconsistent");
+            const uint32_t *cr = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_CODE_ROW]);
+            for (uint32_t i = 0; i < n_code; i++)
+                if (cr[i] >= zero_row) return fail(QX_ERR_INVALID_PLAN, "code row out of range");
+            const int32_t *pr = reinterpret_cast<const int32_t *>(plan + h.off[QX_S_PRINTABLE]);
+            for (uint32_t i = 0; i < n_pr; i++)
+                if (pr[i] < 0 || (uint32_t)pr[i] >= n_text) return fail(QX_ERR_INVALID_PLAN, "printable token out of range");
+            const uint32_t *tt = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_TEXT_TOUCH]);
+            for (uint32_t i = 0; i < n_touch; i++)
+                if (tt[i] >= h.n_feat) return fail(QX_ERR_INVALID_PLAN, "text feature out of range");
         }
     }
     const uint32_t *tp = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FAM_TOUCH_PTR]);
@@ -350,6 +385,23 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.mma_tiles = sec<qx_mma_tile>(ex, QX_S_MMA_TILES);
     d.tiledata = sec<uint4>(ex, QX_S_TILEDATA);
     d.has_mma = (h.flags & QX_PLAN_FLAG_MMA) ? 1 : 0;
+    d.feat_dim = sec<uint32_t>(ex, QX_S_FEAT_DIM);
+    d.code_row = sec<uint32_t>(ex, QX_S_CODE_ROW);
+    d.text_words = sec<uint32_t>(ex, QX_S_TEXT_WORDS);
+    d.text_base = sec<float>(ex, QX_S_TEXT_BASE);
+    d.text_bits = sec<float>(ex, QX_S_TEXT_BITS);
+    d.printable = sec<int32_t>(ex, QX_S_PRINTABLE);
+    d.text_touch = sec<uint32_t>(ex, QX_S_TEXT_TOUCH);
+    {
+        const uint32_t *mi = reinterpret_cast<const uint32_t *>(ex->host_plan.data() + h.off[QX_S_MERGED_INFO]);
+        d.merged = (h.flags & QX_PLAN_FLAG_MERGED) ? 1 : 0;
+        d.q_fid = (int32_t)mi[0];
+        d.n_text = (int32_t)mi[1];
+        d.n_printable = (int32_t)mi[2];
+        d.n_text_touch = (int32_t)mi[3];
+        d.n_code = (int32_t)mi[4];
+        d.n_text_bits = (int32_t)mi[5];
+    }
     d.B = batch;
     d.Bpad = ex->Bpad;
     d.D = (int32_t)h.D;

@@ -824,24 +824,66 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             case QX_PH_DECODE: {
+                // the next token of every machine (warp 0, lanes = machines), then its embedding
+                // (FreeRun._step, fastexec.py:298-307; merged readout: core.py:1287-1304)
                 if (warp == 0) {
-                    float fam = 0.0f, psum = 0.0f;
-                    for (int i = 0; i < d.n_fam; i++)
-                        fam = __fadd_rn(fam, __fmul_rn(rintf(QX_AT(sml, d.fam_row[i])), ldexpf(1.0f, i)));
-                    for (int i = 0; i < d.n_pay; i++) {
-                        const float p = rintf(QX_AT(sml, d.pay_row[i]));
-                        dec_pay[i * 32 + lane] = p;
-                        psum = __fadd_rn(psum, __fmul_rn(p, ldexpf(1.0f, i)));
+                    int kind = 0, fid = 0, pay = 0;  // kind 0: chip token, 1: text token, 2: none
+                    long long tok = -1;
+                    bool bad = false;
+                    if (!d.merged) {
+                        float fam = 0.0f, psum = 0.0f;
+                        for (int i = 0; i < d.n_fam; i++)
+                            fam = __fadd_rn(fam, __fmul_rn(rintf(QX_AT(sml, d.fam_row[i])), ldexpf(1.0f, i)));
+                        for (int i = 0; i < d.n_pay; i++) {
+                            const float pv = rintf(QX_AT(sml, d.pay_row[i]));
+                            dec_pay[i * 32 + lane] = pv;
+                            psum = __fadd_rn(psum, __fmul_rn(pv, ldexpf(1.0f, i)));
+                        }
+                        const long long fraw = (long long)fam;
+                        fid = fraw < 0 ? 0 : (fraw > d.n_families - 1 ? d.n_families - 1 : (int)fraw);
+                        const long long p = (long long)psum;
+                        pay = (int)p;
+                        tok = (long long)d.fam_ids[fid] + p;
+                        bad = fraw != fid || p < 0 || p >= d.fam_size[fid];
+                    } else {
+                        // merged: a code dim > 0 is a 1 bit; all zero: the circuit predicts nothing
+                        const int nfam = d.n_code - 16;
+                        uint32_t fb = 0, pb = 0;
+                        bool anyc = false;
+                        for (int i = 0; i < d.n_code; i++) {
+                            const float v = QX_AT(sml, d.code_row[i]);
+                            anyc |= v != 0.0f;
+                            if (v > 0.0f) {
+                                if (i < nfam) fb |= 1u << i;
+                                else pb |= 1u << (i - nfam);
+                            }
+                        }
+                        for (int i = 0; i < 16; i++) dec_pay[i * 32 + lane] = (float)(pb >> i & 1u);
+                        pay = (int)pb;
+                        if (!anyc) {
+                            kind = 2;
+                        } else if ((int)fb == d.q_fid) {
+                            if ((int)pb < d.n_printable) {
+                                kind = 1;
+                                pay = d.printable[pb];  // the text token's qid
+                                tok = QX_TEXT_TOKEN + (long long)pay;
+                            } else {
+                                kind = 2;
+                                bad = true;
+                            }
+                        } else if ((int)fb < d.n_families && (int)pb < d.fam_size[fb]) {
+                            fid = (int)fb;
+                            tok = (long long)d.fam_ids[fid] + pb;
+                        } else {
+                            kind = 2;
+                            bad = true;
+                        }
                     }
-                    const long long fraw = (long long)fam;
-                    const int fid = fraw < 0 ? 0 : (fraw > d.n_families - 1 ? d.n_families - 1 : (int)fraw);
-                    const long long p = (long long)psum;
-                    const long long tok = (long long)d.fam_ids[fid] + p;
-                    dec_i[lane] = fid;
-                    dec_i[32 + lane] = (int)p;
+                    dec_i[lane] = fid | kind << 24;
+                    dec_i[32 + lane] = pay;
                     if (act) {
                         if (crank == 0) {
-                            if (fraw != fid || p < 0 || p >= d.fam_size[fid]) atomicOr(&d.err[m], QX_E_CODE);
+                            if (bad) atomicOr(&d.err[m], QX_E_CODE);
                             if (tokens) tokens[(size_t)t * d.B + m] = (int32_t)tok;
                         }
                         hash = fnv_word(hash, (uint32_t)tok);
@@ -850,38 +892,70 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     }
                 }
                 __syncthreads();
-                // next embedding (FreeRun: table row for small families, base + payload bits)
+                // next embedding (FreeRun: table row for small families, base + payload bits;
+                // a text token: its base + the rows of its bits; no token: the bare text base)
                 for (int mm = warp; mm < 32; mm += QX_NW) {
-                    const int fid = dec_i[mm], p = dec_i[32 + mm];
-                    const int row0 = d.fam_row0[fid];
+                    const int fid = dec_i[mm] & 0xFFFFFF, kind = dec_i[mm] >> 24, p = dec_i[32 + mm];
                     float *smw = sm + mm;
+                    float *xm = d.x + (size_t)(mbase + mm) * d.D;
+                    const bool mact = mbase + mm < d.B;
+                    // a feature's value into its row, or (deferred) into x where its sublayer loads it
+                    auto put = [&](int f, float v) {
+                        const uint32_t fr = d.feat_row[f];
+                        if (!(fr & QX_FEAT_DEFERRED)) QX_AT(smw, fr) = v;
+                        else if (mact) xm[fr & ~QX_FEAT_DEFERRED] = v;
+                    };
+                    if (kind != 0) {
+                        const uint32_t *w = d.text_words + (size_t)(kind == 1 ? p : 0) * 5;
+                        uint32_t wv[5];
+#pragma unroll
+                        for (int k = 0; k < 5; k++) wv[k] = kind == 1 ? __ldg(w + k) : 0u;
+                        for (int f = lane; f < d.n_feat; f += 32) put(f, 0.0f);
+                        __syncwarp();
+                        for (int tt = lane; tt < d.n_text_touch; tt += 32) {
+                            const int f = (int)d.text_touch[tt];
+                            float acc = __ldg(d.text_base + f);
+#pragma unroll 1
+                            for (int k = 0; k < 5; k++) {
+                                uint32_t bits = wv[k];
+                                while (bits) {
+                                    const int j = 32 * k + __ffs(bits) - 1;
+                                    bits &= bits - 1;
+                                    acc = __fadd_rn(acc, __ldg(d.text_bits + (size_t)j * d.n_feat + f));
+                                }
+                            }
+                            put(f, acc);
+                        }
+                        continue;
+                    }
+                    const int row0 = d.fam_row0[fid];
                     if (row0 >= 0) {
                         int r = row0 + p;
                         r = r < 0 ? 0 : (r > d.n_emb_rows - 1 ? d.n_emb_rows - 1 : r);
-                        for (int f = lane; f < d.n_feat; f += 32)
-                            QX_AT(smw, d.feat_row[f]) = __ldg(d.emb_table + (size_t)r * d.n_feat + f);
+                        for (int f = lane; f < d.n_feat; f += 32) put(f, __ldg(d.emb_table + (size_t)r * d.n_feat + f));
                     } else {
                         // every feature 0, then the family's touched ones: base + the payload
                         // bits' rows (four partial sums: exact values, any order)
-                        const float *bits = d.emb_bits + (size_t)fid * d.n_pay * d.n_feat;
-                        for (int f = lane; f < d.n_feat; f += 32) QX_AT(smw, d.feat_row[f]) = 0.0f;
+                        const int npay = d.merged ? 16 : d.n_pay;  // (a merged graph reads no payload dims)
+                        const float *bits = d.emb_bits + (size_t)fid * npay * d.n_feat;
+                        for (int f = lane; f < d.n_feat; f += 32) put(f, 0.0f);
                         __syncwarp();
                         const uint32_t t1 = d.fam_touch_ptr[fid + 1];
-                        for (uint32_t t = d.fam_touch_ptr[fid] + lane; t < t1; t += 32) {
-                            const int f = (int)d.fam_touch[t];
+                        for (uint32_t tt = d.fam_touch_ptr[fid] + lane; tt < t1; tt += 32) {
+                            const int f = (int)d.fam_touch[tt];
                             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                             int i = 0;
-                            for (; i + 4 <= d.n_pay; i += 4) {
+                            for (; i + 4 <= npay; i += 4) {
                                 float w[4];
 #pragma unroll
                                 for (int u = 0; u < 4; u++) w[u] = __ldg(bits + (size_t)(i + u) * d.n_feat + f);
 #pragma unroll
                                 for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(dec_pay[(i + u) * 32 + mm], w[u]));
                             }
-                            for (; i < d.n_pay; i++)
+                            for (; i < npay; i++)
                                 acc[0] = __fadd_rn(acc[0], __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
                             const float tot = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-                            QX_AT(smw, d.feat_row[f]) = __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), tot);
+                            put(f, __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), tot));
                         }
                     }
                 }
@@ -946,7 +1020,8 @@ template __global__ void qx_token_kernel<1, 2, 1>(const __grid_constant__ QxDev,
 template __global__ void qx_token_kernel<0, 4, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
 template __global__ void qx_token_kernel<1, 4, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
 
-// Sets rows [row0, row0 + n) of x to the embeddings of the given tokens (FreeRun.load).
+// Sets rows [row0, row0 + n) of x to the embeddings of the given tokens (FreeRun.load): chip
+// tokens through the family tables, text tokens (merged graphs) through their bits.
 __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok) {
     const int r = blockIdx.x;
     if (r >= n) return;
@@ -955,28 +1030,42 @@ __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, i
     float *x = d.x + (size_t)m * d.D;
     for (int i = threadIdx.x; i < d.D; i += blockDim.x) x[i] = 0.0f;
     __syncthreads();
-    int fid = 0;
-    for (int f = 0; f < d.n_families; f++)
-        if (t >= d.fam_ids[f] && t < d.fam_ids[f] + d.fam_size[f]) fid = f;
-    const int p = t - d.fam_ids[fid];
-    const int row0f = d.fam_row0[fid];
-    for (int f = threadIdx.x; f < d.n_feat; f += blockDim.x) {
-        const int dim = d.pairs[f].y;  // PAIRS[0 : n_feat] are (row, dim) of the feature dims
-        float v;
-        if (row0f >= 0) {
-            v = d.emb_table[(size_t)(row0f + p) * d.n_feat + f];
-        } else {
-            float acc = 0.0f;
-            for (int i = 0; i < d.n_pay; i++)
-                acc = __fadd_rn(acc, __fmul_rn((float)((p >> i) & 1), d.emb_bits[((size_t)fid * d.n_pay + i) * d.n_feat + f]));
-            v = __fadd_rn(d.emb_base[(size_t)fid * d.n_feat + f], acc);
+    const bool bad = t >= QX_TEXT_TOKEN && (!d.merged || t - QX_TEXT_TOKEN >= d.n_text);  // no such text token
+    if (t >= QX_TEXT_TOKEN) {
+        const int q = t - QX_TEXT_TOKEN;
+        if (!bad) {
+            const uint32_t *w = d.text_words + (size_t)q * 5;
+            for (int f = threadIdx.x; f < d.n_feat; f += blockDim.x) {
+                float acc = d.text_base[f];
+                for (int j = 0; j < d.n_text_bits; j++)
+                    if (w[j >> 5] >> (j & 31) & 1u) acc = __fadd_rn(acc, d.text_bits[(size_t)j * d.n_feat + f]);
+                x[d.feat_dim[f]] = acc;
+            }
         }
-        x[dim] = v;
+    } else {
+        int fid = 0;
+        for (int f = 0; f < d.n_families; f++)
+            if (t >= d.fam_ids[f] && t < d.fam_ids[f] + d.fam_size[f]) fid = f;
+        const int p = t - d.fam_ids[fid];
+        const int row0f = d.fam_row0[fid];
+        const int npay = d.merged ? 16 : d.n_pay;
+        for (int f = threadIdx.x; f < d.n_feat; f += blockDim.x) {
+            float v;
+            if (row0f >= 0) {
+                v = d.emb_table[(size_t)(row0f + p) * d.n_feat + f];
+            } else {
+                float acc = 0.0f;
+                for (int i = 0; i < npay; i++)
+                    acc = __fadd_rn(acc, __fmul_rn((float)((p >> i) & 1), d.emb_bits[((size_t)fid * npay + i) * d.n_feat + f]));
+                v = __fadd_rn(d.emb_base[(size_t)fid * d.n_feat + f], acc);
+            }
+            x[d.feat_dim[f]] = v;
+        }
     }
     if (threadIdx.x == 0) {
         d.hash[m] = 0xcbf29ce484222325ULL;
         d.count[m] = 0;
         d.halt_at[m] = -1;
-        d.err[m] = 0;
+        d.err[m] = bad ? QX_E_CODE : 0u;
     }
 }

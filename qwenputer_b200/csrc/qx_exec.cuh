@@ -57,6 +57,11 @@ struct QxDev {
     const qx_mma_tile *mma_tiles;
     const uint4 *tiledata;  // [tiles][128 rows][2] (a row: 16 bf16 weights)
     int32_t has_mma;        // the kernel allocates tensor memory
+    // merged readout and text tokens (QX_PLAN_FLAG_MERGED)
+    const uint32_t *feat_dim, *code_row, *text_words, *text_touch;
+    const float *text_base, *text_bits;
+    const int32_t *printable;
+    int32_t merged, q_fid, n_text, n_printable, n_text_touch, n_code, n_text_bits;
 };
 
 // per-machine error bits

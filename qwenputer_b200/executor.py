@@ -152,6 +152,21 @@ def program_image(prog, keep: list) -> Machine:
     return m
 
 
+def state_image(prog, x, anchor: int, n: int, ram, keep: list) -> Machine:
+    """A qx_machine for a machine in a given state (e.g. a firmware run to its park, as the text
+    bridge starts it: ERV/chipformer/rv/bridge.py:106-111): the program's ROM / DROM, and the
+    registers, PC (anchor, n) and 8,192 RAM words given."""
+    m = program_image(prog, keep)
+    ramw = np.ascontiguousarray(np.asarray(ram, np.uint32))
+    assert ramw.shape == (8192,)
+    keep.append(ramw)
+    m.ram = ramw.ctypes.data
+    for i in range(32):
+        m.x[i] = int(x[i]) if i else 0
+    m.anchor, m.n = int(anchor), int(n)
+    return m
+
+
 def snapshot_states(c, head_levels) -> list:
     """Executor2.load_init's host buffers (tritonexec.py:246-258): for each head sublayer level,
     a [V, 128, 128] fp32 array of the value heads' initial rows that the live graph's heads hold
@@ -278,10 +293,14 @@ class Executor:
         return x
 
     # ---- machine images / state ------------------------------------------------------------
-    def load_machines(self, row0: int, programs) -> None:
-        """core.snapshot + load_init of fresh program images into rows row0.. (on the device)."""
+    def load_machines(self, row0: int, programs, states=None) -> None:
+        """core.snapshot + load_init of program images into rows row0.. (on the device): fresh
+        programs, or (``states``: one (x, anchor, n, ram) per program) machines in those states."""
         keep: list = []
-        imgs = (Machine * len(programs))(*[program_image(p, keep) for p in programs])
+        if states is None:
+            imgs = (Machine * len(programs))(*[program_image(p, keep) for p in programs])
+        else:
+            imgs = (Machine * len(programs))(*[state_image(p, *st, keep) for p, st in zip(programs, states)])
         check(lib().qx_load_machines(self.h, C.c_int32(row0), C.c_int32(len(programs)), imgs,
                                      self._stream()), "qx_load_machines")
 

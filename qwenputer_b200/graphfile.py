@@ -40,6 +40,11 @@ A_REF = 2.0 ** 24  # ballast value (ir.py:39)
 A_BIT = 2.0 ** 7  # value of a set bit in a state row (ir.py:40)
 ONE = 0  # dim of the constant-one feature (ERV/chipformer/dsl/graph.py:29)
 FORMAT_VERSION = 1
+TEXT_TOKEN = 1 << 24  # a text token in the circuit's stream: TEXT_TOKEN | qid (ERV/chipformer/rv/spec.py:89)
+# a text token's bits (ERV/chipformer/rv/core.py:139-165): its text row's 16 bytes (bit 8k + i =
+# bit i of byte k), isTCO, isTCC, printable, then the 21 bits of its own output code (family Q,
+# payload = its printable index) when printable; TEXT_WORDS uint32 words per token
+TEXT_ROW_BITS, TEXT_NBITS, TEXT_WORDS = 128, 152, 5
 
 
 def _f32(x: float) -> np.float32:
@@ -138,6 +143,17 @@ class GraphData:
     table_names: np.ndarray  # str [T]
     table_head: np.ndarray  # int32 [T]: head index
     reg_cols: np.ndarray  # int32 [32, 8]: bit -> source columns (-1 padded)
+    # merged graphs (built with the text bridge, ERV/chipformer/rv/core.py:1128-1163): the
+    # prediction is read from the signs of the code dims (empty for a standalone graph, which
+    # reads fam_dims / pay_dims), the P3 echo family Q names text tokens, and text tokens
+    # (TEXT_TOKEN | qid) are embedded as text_base + sum of the rows of their set bits
+    code_dims: np.ndarray = dataclasses.field(default_factory=lambda: np.zeros(0, np.int32))
+    keep_dims: np.ndarray = dataclasses.field(default_factory=lambda: np.zeros(0, np.int32))
+    q_fid: np.ndarray = dataclasses.field(default_factory=lambda: np.full(1, -1, np.int64))  # [1]
+    printable: np.ndarray = dataclasses.field(default_factory=lambda: np.zeros(0, np.int32))  # Q payload -> qid
+    text_words: np.ndarray = dataclasses.field(default_factory=lambda: np.zeros((0, TEXT_WORDS), np.uint32))
+    text_base: np.ndarray = dataclasses.field(default_factory=lambda: np.zeros(0, np.float32))  # [F]
+    text_bits: np.ndarray = dataclasses.field(default_factory=lambda: np.zeros((0, 0), np.float32))  # [152, F]
 
     # ---- derived views -------------------------------------------------------------------
     def head_sublayers(self) -> list[int]:
@@ -168,6 +184,9 @@ class GraphData:
         """[n, D] float32 embeddings through the tabulated FreeRun rule (fastexec.py:305-307)."""
         out = np.zeros((len(toks), self.D), np.float32)
         for i, t in enumerate(toks):
+            if int(t) >= TEXT_TOKEN:
+                out[i, self.feat_dims] = self.text_embedding(int(t) - TEXT_TOKEN)
+                continue
             f, p = self.family_of(int(t))
             if self.fam_small[f]:
                 row = self.emb_table[self.fam_row0[f] + p]
@@ -176,6 +195,45 @@ class GraphData:
                 row = self.emb_base[f] + np.einsum("i,id->d", pay, self.emb_bits[f])
             out[i, self.feat_dims] = row
         return out
+
+    @property
+    def merged(self) -> bool:
+        return len(self.code_dims) > 0
+
+    def text_embedding(self, qid: int) -> np.ndarray:
+        """The feature row of text token qid: text_base + the rows of its set bits (summed in bit
+        order; exact values)."""
+        if not self.merged or not 0 <= qid < len(self.text_words):
+            raise ValueError(f"text token {qid} is not in this graph's text vocabulary")
+        w = self.text_words[qid]
+        row = self.text_base.astype(np.float32).copy()
+        for j in range(TEXT_NBITS):
+            if w[j >> 5] >> (j & 31) & 1:
+                row = row + self.text_bits[j]
+        return row
+
+    def decode(self, x: np.ndarray) -> int:
+        """The token a residual row predicts (FreeRun._step's rule, fastexec.py:298-307, for a
+        standalone graph; core.predictions' merged rule, core.py:1287-1304, for a merged one:
+        code dims > 0 are the bits, a Q code is the text token of printable payload p). -1: the
+        code names no token, or (merged) every code dim is 0 (the circuit does not predict)."""
+        nf, npay = int(self.fam_dims.size or 5), int(self.pay_dims.size or 16)
+        if self.merged:
+            v = x[self.code_dims]
+            if not np.any(v != 0):
+                return -1
+            bits = (v > 0).astype(np.int64)
+            nf = len(self.code_dims) - npay
+            fid = int(sum(int(b) << i for i, b in enumerate(bits[:nf])))
+            p = int(sum(int(b) << i for i, b in enumerate(bits[nf:])))
+            if fid == int(self.q_fid[0]):
+                return TEXT_TOKEN + int(self.printable[p]) if p < len(self.printable) else -1
+        else:
+            fid = int(sum(int(np.rint(x[d])) << i for i, d in enumerate(self.fam_dims)))
+            p = int(sum(int(np.rint(x[d])) << i for i, d in enumerate(self.pay_dims)))
+        if not 0 <= fid < len(self.fam_ids) or p >= int(self.fam_size[fid]):
+            return -1
+        return int(self.fam_ids[fid]) + p
 
     def family_of(self, t: int) -> tuple[int, int]:
         for f in range(len(self.fam_ids)):
@@ -217,13 +275,19 @@ def load_graph(path: str | Path) -> GraphData:
             kw[fld.name] = int(z[fld.name])
         elif fld.type == "Forms":
             kw[fld.name] = _forms_from_npz(fld.name, z)
-        else:
+        elif fld.name in z.files:
             kw[fld.name] = z[fld.name]
     return GraphData(**kw)
 
 
 def default_graph_path() -> Path:
+    """The standalone RV32IM machine shipped with the package."""
     return Path(__file__).parent / "plans" / "rv32im_graph.npz"
+
+
+def merged_graph_path() -> Path:
+    """The machine with the text bridge (merged readout, text tokens) over a byte-level vocabulary."""
+    return Path(__file__).parent / "plans" / "rv32im_merged_graph.npz"
 
 
 # ---- export from a live chipformer graph (needs the reference importable) -------------------
@@ -321,6 +385,7 @@ def export_graph(c) -> GraphData:
 
     names = [nm for nm in C.OUT_NAMES if nm in S.CONTROLS or nm in S.FAMILIES]
     assert names == C.OUT_NAMES[:len(names)], "skipped families must be the last ones"
+    merged = c.out_fam is None
     nf, nb = len(names), C.NPAY
     base = np.zeros((nf, len(feat_dims)))
     bits = np.zeros((nf, nb, len(feat_dims)))
@@ -345,6 +410,9 @@ def export_graph(c) -> GraphData:
         assert w == 1
         return int(d)
 
+    extra = {}
+    if merged:
+        extra = _export_text(c, feat_ids, feat_dims, emb)
     tnames = list(c.tables)
     hidx = {id(n): i for i, n in enumerate(heads)}
     reg_cols = np.full((32, 8), -1, np.int32)
@@ -374,10 +442,68 @@ def export_graph(c) -> GraphData:
         fam_ids=ids, fam_size=sizes, fam_small=small, fam_row0=row0,
         emb_base=base.astype(np.float32), emb_bits=bits.astype(np.float32),
         emb_table=np.asarray(table, np.float32).reshape(-1, len(feat_dims)),
-        fam_dims=np.asarray([dim_of(e) for e in c.out_fam], np.int32),
-        pay_dims=np.asarray([dim_of(e) for e in c.out_pay], np.int32),
+        fam_dims=np.asarray([dim_of(e) for e in c.out_fam] if not merged else [], np.int32),
+        pay_dims=np.asarray([dim_of(e) for e in c.out_pay] if not merged else [], np.int32),
         vocab=int(S.VOCAB),
         table_names=np.asarray(tnames),
         table_head=np.asarray([hidx[id(c.tables[t])] for t in tnames], np.int32),
         reg_cols=reg_cols,
+        **extra,
     )
+
+
+def _export_text(c, feat_ids: list, feat_dims: list, emb) -> dict:
+    """The merged graph's readout and text-token tables: code / keep dims, the Q family's id, the
+    printable tokens, and every text token's bits with the rows they add (the text row's byte
+    bits, the <tool_call> / </tool_call> flags, its own Q code when printable:
+    ERV/chipformer/rv/core.py:139-165).  Checked against the graph's own feature functions for
+    every text token of the vocabulary."""
+    from chipformer.rv import core as C
+
+    text = c.text
+    fcol = {d: j for j, d in enumerate(feat_dims)}
+    name = {c.dims[d].name: d for d in feat_ids}
+
+    def dim_of(e):
+        ((d, w),) = e.terms.items()
+        assert w == 1
+        return int(d)
+
+    code = [dim_of(e) for e in c.code]
+    F = len(feat_dims)
+    rows = np.zeros((TEXT_NBITS, F))
+    for k in range(16):
+        for i in range(8):
+            rows[8 * k + i, fcol[name[f"tb{k}.b{i}"]]] = 1.0
+    rows[128, fcol[name["isTCO"]]] = 1.0
+    rows[129, fcol[name["isTCC"]]] = 1.0
+    for j, d in enumerate(code):
+        rows[130, fcol[d]] = -C.CODE_AMP  # printable: every code dim -CODE_AMP ...
+        rows[131 + j, fcol[d]] = 2 * C.CODE_AMP  # ... + 2 CODE_AMP where its code bit is 1
+    base = emb([TEXT_TOKEN + text.n])[0]  # a text token with no bit set (beyond the vocabulary)
+    words = np.zeros((text.n, TEXT_WORDS), np.uint32)
+    for q in range(text.n):
+        rb = text.row_bytes(q)
+        bits = [rb[k] >> i & 1 for k in range(16) for i in range(8)]
+        p = text.printable_index(q)
+        bits += [int(q == text.TCO), int(q == text.TCC), int(p is not None)]
+        bits += C.code_bits("Q", p) if p is not None else [0] * (C.NFAM + C.NPAY)
+        for j, b in enumerate(bits):
+            if b:
+                words[q, j >> 5] |= np.uint32(1 << (j & 31))
+    # every text token's features through the bits equal the graph's own
+    want = emb([TEXT_TOKEN + q for q in range(text.n)])
+    for q in range(text.n):
+        got = base.copy()
+        for j in range(TEXT_NBITS):
+            if words[q, j >> 5] >> (j & 31) & 1:
+                got = got + rows[j]
+        if not np.array_equal(got, want[q]):
+            bad = np.flatnonzero(got != want[q])
+            raise AssertionError(f"text token {q}: feature dims {[feat_dims[b] for b in bad[:5]]} differ")
+    for a in (base, rows):
+        assert np.all(a.astype(np.float32).astype(np.float64) == a)
+    return dict(code_dims=np.asarray(code, np.int32), keep_dims=np.asarray(c.keep, np.int32),
+                q_fid=np.asarray([C.OUT_NAMES.index("Q")], np.int64),
+                printable=np.asarray(text.printable, np.int32), text_words=words,
+                text_base=base.astype(np.float32), text_bits=rows.astype(np.float32))

@@ -57,7 +57,7 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 14
+VERSION = 15
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -77,7 +77,10 @@ UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most t
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
        "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
-       "TABLES", "REG_COLS", "FAM_TOUCH_PTR", "FAM_TOUCH", "MMA_PHASES", "MMA_TILES", "TILEDATA"]
+       "TABLES", "REG_COLS", "FAM_TOUCH_PTR", "FAM_TOUCH", "MMA_PHASES", "MMA_TILES", "TILEDATA",
+       "FEAT_DIM", "CODE_ROW", "TEXT_WORDS", "TEXT_BASE", "TEXT_BITS", "PRINTABLE", "TEXT_TOUCH",
+       "MERGED_INFO"]
+N_SEC = 48  # section slots in the header
 TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
                + [f"quo{i}" for i in range(4)] + [f"rom{i}" for i in range(32)]
                + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
@@ -93,6 +96,8 @@ MMA_M, MMA_K = 128, 16
 MMA_MAX_KB = 16
 MMA_MAX_FB = 8
 FLAG_MMA = 1  # header flag: the plan has tensor-core form phases
+FLAG_MERGED = 2  # header flag: merged readout (code-dim signs, text tokens; MERGED_INFO)
+DEFERRED = 0x80000000  # FEAT_ROW flag: the feature is loaded where it is first used (low bits: dim)
 
 DT = {
     "phase": np.dtype([("kind", "<u4"), ("a", "<u4"), ("b", "<u4"), ("c", "<u4")]),
@@ -106,7 +111,7 @@ DT = {
                      ("t1", "<u4"), ("pad0", "<u4"), ("pad1", "<u4")]),
     "tile": np.dtype([("data", "<u4"), ("fb", "<u4"), ("kb", "<u4"), ("acc", "<u4")]),
 }
-HEADER = struct.Struct("<QII" + "I" * 16 + "32Q32Q")
+HEADER = struct.Struct("<QII" + "I" * 16 + "48Q48Q")
 
 
 def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int) -> int:
@@ -142,6 +147,10 @@ def split_form(forms, i: int, D: int) -> tuple[tuple, float]:
     return tuple(sorted(terms)), float(np.float32(const))
 
 
+class RowsExhausted(AssertionError):
+    """The residual slots do not leave enough scratch rows in shared memory."""
+
+
 class Plan:
     """The compiled program (numpy arrays per section) and its statistics."""
 
@@ -151,7 +160,7 @@ class Plan:
         self.stats: dict = {}
 
     def blob(self) -> bytes:
-        offs, cnts, parts = [0] * 32, [0] * 32, []
+        offs, cnts, parts = [0] * N_SEC, [0] * N_SEC, []
         pos = (HEADER.size + 255) // 256 * 256
         for i, name in enumerate(SEC):
             a = np.ascontiguousarray(self.sec[name])
@@ -172,11 +181,25 @@ class Plan:
 
 
 def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAULT,
-                 ksel_slots: int = 16, cluster: int = 1, tc: bool = False) -> Plan:
+                 ksel_slots: int | None = None, cluster: int = 1, tc: bool = False,
+                 defer: bool | None = None) -> Plan:
     """The phase program and stream of the graph, for CTAs of ``nw`` warps; one group of 32
     machines runs on a cluster of ``cluster`` CTAs, so stream records are balanced over
     nw * cluster warps.  ``tc``: linear forms run as tensor-core phases (tcgen05) instead of
-    stream records on the CUDA cores (every CTA of a cluster then computes all of them)."""
+    stream records on the CUDA cores (every CTA of a cluster then computes all of them).
+    ``defer`` (default: merged graphs): a token feature gets its row only from the sublayer that
+    first uses it, loaded there from the executor's x (where the decode writes it), so that the
+    rows of features used late are free before; ``ksel_slots`` (default 16, fewer when the rows
+    do not fit otherwise): key heads one key-select phase serves."""
+    if defer is None:
+        defer = g.merged
+    if ksel_slots is None:
+        for k in (16, 12, 8):
+            try:
+                return compile_plan(g, smem_rows, nw, k, cluster, tc, defer)
+            except RowsExhausted:
+                if k == 8:
+                    raise
     assert 1 <= cluster <= 8, cluster
     # the kernel takes the ONE dim as 1 on every machine: no sublayer may write it
     assert ONE not in set(int(d) for d in g.ffn_out) and ONE not in set(int(d) for d in g.out_dim)
@@ -246,9 +269,21 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
             # a dim read before its first write holds its input value (0) until then
             birth[d] = min(birth.get(d, INF), lv)
             last[d] = max(last.get(d, 0), lv)
-    for d in list(g.fam_dims) + list(g.pay_dims) + [ONE]:
+    for d in list(g.fam_dims) + list(g.pay_dims) + [int(x) for x in g.code_dims] + [ONE]:
         birth.setdefault(int(d), 0)
         last[int(d)] = INF
+    deferred = set()
+    if defer:
+        # a feature's first use (a read, or a write that adds to its input value) decides where
+        # it is loaded; features first used by the first sublayer stay born with the token
+        first_use = {}
+        for lv in levels:
+            for d in writes[lv] | {dd for _, dd in reads[lv]}:
+                first_use.setdefault(d, lv)
+        for d in feat:
+            if d != ONE and d in first_use and first_use[d] > levels[0]:
+                birth[d] = first_use[d]
+                deferred.add(d)
     last_write = {}
     for lv in levels:
         for d in writes[lv]:
@@ -277,7 +312,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         slot[k] = s
         heapq.heappush(active, (last[k], s))
     n_scratch = smem_rows - n_slots
-    assert n_scratch >= 64, f"{n_slots} residual slots leave too little scratch"
+    if n_scratch < 64:
+        raise RowsExhausted(f"{n_slots} residual slots leave too little scratch")
     occupied = defaultdict(set)
     for k in items:
         for lv in levels:
@@ -468,7 +504,17 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     step_prog.append((PH["LOADX"], 0, len(born0), 0))
 
     for lv, kind in zip(levels, kinds):
-        born = sorted(d for d in birth if not isinstance(d, tuple) and birth[d] == lv and lv > 0)
+        born_all = sorted(d for d in birth if not isinstance(d, tuple) and birth[d] == lv and lv > 0)
+        # deferred features born here are read by this sublayer's first phase: loaded (from x,
+        # in both modes) behind a barrier of their own
+        born_f = [d for d in born_all if d in deferred]
+        born = [d for d in born_all if d not in deferred]
+        if born_f:
+            p0 = len(pairs_l)
+            pairs_l.extend((W(slot[d]), d) for d in born_f)
+            run_prog.append((PH["LOADX"], p0, len(born_f), 0))
+            step_prog.append((PH["LOADX"], p0, len(born_f), 0))
+            stats["deferred_loads"] += len(born_f)
         tmp = sorted(slot[k] for (l2, d), k in temps.items() if l2 == lv)
         r0 = len(rows_l)
         rows_l.extend(W(slot[d]) for d in born)
@@ -798,9 +844,25 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     s["OUT_W"] = np.asarray(out_w_l, np.float32)
     s["HL_V"] = np.asarray([len(g.vheads_at(lv)) for lv in head_levels], np.uint32)
     s["HL_NE"] = np.asarray([max(1, n) for n in hl_ne], np.uint32)
-    s["FAM_ROW"] = np.asarray([W(slot[int(d)]) for d in g.fam_dims], np.uint32)
-    s["PAY_ROW"] = np.asarray([W(slot[int(d)]) for d in g.pay_dims], np.uint32)
-    s["FEAT_ROW"] = np.asarray([W(slot[d]) for d in feat], np.uint32)
+    s["FAM_ROW"] = np.asarray([W(slot[int(d)]) for d in g.fam_dims] or [0], np.uint32)
+    s["PAY_ROW"] = np.asarray([W(slot[int(d)]) for d in g.pay_dims] or [0], np.uint32)
+    s["FEAT_ROW"] = np.asarray([(DEFERRED | d) if d in deferred else W(slot[d]) for d in feat], np.uint32)
+    s["FEAT_DIM"] = np.asarray(feat, np.uint32)
+    # merged readout and text tokens
+    merged = g.merged
+    s["CODE_ROW"] = np.asarray([W(slot[int(d)]) for d in g.code_dims] or [0], np.uint32)
+    s["TEXT_WORDS"] = np.ascontiguousarray(g.text_words if merged else np.zeros((1, 5), np.uint32)).reshape(-1)
+    s["TEXT_BASE"] = np.asarray(g.text_base if merged else np.zeros(1), np.float32)
+    s["TEXT_BITS"] = np.ascontiguousarray(g.text_bits if merged else np.zeros((1, 1)), np.float32).reshape(-1)
+    s["PRINTABLE"] = np.asarray(g.printable if merged else [0], np.int32)
+    if merged:
+        tt = np.flatnonzero((np.asarray(g.text_base) != 0) | (np.asarray(g.text_bits) != 0).any(axis=0))
+    else:
+        tt = np.zeros(0, np.int64)
+    s["TEXT_TOUCH"] = np.asarray(tt if len(tt) else [0], np.uint32)
+    s["MERGED_INFO"] = np.asarray([int(g.q_fid[0]) if merged else 0, len(g.text_words) if merged else 0,
+                                   len(g.printable) if merged else 0, len(tt), len(g.code_dims),
+                                   g.text_bits.shape[0] if merged else 0, 0, 0], np.uint32)
     s["FAM_IDS"] = np.asarray(g.fam_ids, np.int32)
     s["FAM_SIZE"] = np.asarray(g.fam_size, np.int32)
     s["FAM_ROW0"] = np.asarray([int(r) if sm else -1 for r, sm in zip(g.fam_row0, g.fam_small)],
@@ -833,8 +895,10 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
                  n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
                  vocab=int(g.vocab), n_born0=len(born0), cluster=cluster,
-                 flags=FLAG_MMA if mma_l else 0)
+                 flags=(FLAG_MMA if mma_l else 0) | (FLAG_MERGED if merged else 0))
     stats["n_slots"] = n_slots
+    stats["ksel_slots"] = ksel_slots
+    stats["deferred_features"] = len(deferred)
     stats["n_scratch"] = n_scratch
     stats["phases_run"] = len(run_prog)
     stats["barriers_run"] = sum(1 for k, *_ in run_prog if not k & NOSYNC and k != PH["END"])

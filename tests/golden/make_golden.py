@@ -25,6 +25,12 @@ Writes:
   gdn_general.npz  the same function on unit-norm Gaussian keys (every head), and on a mix drawn
                  like the 1,024 x 48-head step (95% one-hot keys, alpha 90 / 5 / 5% at 1 / 0.5 /
                  0); one-hot queries
+  merged.npz     the machine with the text bridge (``core.build(text=ByteVocab())``, the graph
+                 file ``rv32im_merged_graph.npz``): firmware assembled by the reference's assembler,
+                 parked (``bridge.park``), then driven by ``bridge.Session`` (text, a tool call,
+                 the run with its echoes); per session the parked state, the token stream, who
+                 owns each position, and ``ir.evaluate`` residual hashes and ``core.predictions``
+                 (``--only merged`` rewrites only this file)
   hf_residual.npz  the compiled stack emitted as stock transformers Qwen3_5ForCausalLM weights
                  (the reference's ``hf.build_model``, bf16, torch kernels), the snapshot injected
                  into its cache, decoded token by token: the residual of every IR dim after the
@@ -382,18 +388,90 @@ def hf_goldens(ref_root: str) -> None:
     np.savez_compressed(HERE / "hf_residual.npz", **out)
 
 
+# firmware for the bridge sessions: park at once; each run (GO) prints the first byte of every
+# captured text row (TEXT_ADDR + 16 i, i = 1, 2, ..), then a special token (putchar(256 + k)),
+# then parks again (exit ecall) and loops
+ECHO_FIRMWARE = """_start:
+      li a7, 93
+      ecall
+loop: li t0, 0x8010
+next: lbu a0, 0(t0)
+      beq a0, zero, done
+      li a7, 1
+      ecall
+      addi t0, t0, 16
+      j next
+done: li a0, 257
+      li a7, 1
+      ecall
+      li a7, 93
+      ecall
+      j loop"""
+
+
+def merged_goldens(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    sys.path.insert(0, str(REPO))
+    import numpy as np
+    from chipformer.q35 import ir
+    from chipformer.rv import bridge, core, ref
+    from chipformer.rv.asm import assemble
+
+    from qwenputer_b200.plans.export_rv32im import ByteVocab
+
+    T = ByteVocab()
+    c = core.build(text=T)
+    p = assemble(ECHO_FIRMWARE)
+    prog = SimpleNamespace(text=[int(w) for w in p.text], data=bytes(p.data), data_base=int(p.data_base),
+                           entry=int(p.entry), rodata=bytes(getattr(p, "rodata", b"")))
+    enc = lambda b: [int(x) for x in b]  # bytes -> the byte tokens of ByteVocab
+    w0 = 256 + 8  # the first multi-byte token
+    sessions = {
+        "echo_short": [enc(b"hi "), [T.TCO] + enc(b"7*6") + [T.TCC]],
+        "echo_words": [enc(b"calc: ") + [w0 + 5, w0 + 17], [T.TCO] + enc(b"\n12345678*987654321\n") + [T.TCC]],
+    }
+    out = {"names": np.asarray(sorted(sessions)), "text": np.asarray(prog.text, np.uint32),
+           "data": np.frombuffer(prog.data, np.uint8), "data_base": np.int64(prog.data_base),
+           "entry": np.int64(prog.entry)}
+    for name, parts in sorted(sessions.items()):
+        m = ref.Machine.from_program(prog)
+        bridge.park(m)
+        core.snapshot(c, m)
+        out[f"{name}.x"] = np.asarray(m.x, np.uint32)
+        out[f"{name}.anchor_n"] = np.asarray([m.anchor, m.n], np.uint32)
+        out[f"{name}.ram"] = np.asarray(m.ram, np.uint32)
+        s_ = bridge.Session(T, m)
+        for q in parts:
+            s_.qwen(q)
+        toks = s_.toks
+        t0 = time.time()
+        mat = ir.evaluate(c, toks, check=False)
+        pred = core.predictions(c, mat)
+        m32 = mat.astype(np.float32)
+        assert np.all(m32.astype(np.float64) == mat), "residual not exact in float32"
+        own = s_.own
+        assert all(pred[i] == toks[i + 1] for i in range(len(toks) - 1) if own[i])
+        out[f"{name}.tokens"] = np.asarray(toks, np.int64)
+        out[f"{name}.own"] = np.asarray(own, bool)
+        out[f"{name}.hash"] = np.asarray([fnv1a_bytes(r.tobytes()) for r in m32], np.uint64)
+        out[f"{name}.head"] = m32[:4]
+        out[f"{name}.pred"] = np.asarray(pred, np.int64)
+        print(f"  merged session {name}: {len(toks)} tokens, {sum(own)} owned, {time.time() - t0:.1f} s", flush=True)
+    np.savez_compressed(HERE / "merged.npz", **out)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("ref_root", nargs="?", default=os.environ.get("QX_REFERENCE_ROOT"),
                     help="the reference's experimental/riscv directory (or QX_REFERENCE_ROOT)")
-    ap.add_argument("--only", choices=["gdn", "hf"], default=None)
+    ap.add_argument("--only", choices=["gdn", "hf", "merged"], default=None)
     a = ap.parse_args()
     if a.only == "gdn":
         gdn_goldens()
-    elif a.only == "hf":
+    elif a.only in ("hf", "merged"):
         if not a.ref_root:
             ap.error("give the reference's experimental/riscv directory or set QX_REFERENCE_ROOT")
-        hf_goldens(a.ref_root)
+        (hf_goldens if a.only == "hf" else merged_goldens)(a.ref_root)
     else:
         if not a.ref_root:
             ap.error("give the reference's experimental/riscv directory or set QX_REFERENCE_ROOT")

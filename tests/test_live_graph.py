@@ -118,3 +118,15 @@ def test_executor2_binding_constructs_from_live_graph(live):
     x = ex.embed([0, 0])
     ex.step(x)
     torch.cuda.synchronize()
+
+
+def test_export_of_live_merged_graph_equals_shipped_file():
+    """graphfile.export_graph(core.build(text=ByteVocab())) == plans/rv32im_merged_graph.npz, field
+    by field: the merged readout (code dims, keep dims, the Q family) and every text token's
+    bits, which the export checks against the graph's own feature functions."""
+    from chipformer.rv import core
+
+    from qwenputer_b200.graphfile import export_graph, load_graph, merged_graph_path
+    from qwenputer_b200.plans.export_rv32im import ByteVocab
+
+    _equal(export_graph(core.build(text=ByteVocab())), load_graph(merged_graph_path()), "GraphData")
