@@ -177,7 +177,7 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     if (h.cnt[QX_S_FEAT_DIM] != h.n_feat || h.cnt[QX_S_MERGED_INFO] != 8)
         return fail(QX_ERR_INVALID_PLAN, "feature dims or merged-readout facts missing");
     if (h.cnt[QX_S_HL_V] != h.n_head_levels || h.cnt[QX_S_FEAT_ROW] != h.n_feat ||
-        h.cnt[QX_S_FAM_ROW] != h.n_fam || h.cnt[QX_S_PAY_ROW] != h.n_pay)
+        h.cnt[QX_S_FAM_ROW] < h.n_fam || h.cnt[QX_S_PAY_ROW] < h.n_pay)
         return fail(QX_ERR_INVALID_PLAN, "section counts disagree with the header");
     return QX_OK;
 }

@@ -177,3 +177,26 @@ def test_gdn_step_rejects_bad_shapes_before_any_launch():
     # right shapes, but no CUDA device holds them: still rejected on the host
     with pytest.raises(ValueError, match="CUDA device"):
         gdn_check_args(**ok)
+
+
+@pytest.mark.parametrize("merged,tc,cluster", [(False, False, 1), (False, True, 1), (True, False, 1),
+                                               (True, True, 4), (False, False, 8)])
+def test_library_accepts_every_plan_variant(graph, merged, tc, cluster):
+    """qx_create validates a plan before it touches a device: every plan the compiler emits
+    (standalone or merged graph, CUDA-core or tensor-core forms, cluster sizes) passes the
+    library's validation (without a GPU the call then fails on the device, status 3)."""
+    import torch
+
+    from qwenputer_b200 import build
+    from qwenputer_b200.graphfile import load_graph, merged_graph_path
+    from qwenputer_b200.plan import compile_plan
+
+    if torch.cuda.is_available():
+        pytest.skip("checks the validation path that runs before the device is touched")
+    lib = C.CDLL(str(build.build()))
+    lib.qx_last_error.restype = C.c_char_p
+    g = load_graph(merged_graph_path()) if merged else graph
+    blob = compile_plan(g, cluster=cluster, tc=tc).blob()
+    h = C.c_void_p()
+    st = lib.qx_create(blob, C.c_size_t(len(blob)), 4, 0, C.byref(h))
+    assert st == 3, (st, lib.qx_last_error())
