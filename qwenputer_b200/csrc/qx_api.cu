@@ -700,8 +700,12 @@ qx_status qx_run(qx_t *ex, int32_t n_tokens, int32_t *tokens, void *stream) {
 qx_status qx_set_tokens(qx_t *ex, int32_t row0, int32_t n, const int32_t *tok, void *stream) {
     if (!ex || !tok || row0 < 0 || n < 0 || row0 + n > ex->B) return fail(QX_ERR_INVALID_ARG, "qx_set_tokens");
     if (n == 0) return QX_OK;
-    for (int i = 0; i < n; i++)
-        if (tok[i] < 0 || (uint32_t)tok[i] >= ex->hdr.vocab) return fail(QX_ERR_INVALID_ARG, "token %d", tok[i]);
+    for (int i = 0; i < n; i++) {
+        // a chip token, or (merged graphs) a text token of the graph's vocabulary
+        const bool text = ex->d.merged && tok[i] >= QX_TEXT_TOKEN && tok[i] - QX_TEXT_TOKEN < ex->d.n_text;
+        if (!text && (tok[i] < 0 || (uint32_t)tok[i] >= ex->hdr.vocab))
+            return fail(QX_ERR_INVALID_ARG, "token %d is neither a chip token nor a text token of the graph", tok[i]);
+    }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     CU(cudaMemcpyAsync(ex->dtok, tok, (size_t)n * 4, cudaMemcpyHostToDevice, st));
     qx_embed_kernel<<<n, 256, 0, st>>>(ex->d, row0, n, ex->dtok);
