@@ -24,28 +24,31 @@ sys.dont_write_bytecode = True  # the reference tree is read-only
 SPECIAL_TOKENS = ["<tool_call>", "</tool_call>", "<tool_response>", "</tool_response>", "<think>",
                   "</think>", "<|im_start|>", "<|im_end|>"]
 PRINTED_SPECIALS = ["<tool_response>", "</tool_response>", "<think>", "</think>"]  # putchar(256 + k)
+# the pieces Qwen's tool-call syntax is written in (each within a 16-byte text row)
+CALL_TOKENS = ["<function=", "calc>", "<parameter=", "expression>", "</parameter>", "</function>"]
 
 
 class ByteVocab:
     """The text bridge's view of a vocabulary (the interface of ``chipformer.rv.bridge.Text``,
     ERV/chipformer/rv/bridge.py:45-91): token q < 256 is the byte q, then Qwen's special tokens,
-    then ``n_words`` seeded multi-byte tokens (2 to 8 printable ASCII bytes).  ``printable[b]``
-    is the token of byte b (b < 256), then the four specials the firmware prints."""
+    then the tool-call pieces (CALL_TOKENS), then ``n_words`` seeded multi-byte tokens (2 to 8
+    printable ASCII bytes).  ``printable[b]`` is the token of byte b (b < 256), then the four
+    specials the firmware prints."""
 
     def __init__(self, n_words: int = 4096, seed: int = 35):
         from chipformer.rv import spec as S
 
         self._row = S.TEXT_ROW
         rng = random.Random(seed)
-        self.bytes = [bytes([b]) for b in range(256)] + [s.encode() for s in SPECIAL_TOKENS]
+        self.bytes = [bytes([b]) for b in range(256)] + [s.encode() for s in SPECIAL_TOKENS + CALL_TOKENS]
         seen = set(self.bytes)
-        while len(self.bytes) < 256 + len(SPECIAL_TOKENS) + n_words:
+        while len(self.bytes) < 256 + len(SPECIAL_TOKENS) + len(CALL_TOKENS) + n_words:
             w = bytes(rng.randrange(0x21, 0x7F) for _ in range(rng.randint(2, 8)))
             if w not in seen:
                 seen.add(w)
                 self.bytes.append(w)
         self.n = len(self.bytes)
-        ids = {s: 256 + i for i, s in enumerate(SPECIAL_TOKENS)}
+        ids = {s: 256 + i for i, s in enumerate(SPECIAL_TOKENS + CALL_TOKENS)}
         self.ids = ids
         self.TCO, self.TCC = ids["<tool_call>"], ids["</tool_call>"]
         self.printable = list(range(256)) + [ids[s] for s in PRINTED_SPECIALS]

@@ -30,7 +30,10 @@ Writes:
                  parked (``bridge.park``), then driven by ``bridge.Session`` (text, a tool call,
                  the run with its echoes); per session the parked state, the token stream, who
                  owns each position, and ``ir.evaluate`` residual hashes and ``core.predictions``
-                 (``--only merged`` rewrites only this file)
+                 (``--only merged`` rewrites only this file and calc.npz)
+  calc.npz       the calculator firmware (qwenputer_b200/calc.py) in bridge sessions on the merged
+                 machine: tool calls A*B, the reference evaluator's residual hashes and the owned
+                 tokens (checked against A*B)
   hf_residual.npz  the compiled stack emitted as stock transformers Qwen3_5ForCausalLM weights
                  (the reference's ``hf.build_model``, bf16, torch kernels), the snapshot injected
                  into its cache, decoded token by token: the residual of every IR dim after the
@@ -425,7 +428,9 @@ def merged_goldens(ref_root: str) -> None:
     prog = SimpleNamespace(text=[int(w) for w in p.text], data=bytes(p.data), data_base=int(p.data_base),
                            entry=int(p.entry), rodata=bytes(getattr(p, "rodata", b"")))
     enc = lambda b: [int(x) for x in b]  # bytes -> the byte tokens of ByteVocab
-    w0 = 256 + 8  # the first multi-byte token
+    from qwenputer_b200.plans.export_rv32im import CALL_TOKENS, SPECIAL_TOKENS
+
+    w0 = 256 + len(SPECIAL_TOKENS) + len(CALL_TOKENS)  # the first seeded multi-byte token
     sessions = {
         "echo_short": [enc(b"hi "), [T.TCO] + enc(b"7*6") + [T.TCC]],
         "echo_words": [enc(b"calc: ") + [w0 + 5, w0 + 17], [T.TCO] + enc(b"\n12345678*987654321\n") + [T.TCC]],
@@ -458,6 +463,62 @@ def merged_goldens(ref_root: str) -> None:
         out[f"{name}.pred"] = np.asarray(pred, np.int64)
         print(f"  merged session {name}: {len(toks)} tokens, {sum(own)} owned, {time.time() - t0:.1f} s", flush=True)
     np.savez_compressed(HERE / "merged.npz", **out)
+    calc_goldens(c, T)
+
+
+# two 18-digit operands each, so that every session reaches its </tool_call> at the same position
+CALC_CASES = [(123456789012345678, 987654321098765432), (999999999999999999, 888888888888888888)]
+
+
+def calc_tool_call(T, a: int, b: int) -> list[int]:
+    """Qwen's tool-call syntax naming calc with the expression A*B, in ByteVocab tokens."""
+    ids = T.ids
+    return ([T.TCO, 10, ids["<function="], ids["calc>"], 10, ids["<parameter="], ids["expression>"], 10]
+            + list(str(a).encode()) + [ord("*")] + list(str(b).encode())
+            + [10, ids["</parameter>"], 10, ids["</function>"], 10, T.TCC])
+
+
+def calc_goldens(c, T) -> None:
+    """calc.npz: the calculator firmware (qwenputer_b200/calc.py) on the merged machine, parked,
+    then a bridge session per CALC_CASES (a little text, the tool call, the run); the token
+    stream, who owns each position, ir.evaluate residual hashes, and the firmware's printed
+    bytes checked against A*B."""
+    import numpy as np
+    from chipformer.q35 import ir
+    from chipformer.rv import bridge, core, ref
+
+    from qwenputer_b200.calc import calc_program, expected_response
+
+    p = calc_program()
+    prog = SimpleNamespace(text=[int(w) for w in p.text], data=b"", data_base=int(p.data_base),
+                           entry=int(p.entry), rodata=b"")
+    out = {"names": np.asarray([f"calc{i}" for i in range(len(CALC_CASES))]),
+           "text": np.asarray(prog.text, np.uint32)}
+    for i, (a, b) in enumerate(CALC_CASES):
+        name = f"calc{i}"
+        m = ref.Machine.from_program(prog)
+        bridge.park(m)
+        core.snapshot(c, m)
+        out[f"{name}.x"] = np.asarray(m.x, np.uint32)
+        out[f"{name}.anchor_n"] = np.asarray([m.anchor, m.n], np.uint32)
+        out[f"{name}.ram"] = np.asarray(m.ram, np.uint32)
+        s_ = bridge.Session(T, m)
+        s_.qwen(list(b"result: "))
+        s_.qwen(calc_tool_call(T, a, b))
+        assert b"".join(T.bytes[q] for q in s_.runs[-1][:-1]) == expected_response(a, b)
+        toks, own = s_.toks, s_.own
+        t0 = time.time()
+        mat = ir.evaluate(c, toks, check=False)
+        pred = core.predictions(c, mat)
+        assert all(pred[j] == toks[j + 1] for j in range(len(toks) - 1) if own[j])
+        m32 = mat.astype(np.float32)
+        assert np.all(m32.astype(np.float64) == mat)
+        out[f"{name}.a_b"] = np.asarray([a, b], np.uint64)
+        out[f"{name}.tokens"] = np.asarray(toks, np.int64)
+        out[f"{name}.own"] = np.asarray(own, bool)
+        out[f"{name}.hash"] = np.asarray([fnv1a_bytes(r.tobytes()) for r in m32], np.uint64)
+        print(f"  calc session {name}: {len(toks)} tokens, {sum(own)} owned, {time.time() - t0:.1f} s", flush=True)
+    np.savez_compressed(HERE / "calc.npz", **out)
 
 
 if __name__ == "__main__":

@@ -121,3 +121,76 @@ def test_merged_free_run_through_a_tool_call(qx, mgraph, z, tc):
         assert not own[-1] and got[len(want)] == -1
         assert sum(v >= TEXT_TOKEN for v in want) >= 3  # echoes were decoded as text tokens
         assert ex.errors() == 0
+
+
+@pytest.mark.parametrize("batch", [2, 64])
+def test_calc_tool_call_free_run(qx, mgraph, batch):
+    """The calculator firmware through the bridge on the device (tests/golden/calc.npz): the
+    session teacher-forced up to </tool_call>, then the device runs on its own; every token it
+    generates equals the reference session's until the circuit hands the stream back, and the
+    echoed text is A*B's tool response.  batch 64: the two sessions repeated over 64 machines
+    (the merged workload's batch: two groups of 32 machines on clusters of CTAs)."""
+    from qwenputer_b200.calc import calc_program, expected_response
+    from qwenputer_b200.graphfile import TEXT_TOKEN
+
+    zc = np.load(GOLDEN / "calc.npz")
+    names = [str(n) for n in zc["names"]]
+    rows = [names[i % len(names)] for i in range(batch)]
+    p = calc_program()
+    ex = qx.Executor(mgraph, batch=batch)
+    ex.load_machines(0, [p] * batch, states=[(zc[f"{n}.x"], int(zc[f"{n}.anchor_n"][0]),
+                                              int(zc[f"{n}.anchor_n"][1]), zc[f"{n}.ram"]) for n in rows])
+    toks = {n: zc[f"{n}.tokens"] for n in names}
+    # </tool_call>: the first text token the circuit owns (both sessions put it at one position)
+    tcc = {n: int(next(i for i, v in enumerate(toks[n]) if v >= TEXT_TOKEN and zc[f"{n}.own"][i])) for n in names}
+    assert len(set(tcc.values())) == 1
+    for t in range(tcc[names[0]] + 1):  # teacher-forced through </tool_call>
+        ex.set_tokens(0, [int(toks[n][t]) for n in rows])
+        ex.step(ex.x)
+    go = [mgraph.decode(v) for v in ex.x.cpu().numpy()]
+    assert all(g == int(toks[n][tcc[n] + 1]) for g, n in zip(go, rows))
+    n_run = max(len(toks[n]) - tcc[n] for n in names)
+    ex.set_tokens(0, go)
+    out = torch.empty(n_run, batch, dtype=torch.int32, device="cuda")
+    ex.run(n_run, out)
+    got = out.cpu().numpy().T.astype(np.int64)
+    for r, n in enumerate(rows):
+        want = toks[n][tcc[n] + 2:]
+        assert np.array_equal(got[r, :len(want)], want), (r, n, int(np.argmax(got[r, :len(want)] != want)))
+        echo = [int(v) - TEXT_TOKEN for v in want if v >= TEXT_TOKEN]
+        a, b = (int(v) for v in zc[f"{n}.a_b"])
+        assert b"".join(mgraph_bytes(mgraph, q) for q in echo[:-1]) == expected_response(a, b)
+    assert ex.errors() == 0
+
+
+def mgraph_bytes(g, q: int) -> bytes:
+    """A text token's bytes, from its 128 text-row bits in the graph."""
+    w = g.text_words[q]
+    row = bytes(sum(((int(w[(8 * k + i) >> 5]) >> ((8 * k + i) & 31)) & 1) << i for i in range(8))
+                for k in range(16))
+    return row.rstrip(b"\0")
+
+
+def test_park_matches_reference_parked_state(qx):
+    """rvbatch.park (a standalone executor free running the firmware to its exit ecall, the state
+    read back) gives the parked state the reference's bridge.park gave (tests/golden/calc.npz)."""
+    from qwenputer_b200 import rvbatch
+    from qwenputer_b200.calc import calc_program
+
+    zc = np.load(GOLDEN / "calc.npz")
+    (x, anchor, n, ram), = rvbatch.park([calc_program()])
+    assert list(x)[1:] == [int(v) for v in zc["calc0.x"]][1:]
+    assert (anchor, n) == tuple(int(v) for v in zc["calc0.anchor_n"])
+    assert np.array_equal(ram, zc["calc0.ram"])
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_conversations_with_qwen_layers(qx, fp8):
+    """The merged workload end to end on a small case: 2 conversations of 96 tokens ending in a
+    calc tool call, Qwen3.5-4B-shaped layers (4 of them here, random weights; bf16 or fp8 e4m3)
+    reading the text, the executor running the calls: both tool responses are A*B's."""
+    from qwenputer_b200 import rvbatch
+
+    r = rvbatch.run(batch=2, length=96, fp8=fp8, layers=4, seed=3, chunk=1024)
+    assert r["rows_correct"] == 2 and r["device_errors"] == 0
+    assert r["fp8_linears"] > 0 if fp8 else r["fp8_linears"] == 0

@@ -113,3 +113,26 @@ def test_merged_plan_matches_oracle(mgraph, moracle, z, cluster, tc):
         moracle.step(ost, emb, nthreads=1)
         bad = np.argwhere(x != emb)
         assert not len(bad), (t, bad[:5])
+
+
+@pytest.mark.parametrize("case", ["calc0", "calc1"])
+def test_oracle_runs_calc_tool_call(mgraph, moracle, case):
+    """The calculator firmware (qwenputer_b200/calc.py) called through the bridge (tests/golden/
+    calc.npz): the oracle's residual hashes to the reference evaluator's at every position of
+    the session, and the merged readout predicts every token the circuit owns."""
+    zc = np.load(GOLDEN / "calc.npz")
+    from qwenputer_b200.calc import calc_program
+
+    p = calc_program()
+    assert np.array_equal(p.text, zc["text"])  # the firmware the goldens were made with
+    m = oracle.Machine(p.text, b"", p.data_base, b"", p.entry)
+    m.run()  # parked
+    st = moracle.new_state(1)
+    moracle.snapshot(st, 0, m)
+    toks, own, hashes = zc[f"{case}.tokens"], zc[f"{case}.own"], zc[f"{case}.hash"]
+    for t, tok in enumerate(toks):
+        x = mgraph.embed([int(tok)])
+        moracle.step(st, x, nthreads=1)
+        assert oracle.fnv1a(x[0].view(np.uint32)) == int(hashes[t]), t
+        if own[t] and t + 1 < len(toks):
+            assert mgraph.decode(x[0]) == int(toks[t + 1]), t
