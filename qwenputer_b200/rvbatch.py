@@ -146,8 +146,9 @@ def qwen_text_model(vocab: int, layers: int = 32, fp8: bool = False, seed: int =
 def park(programs, max_tokens: int = 4096) -> list:
     """Each firmware run from its image to its first park (the exit ecall: HALT), as the bridge
     starts it (ERV/chipformer/rv/bridge.py:106-111): free running on a standalone executor one
-    token a launch until every machine has emitted HALT; the states (x, anchor, n, RAM) read back
-    from the heads."""
+    token a launch; a machine's state (x, anchor, n, RAM) is read back from the heads once its
+    HALT has been consumed as an input too (a record commits as its tokens are read: the exit's
+    n + 1, ref.py:526-529, lands then)."""
     import torch
 
     from .executor import Executor
@@ -159,17 +160,17 @@ def park(programs, max_tokens: int = 4096) -> list:
     go = int(g.fam_ids[list(g.fam_names).index("GO")])
     ex.set_tokens(0, [go] * len(programs))
     one = torch.empty(1, len(programs), dtype=torch.int32, device=ex.dev)
+    out: list = [None] * len(programs)
     for _ in range(max_tokens):
         ex.run(1, one)
-        if bool((ex.halt_at >= 0).all()):
-            break
-    else:
-        raise RuntimeError("a firmware did not park")
-    out = []
-    for r in range(len(programs)):
-        st = ex.readback(r)
-        out.append((list(st.x), int(st.anchor), int(st.n), np.ctypeslib.as_array(st.ram).copy()))
-    return out
+        halt, count = ex.halt_at.cpu().numpy(), ex.count.cpu().numpy()
+        for r in np.flatnonzero((halt >= 0) & (count == halt + 1)):
+            if out[r] is None:
+                st = ex.readback(int(r))
+                out[r] = (list(st.x), int(st.anchor), int(st.n), np.ctypeslib.as_array(st.ram).copy())
+        if all(o is not None for o in out):
+            return out
+    raise RuntimeError("a firmware did not park")
 
 
 def run(batch: int = 64, length: int = 512, fp8: bool = False, layers: int = 32, seed: int = 0,
