@@ -190,6 +190,11 @@ def run(batch: int = 64, length: int = 512, fp8: bool = False, layers: int = 32,
     ex = Executor(g, batch=batch)
     ex.load_machines(0, [p] * batch, states=states)
     model, n_fp8 = qwen_text_model(len(g.text_words), layers, fp8, seed, dev)
+    with torch.no_grad():  # warm-up (library initialisation, first-call kernel set-up), untimed
+        w = model(input_ids=torch.zeros(batch, 64, dtype=torch.long, device=dev), use_cache=True)
+        model(input_ids=torch.zeros(batch, 1, dtype=torch.long, device=dev), past_key_values=w.past_key_values,
+              use_cache=True)
+        del w
     torch.cuda.synchronize()
     t = {}
     # 1. the prompt: teacher-forced through the executor (text tokens), prefilled into Qwen
