@@ -235,7 +235,8 @@ QX_API qx_status qx_destroy(qx_t *ex);
  * [3][rows][batch_pad] (lag 1..3, machine fastest); 3 = per-machine error words uint32 [batch];
  * 4 = token hashes uint64 [batch]; 5 = tokens generated int64 [batch]; 6 = index (1-based) of
  * the first HALT token generated, int64 [batch], -1 if none; 7 = head-state bytes read or written
- * by the token kernel so far (uint64 [1], 512 per row transfer: the roofline's touched rows). */
+ * by the token kernel so far (uint64 [1], 512 per row transfer: the roofline's touched rows);
+ * 8 = the machines' table image slots (int32 [batch], after qx_set_table_images). */
 QX_API qx_status qx_buffer(qx_t *ex, int32_t kind, int32_t i, void **dev_ptr, size_t *bytes);
 
 /* Executor2.reset (tritonexec.py:260-263): zero the lag histories of rows [row0, row0 + n). */
@@ -246,6 +247,18 @@ QX_API qx_status qx_reset(qx_t *ex, int32_t row0, int32_t n, void *stream);
  * states are replaced entirely (rows the snapshot does not set become 0). */
 QX_API qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *images /*host*/,
                            void *stream);
+
+/* Share the read-only ROM / DROM tables between machines that run the same firmware (the
+ * snapshot's byte tables, core.py:1236-1246, byte_rows 1194-1212: 96 of the 191 value heads, 6.3 MB
+ * of a machine's 12.5 MB).  The head sublayers that hold only those tables are reallocated as
+ * `slots` copies, one per distinct firmware image (ROM words and DROM bytes); later
+ * qx_load_machines calls give each machine the slot of its image, writing a slot's rows once, when
+ * its image first arrives, and fail with QX_ERR_INVALID_ARG once more than `slots` distinct
+ * images have arrived (slots are not reclaimed; calling this again starts over, and the machines
+ * must then be loaded again).  qx_buffer(1, i) of such a sublayer is then [slots][V][128][128];
+ * qx_buffer(8, 0) is the machines' slots (int32 [batch]).  Synchronises the device.  No
+ * counterpart in the reference (each ExecRow holds its own copy). */
+QX_API qx_status qx_set_table_images(qx_t *ex, int32_t slots);
 
 /* Executor2.step (tritonexec.py:272-289): one token for every machine.  x (dev, [batch][D],
  * the embeddings in) is updated in place to the residual after every node. */

@@ -82,6 +82,10 @@ struct qx_executor {
     // kernels build chunk k
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t copied[2] = {nullptr, nullptr};
+    // shared read-only tables (qx_set_table_images): the content of each image slot in use
+    int table_slots = 0;
+    std::vector<std::vector<uint32_t>> slot_rom;
+    std::vector<std::vector<uint8_t>> slot_drom;
     ~qx_executor() {
         for (void *p : allocs) cudaFree(p);
         if (dplan) cudaFree(dplan);
@@ -558,7 +562,11 @@ qx_status qx_buffer(qx_t *ex, int32_t kind, int32_t i, void **ptr, size_t *bytes
     case 1:
     case 2:
         if (i < 0 || i >= ex->n_hl) return fail(QX_ERR_INVALID_ARG, "qx_buffer: head sublayer %d", i);
-        if (kind == 1) { *ptr = d.S[i]; *bytes = (size_t)ex->B * d.V[i] * QX_HD * QX_HD * 4; }
+        if (kind == 1) {
+            const size_t copies = (d.shared_hl >> i & 1u) ? (size_t)ex->table_slots : (size_t)ex->B;
+            *ptr = d.S[i];
+            *bytes = copies * d.V[i] * QX_HD * QX_HD * 4;
+        }
         else { *ptr = d.hist[i]; *bytes = (size_t)3 * d.NE[i] * ex->Bpad * 4; }
         return QX_OK;
     case 3: *ptr = d.err; *bytes = (size_t)ex->B * 4; return QX_OK;
@@ -566,6 +574,9 @@ qx_status qx_buffer(qx_t *ex, int32_t kind, int32_t i, void **ptr, size_t *bytes
     case 5: *ptr = d.count; *bytes = (size_t)ex->B * 8; return QX_OK;
     case 6: *ptr = d.halt_at; *bytes = (size_t)ex->B * 8; return QX_OK;
     case 7: *ptr = d.state_bytes; *bytes = 8; return QX_OK;
+    case 8:
+        if (!d.img) return fail(QX_ERR_INVALID_ARG, "qx_buffer: the executor shares no tables");
+        *ptr = d.img; *bytes = (size_t)ex->B * 4; return QX_OK;
     default: return fail(QX_ERR_INVALID_ARG, "qx_buffer: kind %d", kind);
     }
 }
@@ -580,6 +591,55 @@ qx_status qx_reset(qx_t *ex, int32_t row0, int32_t n, void *stream) {
     return QX_OK;
 }
 
+qx_status qx_set_table_images(qx_t *ex, int32_t slots) {
+    if (!ex || slots < 1 || slots > ex->B) return fail(QX_ERR_INVALID_ARG, "qx_set_table_images: %d slots", slots);
+    CU(cudaSetDevice(ex->device));
+    // the head sublayers every value head of which is a ROM or DROM table (read-only: no key
+    // writes them, no decay): tables T_ROM .. T_ROM + 31 and T_DROM .. T_DROM + 15, two value
+    // heads each
+    const uint32_t *tab = reinterpret_cast<const uint32_t *>(ex->host_plan.data() + ex->hdr.off[QX_S_TABLES]);
+    std::vector<int> table_vh(ex->n_hl, 0);
+    for (int t = 11; t < 59; t++) table_vh[tab[2 * t]] += 2;
+    uint32_t shared = 0;
+    for (int hl = 0; hl < ex->n_hl; hl++)
+        if (table_vh[hl] == (int)ex->d.V[hl]) shared |= 1u << hl;
+    if (!shared) return fail(QX_ERR_INVALID_PLAN, "qx_set_table_images: no head sublayer holds only tables");
+    CU(cudaDeviceSynchronize());
+    QxDev &d = ex->d;
+    for (int hl = 0; hl < ex->n_hl; hl++) {
+        if (!(shared >> hl & 1u)) continue;
+        const size_t bytes = (size_t)slots * d.V[hl] * QX_HD * QX_HD * 4;
+        void *p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(QX_ERR_OOM, "qx_set_table_images: %zu B", bytes);
+        }
+        if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+            cudaFree(p);
+            return fail(QX_ERR_CUDA, "qx_set_table_images: memset");
+        }
+        auto it = std::find(ex->allocs.begin(), ex->allocs.end(), static_cast<void *>(d.S[hl]));
+        if (it != ex->allocs.end()) {
+            cudaFree(*it);
+            ex->allocs.erase(it);
+        }
+        ex->allocs.push_back(p);
+        d.S[hl] = static_cast<float *>(p);
+    }
+    if (!d.img) {
+        void *p = nullptr;
+        qx_status st = dev_alloc(ex, &p, (size_t)ex->Bpad * 4);
+        if (st != QX_OK) return st;
+        d.img = static_cast<int32_t *>(p);
+    }
+    CU(cudaMemset(d.img, 0, (size_t)ex->Bpad * 4));
+    d.shared_hl = shared;
+    ex->table_slots = slots;
+    ex->slot_rom.clear();
+    ex->slot_drom.clear();
+    return QX_OK;
+}
+
 qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *images, void *stream) {
     if (!ex || !images || row0 < 0 || n < 0 || row0 + n > ex->B)
         return fail(QX_ERR_INVALID_ARG, "qx_load_machines: rows");
@@ -588,6 +648,29 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
         const qx_machine &m = images[i];
         if (m.rom_words > 65536 || m.drom_bytes > 131072 || (!m.rom && m.rom_words) || !m.ram)
             return fail(QX_ERR_INVALID_ARG, "qx_load_machines: image %d", i);
+    }
+    // shared tables: each image's slot (an existing one with the same ROM and DROM content, or a
+    // new one, written by the first machine that brings it)
+    std::vector<uint32_t> slot(n, 0), writes(n, 0);
+    if (ex->d.shared_hl) {
+        for (int i = 0; i < n; i++) {
+            const qx_machine &m = images[i];
+            size_t k = 0;
+            for (; k < ex->slot_rom.size(); k++)
+                if (ex->slot_rom[k].size() == m.rom_words && ex->slot_drom[k].size() == m.drom_bytes &&
+                    (m.rom_words == 0 || !memcmp(ex->slot_rom[k].data(), m.rom, (size_t)m.rom_words * 4)) &&
+                    (m.drom_bytes == 0 || !memcmp(ex->slot_drom[k].data(), m.drom, m.drom_bytes)))
+                    break;
+            if (k == ex->slot_rom.size()) {
+                if ((int)k == ex->table_slots)
+                    return fail(QX_ERR_INVALID_ARG, "qx_load_machines: more distinct firmware images than the %d table slots",
+                                ex->table_slots);
+                ex->slot_rom.emplace_back(m.rom, m.rom + m.rom_words);
+                ex->slot_drom.emplace_back(m.drom, m.drom + m.drom_bytes);
+                writes[i] = 1;
+            }
+            slot[i] = (uint32_t)k;
+        }
     }
     CU(cudaSetDevice(ex->device));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -659,6 +742,8 @@ qx_status qx_load_machines(qx_t *ex, int32_t row0, int32_t n, const qx_machine *
                 q.x[0] = 0;
                 q.anchor = m.anchor;
                 q.n = m.n;
+                q.img = slot[c0 + i];
+                q.write_tables = writes[c0 + i];
             }
         };
         pack_parallel(cn, pack);

@@ -699,7 +699,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     float4 qv[4][QH];
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
-                        const float *Sb = S0 + (size_t)(mbase + mmv[b]) * mstride;
+                        const float *Sb = S0 + qx_copy(d, vh.hl, mbase + mmv[b]) * mstride;
 #pragma unroll
                         for (int j = 0; j < QH; j++)
                             qv[b][j] = qr[b][j] >= 0 ? *reinterpret_cast<const float4 *>(Sb + qr[b][j] * QX_HD)
@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
                         if (!valid[b]) continue;
-                        float *Sb = const_cast<float *>(S0) + (size_t)(mbase + mmv[b]) * mstride;
+                        float *Sb = const_cast<float *>(S0) + qx_copy(d, vh.hl, mbase + mmv[b]) * mstride;
                         const float *smm = sm + mmv[b];
                         const float x0m = QX_ATC(smm, d.one_row);
                         // decay of the first nrows rows (rare: a read-modify-write of its own)

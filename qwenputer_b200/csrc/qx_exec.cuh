@@ -62,6 +62,10 @@ struct QxDev {
     const float *text_base, *text_bits;
     const int32_t *printable;
     int32_t merged, q_fid, n_text, n_printable, n_text_touch, n_code, n_text_bits;
+    // shared read-only tables (qx_set_table_images): head sublayers whose every value head is a
+    // ROM / DROM table hold one copy per firmware image; a machine's copy is img[machine]
+    uint32_t shared_hl;  // bit hl: sublayer hl is shared
+    int32_t *img;        // [Bpad] image slot of each machine
 };
 
 // per-machine error bits
@@ -75,7 +79,13 @@ struct QxImage {  // one machine inside a packed image upload (offsets into the 
     uint32_t rom_off, rom_len, drom_off, drom_words, ram_off, bn_off;  // bn_off: ~0 = none
     uint32_t x[32];
     uint32_t anchor, n;
+    uint32_t img, write_tables;  // shared tables: the machine's image slot; 1: this machine writes it
 };
+
+// The state copy of machine m in head sublayer hl: m, or its image slot where hl is shared.
+__device__ __forceinline__ size_t qx_copy(const QxDev &d, uint32_t hl, int m) {
+    return (d.shared_hl >> hl & 1u) ? (size_t)d.img[m] : (size_t)m;
+}
 
 // shared memory: the rows (byte offsets row * 132; row smem_rows is kept at zero), then the
 // key-select slots, the decode area ([2][32] ints, [16][32] payload floats), a 64-byte counter

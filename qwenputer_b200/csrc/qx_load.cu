@@ -118,6 +118,8 @@ __device__ __forceinline__ float *row_ptr(const QxDev &d, int t, int x, int r, i
     const uint32_t hl = d.tables[2 * t], vh0 = d.tables[2 * t + 1];
     return d.S[hl] + (((size_t)m * d.V[hl] + vh0 + x) * QX_HD + r) * QX_HD;
 }
+// Whether table t lives in a shared sublayer (one copy per firmware image).
+__device__ __forceinline__ bool shared_table(const QxDev &d, int t) { return d.shared_hl >> d.tables[2 * t] & 1u; }
 
 #define QX_LOAD_TASKS 22636  // content rows a machine's load writes (the zero-row list follows)
 
@@ -226,7 +228,12 @@ static __device__ __forceinline__ void load_group(const QxDev &d, const QxImage 
         const bool rom = g < 2048;
         const int k0 = 4 * (rom ? g : g - 2048);
         const int h = k0 / 256, x = (k0 / 128) % 2, rr = k0 % 128;
-        row = row_ptr(d, (rom ? T_ROM : T_DROM) + h, x, rr, m);
+        const int t = (rom ? T_ROM : T_DROM) + h;
+        if (shared_table(d, t)) {
+            if (!im.write_tables) return;  // the image's copy is (being) written by another machine
+            m = (int)im.img;
+        }
+        row = row_ptr(d, t, x, rr, m);
         const int half = rr >> 6, q = lane - 8 * half;
         const uint32_t len = rom ? im.rom_len : im.drom_words, off = rom ? im.rom_off : im.drom_off;
         const uint32_t base = (uint32_t)(h * 2048 + x * 1024 + (rr & 63) * 16 + half * 8);
@@ -298,6 +305,7 @@ __global__ void qx_load_kernel(const __grid_constant__ QxDev d, const QxImage *i
     const int warps = blockDim.x / 32, gw = blockIdx.x * warps + (threadIdx.x >> 5);
     const int stride = gridDim.x * warps;
     const int z0 = QX_LOAD_GROUPS + QX_LOAD_SMALL, total = z0 + (d.n_zero_rows + 3) / 4;
+    if (d.shared_hl && blockIdx.x == 0 && threadIdx.x == 0) d.img[m] = (int32_t)im.img;
     for (int w = gw; w < total; w += stride) {
         if (w < QX_LOAD_GROUPS) {
             load_group(d, im, pool, w, m, lane);
@@ -311,7 +319,10 @@ __global__ void qx_load_kernel(const __grid_constant__ QxDev d, const QxImage *i
             for (int j = 0; j < 4; j++) {
                 if (e0 + j >= d.n_zero_rows) break;
                 const uint2 z = d.zero_rows[e0 + j];
-                float *row = d.S[z.x] + ((size_t)m * d.V[z.x] * QX_HD + z.y) * QX_HD;
+                const bool shared = d.shared_hl >> z.x & 1u;
+                if (shared && !im.write_tables) continue;
+                const size_t c = shared ? (size_t)im.img : (size_t)m;
+                float *row = d.S[z.x] + (c * d.V[z.x] * QX_HD + z.y) * QX_HD;
                 *reinterpret_cast<float4 *>(row + lane * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }

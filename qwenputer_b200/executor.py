@@ -51,7 +51,7 @@ def lib():
         for name in ("qx_create", "qx_destroy", "qx_buffer", "qx_reset", "qx_load_machines",
                      "qx_step", "qx_run", "qx_set_tokens", "qx_readback", "qx_checksums",
                      "qx_errors", "qx_gdn_step", "qx_gdn_step_noalloc", "qx_info",
-                     "qx_cluster_capacity"):
+                     "qx_cluster_capacity", "qx_set_table_images"):
             getattr(L, name).restype = C.c_int
         L.qx_gdn_work_bytes.restype = C.c_size_t
         L.qx_gdn_work_bytes.argtypes = [C.c_int64]
@@ -191,9 +191,13 @@ def snapshot_states(c, head_levels) -> list:
 class Executor:
     """Executor2's surface (tritonexec.py:173-289) on the B200 kernel."""
 
-    def __init__(self, c=None, batch: int = 1, device="cuda", cluster: int | None = None, tc: bool = False):
+    def __init__(self, c=None, batch: int = 1, device="cuda", cluster: int | None = None, tc: bool = False,
+                 table_images: int | None = None):
         """``tc``: run the linear forms on the tensor cores (tcgen05 MMA phases) instead of the
-        CUDA cores; the results are the same bits either way."""
+        CUDA cores; the results are the same bits either way.  ``table_images``: machines running
+        the same firmware share one copy of its read-only ROM / DROM tables, in that many image
+        slots (qx_set_table_images); the head sublayers holding only those tables then expose
+        ``S`` as [table_images, V, 128, 128] and ``table_image`` gives each machine's slot."""
         torch = _torch()
         self.g = load_graph(c)
         self.c = c
@@ -214,6 +218,9 @@ class Executor:
             check(lib().qx_create(self._blob, C.c_size_t(len(blob)), C.c_int32(self.B),
                                   C.c_int32(self.dev.index), C.byref(h)), "qx_create")
         self.h = h
+        self.table_images = int(table_images) if table_images else 0
+        if self.table_images:
+            check(lib().qx_set_table_images(self.h, C.c_int32(self.table_images)), "qx_set_table_images")
         self.x = self._buffer(0, 0, (self.B, self.D), "<f4")
         self.err = self._buffer(3, 0, (self.B,), "<u4")
         self.hash = self._buffer(4, 0, (self.B,), "<u8")
@@ -230,19 +237,36 @@ class Executor:
             V = len(self.g.vheads_at(int(lv)))
             ne = max(1, len(self.plan.lag_dims[int(lv)]))
             bpad = (self.B + 31) // 32 * 32
-            S = self._buffer(1, hl, (self.B, V, HD, HD), "<f4")
+            copies = self._buffer_bytes(1, hl) // (V * HD * HD * 4)  # B, or the image slots (shared)
+            S = self._buffer(1, hl, (copies, V, HD, HD), "<f4")
             H = self._buffer(2, hl, (3, ne, bpad), "<f4").permute(2, 0, 1)[:self.B]
             self.steps.append({"kind": "head", "level": int(lv), "V": V, "S": S, "hist": H,
+                               "shared": bool(self.table_images) and self._shared(hl),
                                "heads": [str(self.g.head_name[h]) for h in self.g.heads_at(int(lv))]})
             self.hist_dims.append(self.plan.lag_dims[int(lv)])
             hl += 1
         self.feat_ids = [int(d) for d in self.g.feat_dims[1:]]
+        self.table_image = self._buffer(8, 0, (self.B,), "<i4") if self.table_images else None
 
     def info(self, what: int) -> int:
         """qx_info: 0 cluster size, 1 clusters the device holds at once, 2 CTAs a launch, 3 smem."""
         v = C.c_int64()
         check(lib().qx_info(self.h, C.c_int32(what), C.byref(v)), "qx_info")
         return int(v.value)
+
+    def _buffer_bytes(self, kind: int, i: int) -> int:
+        p, n = C.c_void_p(), C.c_size_t()
+        check(lib().qx_buffer(self.h, C.c_int32(kind), C.c_int32(i), C.byref(p), C.byref(n)), "qx_buffer")
+        return int(n.value)
+
+    def _shared(self, hl: int) -> bool:
+        """Whether head sublayer hl holds only ROM / DROM tables (shared with table_images)."""
+        from .plan import TABLE_ORDER
+
+        names = [n for n in TABLE_ORDER if n.startswith("rom") or n.startswith("drom")]
+        lv = self.g.head_sublayers()[hl]
+        return sum(self.g.table_position(n)[2] for n in names if self.g.table_position(n)[0] == lv) == \
+            len(self.g.vheads_at(lv))
 
     def _buffer(self, kind: int, i: int, shape, typestr: str):
         torch = _torch()

@@ -21,7 +21,7 @@ def test_library_exports_every_declared_symbol():
 
     lib = C.CDLL(str(build.build()))
     names = declared_symbols()
-    assert len(names) == 17, names
+    assert len(names) == 18, names
     for n in names:
         assert hasattr(lib, n), n
 

@@ -365,3 +365,44 @@ def test_step_in_cuda_graph(qx, graph, programs, cluster, tc):
                     [s_["S"] for s_ in capt.steps if s_["kind"] == "head"]):
         assert torch.equal(a, b)
     del g
+
+
+def test_shared_table_images_match_private_copies(qx):
+    """96 machines running 3 firmware images (each with its own RAM data): with the ROM / DROM
+    tables shared in 3 image slots, free running generates the tokens, final states and
+    checksums of an executor whose machines hold private copies; the shared sublayers hold 3
+    copies; a 4th distinct image is refused."""
+    import random
+
+    from qwenputer_b200 import workload
+
+    base = workload.workload_programs("base", 3, 4242)
+    progs = []
+    for i in range(96):
+        rng = random.Random(i)
+        p = base[i % 3]
+        progs.append(workload.Program(p.text, bytes(rng.getrandbits(8) for _ in range(2048)), p.data_base,
+                                      p.rodata, p.entry))
+    go = int(oracle.lib().qxo_tok_family(18, 0))
+    outs = []
+    for shared in (0, 3):
+        ex = qx.Executor(None, batch=96, table_images=shared or None)
+        ex.load_machines(0, progs)
+        ex.reset()
+        ex.set_tokens(0, [go] * 96)
+        out = torch.zeros(1500, 96, dtype=torch.int32, device="cuda")
+        ex.run(1500, out)
+        if shared:
+            heads = [s_ for s_ in ex.steps if s_["kind"] == "head"]
+            assert sum(h["shared"] for h in heads) == 3
+            assert all(h["S"].shape[0] == 3 for h in heads if h["shared"])
+            assert sorted(set(ex.table_image.cpu().tolist())) == [0, 1, 2]
+            with pytest.raises(qx.QxError, match="table slots"):
+                ex.load_machines(0, workload.workload_programs("base", 1, 999))
+        outs.append((out.cpu().numpy(), ex.checksums().cpu().numpy(),
+                     [list(ex.readback(r).x) for r in (0, 1, 2, 95)]))
+        assert ex.errors() == 0
+        del ex
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1], outs[1][1])
+    assert outs[0][2] == outs[1][2]
