@@ -187,7 +187,7 @@ def run(batch: int = 64, length: int = 512, fp8: bool = False, layers: int = 32,
     tre = TEXT_TOKEN + v["pieces"]["</tool_response>"]
     p = calc_program()
     states = park([p] * batch)
-    ex = Executor(g, batch=batch)
+    ex = Executor(g, batch=batch, table_images=1)  # every row runs the one firmware: one table copy
     ex.load_machines(0, [p] * batch, states=states)
     model, n_fp8 = qwen_text_model(len(g.text_words), layers, fp8, seed, dev)
     with torch.no_grad():  # warm-up (library initialisation, first-call kernel set-up), untimed
