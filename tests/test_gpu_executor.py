@@ -406,3 +406,11 @@ def test_shared_table_images_match_private_copies(qx):
     assert np.array_equal(outs[0][0], outs[1][0])
     assert np.array_equal(outs[0][1], outs[1][1])
     assert outs[0][2] == outs[1][2]
+
+
+def test_fresh_executor_counters_are_zero(qx):
+    """A new executor's device counters start at zero (the head-state byte counter included)."""
+    ex = qx.Executor(None, batch=3)
+    torch.cuda.synchronize()
+    assert int(ex.state_bytes.cpu().numpy().view(np.uint64)[0]) == 0
+    assert int(ex.count.cpu().sum()) == 0 and int(ex.err.cpu().numpy().sum()) == 0
