@@ -196,7 +196,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
                                         loaded where it is first used (a LOADX phase) */
 #define QX_TEXT_TOKEN (1 << 24) /* a text token in the machine's stream: QX_TEXT_TOKEN | qid */
 
-#define QX_PLAN_VERSION 15
+#define QX_PLAN_VERSION 16
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

@@ -58,13 +58,43 @@ __device__ __forceinline__ void put_all(float *p, float v, int C) {
     for (int r = 0; r < C; r++)
         asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(peer_addr(p, r)), "f"(v) : "memory");
 }
-__device__ __forceinline__ void put_all(int *p, int v, int C) {
+__device__ __forceinline__ void put_all(uint32_t *p, uint32_t v, int C) {
     if (C == 1) {
         *p = v;
         return;
     }
     for (int r = 0; r < C; r++)
-        asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(peer_addr(p, r)), "r"(v) : "memory");
+        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_addr(p, r)), "r"(v) : "memory");
+}
+// atomic maximum of a selection word in copy `r` of the cluster (the local copy when C == 1);
+// returns the word it replaced
+__device__ __forceinline__ uint32_t max_at(uint32_t *p, uint32_t v, int C, uint32_t r) {
+    if (C == 1) return atomicMax(p, v);
+    uint32_t old;
+    asm volatile("atom.relaxed.cluster.shared::cluster.max.u32 %0, [%1], %2;" : "=r"(old) : "r"(peer_addr(p, r)), "r"(v)
+                 : "memory");
+    return old;
+}
+// A key-select slot word: 0 for no channel, else a positive channel's value bits above bit 7 and
+// 127 - channel in bits 0..6, so that a larger word is a larger value, or the same value
+// (to 7 bits less) at a lower channel: the order of the reference's first-maximum selection,
+// in which parts of one record merge by atomic maxima.
+__device__ __forceinline__ uint32_t kq_word(float v, int ch) {
+    return max(__float_as_uint(v) & ~0x7Fu, 0x80u) | (uint32_t)(127 - ch);
+}
+__device__ __forceinline__ int kq_channel(uint32_t w) { return w ? 127 - (int)(w & 0x7Fu) : -1; }
+// a part's positive channel into slot levels p[0], p[stride], ... (qhot of them) of every copy:
+// each level keeps the larger word and passes the smaller one down, so after every part of the
+// record the levels hold its qhot largest words (a lock-free tournament); returns true when a
+// positive word fell off the last level of copy 0 (more positive channels than the levels hold)
+__device__ __forceinline__ bool kq_insert(uint32_t *p, int stride, int levels, uint32_t w, int C) {
+    bool over = false;
+    for (int r = 0; r < C; r++) {
+        uint32_t x = w;
+        for (int l = 0; l < levels && x; l++) x = min(x, max_at(p + l * stride, x, C, (uint32_t)r));
+        if (r == 0) over = x != 0;
+    }
+    return over;
 }
 // a contribution to a row that several records sum into, added in each CTA of the cluster
 __device__ __forceinline__ void add_all(float *p, float v, int C) {
@@ -307,9 +337,11 @@ template <int RUN, int QH, int TC>
 __global__ void __launch_bounds__(QX_NT, 1)
     qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens) {
     extern __shared__ __align__(16) float sm[];
-    int *ksel = reinterpret_cast<int *>(sm + (size_t)(d.smem_rows + 1) * QX_RP);  // [slots][32]
-    int *qsel = ksel + d.ksel_slots * 32;                                    // [slots][qhot][32]
-    int *dec_i = qsel + d.ksel_slots * d.qhot_max * 32;                      // [2][32]
+    // key-select slot words (kq_word): [slots][32] keys, then [slots][qhot][32] query levels
+    uint32_t *ksel = reinterpret_cast<uint32_t *>(sm + (size_t)(d.smem_rows + 1) * QX_RP);
+    uint32_t *qsel = ksel + d.ksel_slots * 32;
+    const int nsel = d.ksel_slots * 32 * (1 + d.qhot_max);
+    int *dec_i = reinterpret_cast<int *>(qsel + d.ksel_slots * d.qhot_max * 32);  // [2][32]
     float *dec_pay = reinterpret_cast<float *>(dec_i + 64);                  // [16][32]
     unsigned int *touched = reinterpret_cast<unsigned int *>(dec_pay + 16 * 32);  // state rows
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -331,6 +363,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
     int dpar = 0;
     uint32_t dprev = 0;
     if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
+    for (int i = threadIdx.x; i < nsel; i += QX_NT) ksel[i] = 0u;  // (cleared again by each VHRUN)
     if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; touched[13] = 0; }
     // tensor-core phases: the CTA's tensor memory (warp 0 allocates it; a CTA per SM) and the
     // mbarrier its MMA commits arrive on, in the counter block
@@ -525,10 +558,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             case QX_PH_KSEL: {
-                // per key head, lanes walk machines: pieces [slot | qhot << 16, common row,
-                // lag-ONE row, n | flags] + n channels [row, c0, c1, has common]: the key's first
-                // maximal channel (a write when positive), then (R_QUERY) the query's top-qhot
-                // positive channels
+                // per key head, lanes walk machines: pieces [slot | qhot << 16 | first channel
+                // << 24, common row, lag-ONE row, n | flags] + n channels [row, c0, c1, has
+                // common]: the key's first maximal channel (a write when positive), then
+                // (R_QUERY) the query's top-qhot positive channels.  A record split into parts
+                // (R_MERGE) merges each part's selection into the slot words by atomic maxima
+                // (the slots start at 0: cleared by the value-head serving phase before)
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream st;
@@ -548,12 +583,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     }
                     const uint4 *q = st.rp + 1;
                     const float com = QX_AT(sml, h.y), x1 = QX_AT(sml, h.z);
-                    const uint32_t slot = h.x & 0xFFFFu, qhot = h.x >> 16;
+                    const uint32_t slot = h.x & 0xFFFFu, qhot = (h.x >> 16) & 0xFFu;
                     if (fl & QX_R_FIRST) {
                         bk = 0.0f;
                         ik = -1;
                         npos = 0;
-                        base = 0;
+                        base = (int)(h.x >> 24);
 #pragma unroll
                         for (int k = 0; k < QH; k++) {
                             qb[k] = 0.0f;
@@ -596,14 +631,28 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     base += (int)n;
                     if (fl & QX_R_LAST) {
                         if (!(fl & QX_R_QUERY)) {
-                            put_all(&ksel[slot * 32 + lane], ik, C);
-                            if (npos > 1 && act) atomicOr(&d.err[m], QX_E_KEY);
+                            uint32_t *kp = &ksel[slot * 32 + lane];
+                            const uint32_t w = ik >= 0 ? kq_word(bk, ik) : 0u;
+                            bool err = npos > 1;
+                            // merged: a positive channel of another part shows as a word that
+                            // falls off the slot's one level (more than one positive channel)
+                            if (!(fl & QX_R_MERGE)) put_all(kp, w, C);
+                            else if (w) err |= kq_insert(kp, 0, 1, w, C);
+                            if (err && act) atomicOr(&d.err[m], QX_E_KEY);
                         } else {
+                            uint32_t *qp = &qsel[slot * d.qhot_max * 32 + lane];
+                            bool err = npos > (int)qhot;
+                            if (!(fl & QX_R_MERGE)) {
 #pragma unroll
-                            for (int k = 0; k < 4; k++)
-                                if (k < d.qhot_max)
-                                    put_all(&qsel[(slot * d.qhot_max + k) * 32 + lane], k < QH ? qi[k < QH ? k : 0] : -1, C);
-                            if (npos > (int)qhot && act) atomicOr(&d.err[m], QX_E_QUERY);
+                                for (int k = 0; k < 4; k++)
+                                    if (k < d.qhot_max)
+                                        put_all(qp + k * 32, k < QH && qi[k < QH ? k : 0] >= 0 ? kq_word(qb[k < QH ? k : 0], qi[k < QH ? k : 0]) : 0u, C);
+                            } else {
+#pragma unroll
+                                for (int k = 0; k < QH; k++)
+                                    if (qi[k] >= 0) err |= kq_insert(qp, 32, (int)qhot, kq_word(qb[k], qi[k]), C);
+                            }
+                            if (err && act) atomicOr(&d.err[m], QX_E_QUERY);
                         }
                     }
                     st.rp += 1 + n;
@@ -627,13 +676,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         fcode = av == 0.0f ? 0u : (av == 110.0f ? 1u : 2u);
                     }
                     const float bv = fmaf(vh.cb, x0, QX_AT(sml, vh.b_row)) + vh.bconst;
-                    const int kr = ksel[vh.slot * 32 + lane];
+                    const int kr = kq_channel(ksel[vh.slot * 32 + lane]);
                     const int wrow = (kr >= 0 && bv == 1.0f) ? kr : -1;
                     uint32_t qpack = 0;
                     bool anyq = false;
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
-                        const int qj = j < d.qhot_max ? qsel[(vh.slot * d.qhot_max + j) * 32 + lane] : -1;
+                        const int qj = j < d.qhot_max ? kq_channel(qsel[(vh.slot * d.qhot_max + j) * 32 + lane]) : -1;
                         qpack |= (uint32_t)(qj + 1) << (8 * j);
                         anyq |= qj >= 0;
                     }
@@ -671,6 +720,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 }
                 if (threadIdx.x == 0) wcount[vpar ^ 1] = 0;
                 vpar ^= 1;
+                // the key-select slots were read by the VH phase before: cleared for the next
+                // KSEL phase (a barrier away), whose merged parts take atomic maxima into them
+                for (int i = threadIdx.x; i < nsel; i += QX_NT) ksel[i] = 0u;
                 for (uint32_t r0 = warp * 4; r0 < cnt; r0 += QX_NW * 4) {
                     uint2 rec[4];
 #pragma unroll

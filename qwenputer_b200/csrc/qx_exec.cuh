@@ -98,6 +98,7 @@ __device__ __forceinline__ size_t qx_copy(const QxDev &d, uint32_t hl, int m) {
 #define QX_R_LAST 2u
 #define QX_R_STORE 4u
 #define QX_R_QUERY 8u
+#define QX_R_MERGE 0x10u  // a part of a split key / query record: merged into the slot words
 #define QX_R_SKIP 0x80u
 #define QX_RING_BYTES (QX_NW * 2 * QX_RING_QUADS * 16)
 

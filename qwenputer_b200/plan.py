@@ -57,7 +57,7 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 15
+VERSION = 16
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -67,13 +67,17 @@ NOSYNC = 0x100  # phase kind flag: no barrier after the phase
 # crossing a ring chunk of RING_QUADS quads (counted from the warp's range start); a record longer
 # than a piece continues in the next pieces of the same warp
 PIECE_MAX = 16
-R_FIRST, R_LAST, R_STORE, R_QUERY, R_SKIP = 1, 2, 4, 8, 0x80
+R_FIRST, R_LAST, R_STORE, R_QUERY, R_MERGE, R_SKIP = 1, 2, 4, 8, 0x10, 0x80
 # value heads a VH phase lists: its worklist of (value head, machine) records, 8 bytes each,
 # lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps); with a
 # cluster the rings also hold the CTA's output deltas (one row per output row of the phase)
 VH_CHUNK = 64
 DELTA_ROWS = 128  # output rows one value-head phase may sum into (the group's delta buffer)
 UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most this many
+# key / query records of a cluster plan are split into parts of at most this many channels (by
+# cluster size), each on its own warp; the parts merge into the slots with atomic maxima of
+# packed selection words (a positive channel's value bits above bit 7, 127 - channel below)
+KSEL_PART = {1: 128, 2: 64, 3: 48, 4: 32, 5: 32, 6: 24, 7: 24, 8: 16}
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
        "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
@@ -182,7 +186,7 @@ class Plan:
 
 def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAULT,
                  ksel_slots: int | None = None, cluster: int = 1, tc: bool = False,
-                 defer: bool | None = None) -> Plan:
+                 defer: bool | None = None, ksel_part: int | None = None) -> Plan:
     """The phase program and stream of the graph, for CTAs of ``nw`` warps; one group of 32
     machines runs on a cluster of ``cluster`` CTAs, so stream records are balanced over
     nw * cluster warps.  ``tc``: linear forms run as tensor-core phases (tcgen05) instead of
@@ -190,17 +194,21 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     ``defer`` (default: merged graphs): a token feature gets its row only from the sublayer that
     first uses it, loaded there from the executor's x (where the decode writes it), so that the
     rows of features used late are free before; ``ksel_slots`` (default 16, fewer when the rows
-    do not fit otherwise): key heads one key-select phase serves."""
+    do not fit otherwise): key heads one key-select phase serves; ``ksel_part`` (default by
+    cluster size, KSEL_PART): channels per part of a key or query record."""
     if defer is None:
         defer = g.merged
     if ksel_slots is None:
         for k in (16, 12, 8):
             try:
-                return compile_plan(g, smem_rows, nw, k, cluster, tc, defer)
+                return compile_plan(g, smem_rows, nw, k, cluster, tc, defer, ksel_part)
             except RowsExhausted:
                 if k == 8:
                     raise
     assert 1 <= cluster <= 8, cluster
+    if ksel_part is None:
+        ksel_part = KSEL_PART[cluster]
+    assert 1 <= ksel_part <= 128
     # the kernel takes the ONE dim as 1 on every machine: no sublayer may write it
     assert ONE not in set(int(d) for d in g.ffn_out) and ONE not in set(int(d) for d in g.out_dim)
     ring_bytes = nw * 2 * RING_QUADS * 16
@@ -709,18 +717,30 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         com, lag, res = hf[h][nm]
                         com_row = frow[com] if com else ZW
                         one_row = W(stage_row[(lag, ONE)]) if lag else ZW
+                        # channels past the last present one (zero rows, all weights 0) can
+                        # never be selected or count as positive: they are not emitted
                         chans = []
                         if res:
-                            for c in range(HD):
+                            for c in range(max(res) + 1):
                                 if c in res:
                                     t, c0, c1 = res[c]
                                     chans.append((frow[t] if t else ZW, _fbits(c0), _fbits(c1), one_f if com else 0))
                                 else:
                                     chans.append((ZW, 0, 0, 0))
-                        rec = pieces(sl | int(g.head_qhot[h]) << 16, com_row, one_row, chans, qf_flag)
-                        recs.append(rec)
-                        costs.append((12 if nm == "k" else 18) * len(chans) + 12 * len(rec))
+                        # a record longer than ksel_part channels goes out as parts of even
+                        # length (header x: slot | qhot << 16 | first channel << 24), each on
+                        # any warp, merged into the slot (R_MERGE)
+                        npart = max(1, -(-len(chans) // ksel_part))
+                        plen = -(-len(chans) // npart) if chans else 0
+                        for lo in range(0, max(len(chans), 1), max(plen, 1)):
+                            part = chans[lo:lo + plen]
+                            fl = qf_flag | (R_MERGE if npart > 1 else 0)
+                            rec = pieces(sl | int(g.head_qhot[h]) << 16 | lo << 24, com_row, one_row, part, fl)
+                            recs.append(rec)
+                            costs.append((12 if nm == "k" else 18) * len(part) + 12 * len(rec)
+                                         + (40 * cluster if npart > 1 else 0))
                         stats["kq_channels"] += len(chans)
+                        stats["kq_parts"] += npart
                 stream_phase(PH["KSEL"], recs, costs, body)
                 v0 = len(vheads_l)
                 for sl, h in enumerate(gheads):
@@ -798,6 +818,11 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     # the commits of a token before it (pad0) and a token's total (pad1), whose parities give the
     # barrier phase the kernel waits on (both programs run the same MMA phases in the same order)
     assert [p for p in run_prog if p[0] == PH["MMA"]] == [p for p in step_prog if p[0] == PH["MMA"]]
+    # the key-select slots are read by the VH phase after their KSEL phase and cleared by the VH
+    # serving phase after it, so every KSEL phase is followed by VH, then VHRUN, before the next
+    for prog in (run_prog, step_prog):
+        ks = [p[0] & 0xFF for p in prog if p[0] & 0xFF in (PH["KSEL"], PH["VH"], PH["VHRUN"])]
+        assert all(ks[i:i + 3] == [PH["KSEL"], PH["VH"], PH["VHRUN"]] for i in range(0, len(ks), 3)), ks
     commits = 0
     for i, mp in enumerate(mma_l):
         mma_l[i] = mp[:6] + (commits, 0)

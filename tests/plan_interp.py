@@ -151,11 +151,21 @@ class PlanInterp:
                         self.X[out] = self.X[out] + acc
             elif k == PH["KSEL"]:
                 f32 = lambda v: np.uint32(v).view(np.float32)
+
+                def word(v, ch):
+                    # the kernel's slot word: value bits above bit 7, 127 - channel below (0: none)
+                    w = np.maximum(v.view(np.uint32) & np.uint32(0xFFFFFF80), np.uint32(0x80))
+                    return np.where(v > 0, w | (np.uint32(127) - ch.astype(np.uint32)), np.uint32(0))
+
+                # the slots start cleared (the previous value-head serving phase clears them)
+                self.kword, self.qword = {}, {}
                 for recs in self.warp_records(c, k):
                     for pcs in recs:
-                        # a key part or a query part of a key head
-                        slot, qhot = int(pcs[0][0][0]) & 0xFFFF, int(pcs[0][0][0]) >> 16
-                        query = bool(int(pcs[0][0][3]) >> 24 & 8)
+                        # a key part or a query part of a key head (or a part of one: R_MERGE)
+                        x0 = int(pcs[0][0][0])
+                        slot, qhot, lo = x0 & 0xFFFF, (x0 >> 16) & 0xFF, x0 >> 24
+                        fl = int(pcs[0][0][3]) >> 24
+                        query, merge = bool(fl & 8), bool(fl & 0x10)
                         vals = []
                         for h, q in pcs:
                             com, x1 = self.X[h[1]], self.X[h[2]]
@@ -163,16 +173,23 @@ class PlanInterp:
                                 v = f32(qq[2]) * x1 + (f32(qq[1]) + (f32(qq[3]) * com + self.X[qq[0]]))
                                 vals.append(np.maximum(v, 0))
                         vv = np.stack(vals) if vals else np.zeros((1, self.B), np.float32)
-                        if not query:
-                            km, ka = vv.max(0), vv.argmax(0)
-                            self.ksel[slot] = np.where(km > 0, ka, -1)
-                        else:
-                            sel = []
-                            for j in range(qhot):
-                                qm, qa = vv.max(0), vv.argmax(0)
-                                sel.append(np.where(qm > 0, qa, -1))
-                                vv[qa, np.arange(self.B)] = 0
-                            self.qsel[slot] = sel
+                        # the part's own selection (first maxima, exact)
+                        sel = []
+                        for j in range(1 if not query else qhot):
+                            qm, qa = vv.max(0), vv.argmax(0)
+                            sel.append(word(qm, qa + lo))
+                            vv[qa, np.arange(self.B)] = 0
+                        levels = 1 if not query else qhot
+                        tab = self.kword if not query else self.qword
+                        if not merge:
+                            tab[slot] = sel
+                        else:  # the merged levels: the largest words of every part, in order
+                            prev = tab.get(slot, [np.zeros(self.B, np.uint32)] * levels)
+                            allw = np.sort(np.stack(prev + sel), axis=0)[::-1]
+                            tab[slot] = list(allw[:levels])
+                dec = lambda w: np.where(w != 0, 127 - (w & 0x7F).astype(np.int64), -1)
+                self.ksel = {sl: dec(w[0]) for sl, w in self.kword.items()}
+                self.qsel = {sl: [dec(x) for x in w] for sl, w in self.qword.items()}
             elif k == PH["MMA"]:
                 # tensor-core forms: per form block, D = sum over its tiles of A (bf16 weights,
                 # [128 forms x 16 rows]) x the staged source rows (bf16-exact, checked); the sums
