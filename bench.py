@@ -11,8 +11,8 @@ machines of the whole job, split evenly over the ranks ("scaling": "strong": 4,0
 ``--machines`` on every rank (programs seeded per rank), so the job grows with the GPUs.
 A step is one launch of the persistent token kernel: ``--tokens-per-step`` free-running tokens
 for every local machine (each token is decoded into the next input on the device).  With fewer
-machines per GPU each group of 32 machines runs on a thread-block cluster of several CTAs, so the
-SMs stay busy.  Ranks exchange nothing per step; one NCCL all-gather of the per-machine state
+machines per GPU a CTA runs a smaller group of machines (16, 8 or 4, its warps running 2, 4 or 8
+stream records side by side), so the SMs stay busy with independent CTAs.  Ranks exchange nothing per step; one NCCL all-gather of the per-machine state
 checksums closes the run.  The head states (12.5 MB per machine, 51 GB on one GPU) are far larger
 than L2, so no flush is needed between steps.
 
@@ -58,7 +58,9 @@ def parse():
     ap.add_argument("--weak", action="store_true",
                     help="run --machines on every rank instead of splitting them over the ranks")
     ap.add_argument("--cluster", type=int, default=None,
-                    help="CTAs per group of 32 machines (default: the executor's choice)")
+                    help="CTAs (a thread-block cluster) per group of 32 machines")
+    ap.add_argument("--group", type=int, default=None, choices=[4, 8, 16, 32],
+                    help="machines a CTA runs (default: the executor's choice by machines per GPU)")
     ap.add_argument("--tc", type=int, default=0, choices=[0, 1],
                     help="1: linear forms on the tensor cores (tcgen05), 0: on the CUDA cores")
     ap.add_argument("--tokens-per-step", type=int, default=200)
@@ -275,7 +277,7 @@ def main() -> None:
 
     B, seed0 = shard(args.machines, world, rank, args.weak, args.seed)
     progs = workload.workload_programs("bignum", B, seed0)
-    ex = Executor(None, batch=B, cluster=args.cluster, tc=bool(args.tc))
+    ex = Executor(None, batch=B, cluster=args.cluster, tc=bool(args.tc), group=args.group)
     ex.load_machines(0, progs)
     ex.reset()
     ex.set_tokens(0, [GO_TOKEN] * B)
@@ -379,9 +381,9 @@ def main() -> None:
             "config": {"workload": WORKLOAD,
                        "machines_per_gpu": B, "machines_total": B * world,
                        "tokens_per_step": tps, "parallelism": f"machines sharded over {world} GPU(s)",
-                       "ctas_per_group": ex.cluster, "groups_per_gpu": (B + 31) // 32,
+                       "machines_per_cta_group": ex.group, "ctas_per_group": ex.cluster,
+                       "groups_per_gpu": -(-B // ex.group), "ctas": ex.info(2),
                        "forms_on": "tensor cores (tcgen05)" if args.tc else "CUDA cores",
-                       "clusters_resident": ex.info(1),
                        "l2": f"no flush: {B * 12.5e6 / 1e9:.0f} GB of head states per GPU, far above L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,

@@ -141,6 +141,11 @@ typedef struct {
     uint32_t cluster;              /* CTAs (a thread-block cluster) that share one group of 32
                                       machines; stream ranges exist for nw * cluster warps */
     uint32_t flags;                /* QX_PLAN_FLAG_* */
+    uint32_t group;                /* machines one CTA runs: 32 (a lane per machine), or 16, 8 or 4
+                                      for few machines per GPU: a warp then runs 32 / group stream
+                                      records side by side (lines of 32 / group quads), residual
+                                      rows are group + 1 floats; no cluster, no tensor cores */
+    uint32_t reserved;
     /* sections: byte offset from the blob start, element count */
     uint64_t off[48];
     uint64_t cnt[48];
@@ -196,7 +201,7 @@ enum { /* section ids of qx_plan_header.off / cnt */
                                         loaded where it is first used (a LOADX phase) */
 #define QX_TEXT_TOKEN (1 << 24) /* a text token in the machine's stream: QX_TEXT_TOKEN | qid */
 
-#define QX_PLAN_VERSION 16
+#define QX_PLAN_VERSION 17
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

@@ -12,17 +12,30 @@
 #include "qx.h"
 #include "qx_exec.cuh"
 
-template <int RUN, int QH, int TC>
+template <int RUN, int QH, int TC, int R>
 __global__ void qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens);
 // the token kernel instantiation for the plan: run or step mode, query rows per read (2 or 4),
-// tensor-core form phases or none
+// tensor-core form phases or none, record slots a warp (32 / machines a CTA)
+template <int RUN, int R>
+void *token_kernel_qh(const QxDev &d) {
+    return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2, 0, R>)
+                           : reinterpret_cast<void *>(qx_token_kernel<RUN, 4, 0, R>);
+}
 template <int RUN>
 void *token_kernel_for(const QxDev &d) {
     if (d.has_mma)
-        return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2, 1>)
-                               : reinterpret_cast<void *>(qx_token_kernel<RUN, 4, 1>);
-    return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2, 0>)
-                           : reinterpret_cast<void *>(qx_token_kernel<RUN, 4, 0>);
+        return d.qhot_max <= 2 ? reinterpret_cast<void *>(qx_token_kernel<RUN, 2, 1, 1>)
+                               : reinterpret_cast<void *>(qx_token_kernel<RUN, 4, 1, 1>);
+    switch (d.group) {
+    case 16: return token_kernel_qh<RUN, 2>(d);
+    case 8: return token_kernel_qh<RUN, 4>(d);
+    case 4: return token_kernel_qh<RUN, 8>(d);
+    default: return token_kernel_qh<RUN, 1>(d);
+    }
+}
+// CTAs of one token-kernel launch: a CTA (or a cluster of d.cluster CTAs) per group of machines
+unsigned token_ctas(int B, const QxDev &d) {
+    return (unsigned)((B + d.group - 1) / d.group) * (unsigned)d.cluster;
 }
 __global__ void qx_embed_kernel(const __grid_constant__ QxDev d, int32_t row0, int32_t n, const int32_t *tok);
 __global__ void qx_predecode_kernel(const QxImage *img, uint32_t *pool, int32_t n);
@@ -103,12 +116,12 @@ struct qx_executor {
 
 namespace {
 
-// One launch of the token kernel: a CTA per group of 32 machines, or a cluster of d.cluster CTAs
-// per group (launched with the cluster-dimension attribute).
+// One launch of the token kernel: a CTA per group of machines, or a cluster of d.cluster CTAs
+// per group of 32 (launched with the cluster-dimension attribute).
 template <int RUN>
 cudaError_t launch_token(const qx_t *ex, const QxDev &d, int32_t n_tokens, int32_t *tokens, cudaStream_t st) {
     const int C = d.cluster;
-    const unsigned grid = (unsigned)(ex->Bpad / 32 * C);
+    const unsigned grid = token_ctas(ex->B, d);
     void *args[] = {const_cast<QxDev *>(&d), &n_tokens, &tokens};
     if (C == 1) return cudaLaunchKernel(token_kernel_for<RUN>(d), dim3(grid), dim3(QX_NT), args, ex->smem, st);
     cudaLaunchConfig_t cfg = {};
@@ -155,6 +168,10 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     if (h.qhot_max > 4) return fail(QX_ERR_INVALID_PLAN, "queries read at most 4 rows");
     if (h.nw != QX_NW) return fail(QX_ERR_INVALID_PLAN, "plan balanced for %u warps, kernel has %d", h.nw, QX_NW);
     if (h.cluster < 1 || h.cluster > 8) return fail(QX_ERR_INVALID_PLAN, "cluster of %u CTAs (1 to 8)", h.cluster);
+    if (h.group != 32 && h.group != 16 && h.group != 8 && h.group != 4)
+        return fail(QX_ERR_INVALID_PLAN, "groups of %u machines (32, 16, 8 or 4)", h.group);
+    if (h.group != 32 && (h.cluster != 1 || (h.flags & QX_PLAN_FLAG_MMA)))
+        return fail(QX_ERR_INVALID_PLAN, "a group of %u machines runs on one CTA, without tensor-core phases", h.group);
     if (h.n_head_levels > QX_MAX_HL) return fail(QX_ERR_INVALID_PLAN, "too many head sublayers");
     if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
     if (h.n_born0 > h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
@@ -216,9 +233,20 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
                 (uint64_t)p[i].c + (uint64_t)h.nw * h.cluster >= h.cnt[QX_S_WARP_PTR])
                 return fail(QX_ERR_INVALID_PLAN, "stream phase %llu: warp ranges beyond the section",
                             (unsigned long long)i);
+            if (kind == QX_PH_FORMS || kind == QX_PH_UNITS || kind == QX_PH_KSEL) {
+                // every warp range inside the stream, in whole lines of 32 / group quads
+                const uint32_t *wp = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_WARP_PTR]);
+                const uint32_t ways = 32 / h.group;
+                for (uint32_t w = 0; w <= h.nw * h.cluster; w++) {
+                    const uint32_t v = wp[p[i].c + w];
+                    if (v > h.cnt[QX_S_STREAM] || v % ways || (w && v < wp[p[i].c + w - 1]))
+                        return fail(QX_ERR_INVALID_PLAN, "stream phase %llu: a warp range outside the stream",
+                                    (unsigned long long)i);
+                }
+            }
             if ((kind == QX_PH_VH || kind == QX_PH_VHRUN) &&
                 (p[i].b < p[i].a || p[i].b - p[i].a > QX_VH_CHUNK || p[i].b > h.cnt[QX_S_VHEADS] ||
-                 p[i].c > QX_DELTA_ROWS || (size_t)(p[i].b - p[i].a) * 32 * 8 > QX_RING_BYTES))
+                 p[i].c > QX_DELTA_ROWS || (size_t)(p[i].b - p[i].a) * h.group * 8 > QX_RING_BYTES))
                 return fail(QX_ERR_INVALID_PLAN, "value-head phase [%u, %u) with %u delta rows exceeds its buffers",
                             p[i].a, p[i].b, p[i].c);
             if (kind == QX_PH_VHSUM && (p[i].b > QX_DELTA_ROWS || (uint64_t)p[i].a + p[i].b > h.cnt[QX_S_VHSUM_ROWS]))
@@ -233,7 +261,7 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
         const qx_mma_phase *mp = reinterpret_cast<const qx_mma_phase *>(plan + h.off[QX_S_MMA_PHASES]);
         const qx_mma_tile *mt = reinterpret_cast<const qx_mma_tile *>(plan + h.off[QX_S_MMA_TILES]);
         const uint32_t *rows = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_ROWS]);
-        const uint64_t zero_row = (uint64_t)(h.n_slots + h.n_scratch) * QX_RP * 4;
+        const uint64_t zero_row = (uint64_t)(h.n_slots + h.n_scratch) * QX_RP * 4;  // (groups of 32)
         const uint64_t n_tiles = h.cnt[QX_S_TILEDATA] / (128 * 16);
         for (uint64_t i = 0; i < h.cnt[QX_S_MMA_PHASES]; i++) {
             const qx_mma_phase &m = mp[i];
@@ -260,7 +288,7 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
         // code rows inside the rows, the text tables' sizes, printable tokens inside the vocabulary
         const uint32_t *fr = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FEAT_ROW]);
         const uint32_t *fd = reinterpret_cast<const uint32_t *>(plan + h.off[QX_S_FEAT_DIM]);
-        const uint64_t zero_row = (uint64_t)(h.n_slots + h.n_scratch) * QX_RP * 4;
+        const uint64_t zero_row = (uint64_t)(h.n_slots + h.n_scratch) * (h.group + 1) * 4;
         for (uint32_t f = 0; f < h.n_feat; f++) {
             if (fd[f] >= h.D) return fail(QX_ERR_INVALID_PLAN, "feature %u names no dim", f);
             if (fr[f] & QX_FEAT_DEFERRED ? (fr[f] & ~QX_FEAT_DEFERRED) != fd[f] : fr[f] >= zero_row)
@@ -410,7 +438,8 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.Bpad = ex->Bpad;
     d.D = (int32_t)h.D;
     d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
-    d.zero_row = (uint32_t)d.smem_rows * QX_RP * 4;
+    d.group = (int32_t)h.group;
+    d.zero_row = (uint32_t)d.smem_rows * (d.group + 1) * 4;
     d.cluster = (int32_t)h.cluster;
     d.one_row = (int32_t)h.one_row;
     d.n_fam = (int32_t)h.n_fam;
@@ -464,7 +493,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     if ((s = dev_alloc(ex, &p, 64)) != QX_OK) return bail(s);
     d.state_bytes = static_cast<unsigned long long *>(p);
     {
-        const size_t vb = (size_t)(ex->Bpad / 32) * 2 * QX_DELTA_ROWS * 32 * 4;
+        const size_t vb = (size_t)token_ctas(batch, d) / d.cluster * 2 * QX_DELTA_ROWS * 32 * 4;
         if ((s = dev_alloc(ex, &p, vb)) != QX_OK) return bail(s);
         d.vdelta = static_cast<float *>(p);
         if (cudaMemset(p, 0, vb) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "delta init"));
@@ -526,7 +555,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     {
         // how many clusters (or CTAs) of the token kernel the device holds at once
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(ex->Bpad / 32 * d.cluster));
+        cfg.gridDim = dim3(token_ctas(batch, d));
         cfg.blockDim = dim3(QX_NT);
         cfg.dynamicSmemBytes = ex->smem;
         cudaLaunchAttribute at[1];
@@ -857,10 +886,13 @@ qx_status qx_cluster_capacity(const void *plan, size_t plan_bytes, int32_t devic
     memcpy(&h, plan, sizeof(h));
     qx_status st = validate(h, plan_bytes);
     if (st != QX_OK) return st;
+    if (h.group != 32) return fail(QX_ERR_INVALID_ARG, "qx_cluster_capacity: clusters run groups of 32 machines");
     QxDev d{};
     d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
     d.qhot_max = (int32_t)h.qhot_max;
     d.ksel_slots = (int32_t)h.n_ksel_slots;
+    d.group = 32;
+    d.cluster = 1;
     const size_t smem = qx_smem_bytes(d);
     CU(cudaSetDevice(device));
     CU(cudaFuncSetAttribute(token_kernel_for<1>(d), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -886,7 +918,7 @@ qx_status qx_info(qx_t *ex, int32_t what, int64_t *out) {
     switch (what) {
     case QX_INFO_CLUSTER: *out = ex->d.cluster; return QX_OK;
     case QX_INFO_MAX_CLUSTERS: *out = ex->max_clusters; return QX_OK;
-    case QX_INFO_CTAS: *out = (int64_t)ex->Bpad / 32 * ex->d.cluster; return QX_OK;
+    case QX_INFO_CTAS: *out = (int64_t)token_ctas(ex->B, ex->d); return QX_OK;
     case QX_INFO_SMEM: *out = (int64_t)ex->smem; return QX_OK;
     default: return fail(QX_ERR_INVALID_ARG, "qx_info: unknown item %d", what);
     }

@@ -164,26 +164,33 @@ __device__ __forceinline__ bool mbar_wait(const uint64_t *bar, uint32_t par) {
 }
 
 // A warp's view of its range [begin, end) of the plan stream, read through a ring of QX_NCHUNK
-// chunks of QX_CHUNK quads: while the warp reads one chunk, the next QX_NCHUNK - 1 are in flight.
+// chunks of QX_CHUNK lines of R quads (R = 32 / group: the record slots of a bundled plan, 1 for a
+// 32-machine group): while the warp reads one chunk, the next QX_NCHUNK - 1 are in flight.
+// `left` and the pieces count lines.
 #define QX_CHUNK 32
 #define QX_NCHUNK 2
-static_assert(QX_CHUNK * QX_NCHUNK == 2 * QX_RING_QUADS, "a warp's ring holds 2 * QX_RING_QUADS quads");
+static_assert(QX_CHUNK * QX_NCHUNK == 2 * QX_RING_QUADS, "a warp's ring holds 2 * QX_RING_QUADS lines");
+template <int R>
 struct Stream {
+    static constexpr uint32_t CQ = QX_CHUNK * R;  // quads per chunk
     const uint4 *g;
-    uint4 *ring;        // this warp's QX_NCHUNK * QX_CHUNK quads
-    const uint4 *rp;    // next quad to read (in the ring)
+    uint4 *ring;        // this warp's QX_NCHUNK * CQ quads
+    const uint4 *rp;    // next line to read (in the ring)
     uint32_t begin, end, chunk;
-    int left, lane;     // quads left in the current chunk
+    int left, lane;     // lines left in the current chunk
 
     __device__ __forceinline__ void issue(uint32_t c) {
-        const uint32_t q = begin + c * QX_CHUNK + lane;
-        if (lane < QX_CHUNK && q < end) cp_async16(ring + (c % QX_NCHUNK) * QX_CHUNK + lane, g + q);
+#pragma unroll
+        for (int k = 0; k < R; k++) {
+            const uint32_t q = begin + c * CQ + k * 32 + lane;
+            if (q < end) cp_async16(ring + (c % QX_NCHUNK) * CQ + k * 32 + lane, g + q);
+        }
         cp_commit();
     }
     __device__ __forceinline__ void settle() {
-        rp = ring + (chunk % QX_NCHUNK) * QX_CHUNK;
-        const uint32_t rest = end - (begin + chunk * QX_CHUNK);
-        left = rest < QX_CHUNK ? (int)rest : QX_CHUNK;
+        rp = ring + (chunk % QX_NCHUNK) * CQ;
+        const uint32_t rest = end - (begin + chunk * CQ);
+        left = rest < CQ ? (int)(rest / R) : QX_CHUNK;
     }
     // begin reading: the first QX_NCHUNK chunks in flight, wait for the first
     __device__ __forceinline__ void start(const uint4 *g_, uint4 *ring_, uint32_t b, uint32_t e, int l) {
@@ -204,7 +211,12 @@ struct Stream {
         __syncwarp();
         settle();
     }
-    __device__ __forceinline__ bool more() const { return left > 0 || begin + (chunk + 1) * QX_CHUNK < end; }
+    __device__ __forceinline__ bool more() const { return left > 0 || begin + (chunk + 1) * CQ < end; }
+    // past a piece of n body lines
+    __device__ __forceinline__ void skip(uint32_t n) {
+        rp += R * (1 + n);
+        left -= 1 + (int)n;
+    }
     __device__ __forceinline__ void finish() {
         cp_wait<0>();
         __syncwarp();
@@ -333,26 +345,34 @@ __device__ __noinline__ void mma_forms_phase(const QxDev &d, uint32_t pi, int32_
 }
 }  // namespace
 
-template <int RUN, int QH, int TC>
+// R: record slots a warp runs side by side (1: a group of 32 machines, one a lane; 2, 4, 8: a
+// group of M = 32 / R machines, lane = slot * M + machine, the stream in lines of R quads)
+template <int RUN, int QH, int TC, int R>
 __global__ void __launch_bounds__(QX_NT, 1)
     qx_token_kernel(const __grid_constant__ QxDev d, int32_t n_tokens, int32_t *tokens) {
+    constexpr int M = 32 / R;   // machines of the CTA's group
+    constexpr int RP = M + 1;   // floats per residual row
+    static_assert(R == 1 || !TC, "tensor-core phases need a group of 32 machines");
     extern __shared__ __align__(16) float sm[];
     // key-select slot words (kq_word): [slots][32] keys, then [slots][qhot][32] query levels
-    uint32_t *ksel = reinterpret_cast<uint32_t *>(sm + (size_t)(d.smem_rows + 1) * QX_RP);
+    // (machine-indexed; a group of M < 32 uses the first M of each 32)
+    uint32_t *ksel = reinterpret_cast<uint32_t *>(sm + (size_t)(d.smem_rows + 1) * RP);
     uint32_t *qsel = ksel + d.ksel_slots * 32;
     const int nsel = d.ksel_slots * 32 * (1 + d.qhot_max);
     int *dec_i = reinterpret_cast<int *>(qsel + d.ksel_slots * d.qhot_max * 32);  // [2][32]
     float *dec_pay = reinterpret_cast<float *>(dec_i + 64);                  // [16][32]
     unsigned int *touched = reinterpret_cast<unsigned int *>(dec_pay + 16 * 32);  // state rows
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // this lane's record slot and machine (R == 1: slot 0, machine = lane)
+    const int way = lane / M, ml = lane % M;
     // a group of 32 machines runs on C CTAs; stream ranges are per warp of the group (gw of nwv),
     // interleaved over the CTAs (the plan hands its largest records to the lowest warps)
     const int C = d.cluster;
     const int crank = C > 1 ? (int)cluster_rank() : 0;
     const int gw = warp * C + crank, nwv = C * QX_NW;
     uint4 *ring = reinterpret_cast<uint4 *>(reinterpret_cast<char *>(sm) + qx_ring_offset(d)) +
-                  warp * QX_NCHUNK * QX_CHUNK;
-    float *sml = sm + lane;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
+                  warp * QX_NCHUNK * QX_CHUNK * R;
+    float *sml = sm + ml;  // this lane's machine column: the row at byte offset o is QX_AT(sml, o)
     unsigned int *wcount = touched + 1;  // [2] value-head worklist lengths, used in turn
     int vpar = 0;                        // which of the two the next VH phase appends to
     // value-head phases reuse the stream rings for their worklist; their outputs are summed in
@@ -362,7 +382,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
     float *const D0 = d.vdelta + (size_t)(blockIdx.x / d.cluster) * (2 * QX_DELTA_ROWS * 32);
     int dpar = 0;
     uint32_t dprev = 0;
-    if (threadIdx.x < QX_RP) sm[(size_t)d.smem_rows * QX_RP + threadIdx.x] = 0.0f;  // the zero row
+    if (threadIdx.x < RP) sm[(size_t)d.smem_rows * RP + threadIdx.x] = 0.0f;  // the zero row
     for (int i = threadIdx.x; i < nsel; i += QX_NT) ksel[i] = 0u;  // (cleared again by each VHRUN)
     if (threadIdx.x == 0) { touched[0] = 0; touched[1] = 0; touched[2] = 0; touched[13] = 0; }
     // tensor-core phases: the CTA's tensor memory (warp 0 allocates it; a CTA per SM) and the
@@ -383,19 +403,20 @@ __global__ void __launch_bounds__(QX_NT, 1)
         tc_before();
     }
     const int grp = blockIdx.x / C;
-    const int m = grp * 32 + lane;  // this lane's machine
+    const int m = grp * M + ml;  // this lane's machine
     const bool act = m < d.B;
-    const int mbase = grp * 32;
+    const bool lact = lane < M && act;  // this lane is its machine's decode lane (warp 0)
+    const int mbase = grp * M;
 
     // run mode: the embedding of each machine's next input comes from x
     uint64_t hash = 0;
     int64_t count = 0, halt_at = -1;
     if (RUN) {
-        for (int i = warp; i < d.n_born0; i += QX_NW) {
+        for (int i = warp * R + way; i < d.n_born0; i += QX_NW * R) {
             uint2 p = d.pairs[i];
             QX_AT(sml, p.x) = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
         }
-        if (warp == 0 && act) {
+        if (warp == 0 && lact) {
             hash = d.hash[m];
             count = d.count[m];
             halt_at = d.halt_at[m];
@@ -411,23 +432,23 @@ __global__ void __launch_bounds__(QX_NT, 1)
             if (kind == QX_PH_END) break;
             switch (kind) {
             case QX_PH_ZERO:
-                for (uint32_t i = warp; i < ph.b; i += QX_NW) QX_AT(sml, d.rows[ph.a + i]) = 0.0f;
+                for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) QX_AT(sml, d.rows[ph.a + i]) = 0.0f;
                 break;
             case QX_PH_LOADX:
-                for (uint32_t i = warp; i < ph.b; i += QX_NW) {
+                for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) {
                     uint2 p = d.pairs[ph.a + i];
                     QX_AT(sml, p.x) = act ? d.x[(size_t)m * d.D + p.y] : 0.0f;
                 }
                 break;
             case QX_PH_WRITEOUT:
                 if (act)
-                    for (uint32_t i = gw; i < ph.b; i += nwv) {
+                    for (uint32_t i = gw * R + way; i < ph.b; i += nwv * R) {
                         uint2 p = d.pairs[ph.a + i];
                         d.x[(size_t)m * d.D + p.y] = QX_AT(sml, p.x);
                     }
                 break;
             case QX_PH_APPLY:
-                for (uint32_t i = warp; i < ph.b; i += QX_NW) {
+                for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) {
                     uint2 p = d.pairs[ph.a + i];
                     QX_AT(sml, p.x) += QX_AT(sml, p.y);
                 }
@@ -437,7 +458,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // the history on: lag 1 <- the input x, lag k <- lag k-1
                 float *H = d.hist[ph.c];
                 const size_t ne = d.NE[ph.c], bp = d.Bpad;
-                for (uint32_t i = gw; i < ph.b; i += nwv) {
+                for (uint32_t i = gw * R + way; i < ph.b; i += nwv * R) {
                     const qx_stage s = d.stages[ph.a + i];
                     float *h = H + (size_t)s.e * bp + m;
                     float h0 = h[0];
@@ -454,10 +475,11 @@ __global__ void __launch_bounds__(QX_NT, 1)
             }
             case QX_PH_FORMS: {
                 // two forms a record: pieces [dst A, dst B, 0, n | flags] + n quads [row, w of A,
-                // row, w of B]: F = sum w * X[row], two independent sums a warp
+                // row, w of B]: F = sum w * X[row], two independent sums a lane (a bundled plan:
+                // lines of R quads, this lane's record is quad `way` of each line)
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
-                Stream st;
+                Stream<R> st;
                 st.start(d.stream, ring, b0, b1, lane);
                 float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
                 while (true) {
@@ -465,17 +487,17 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         if (!st.more()) break;
                         st.advance();
                     }
-                    const uint4 h = st.rp[0];
+                    const uint4 h = st.rp[way];
                     const uint32_t n = h.w & 0xFFFFFFu, fl = h.w >> 24;
                     if (fl & QX_R_SKIP) {
                         st.left = 0;
                         continue;
                     }
-                    const uint4 *q = st.rp + 1;
+                    const uint4 *q = st.rp + R + way;
                     if (fl & QX_R_FIRST) a0 = a1 = a2 = a3 = 0.0f;  // a0, a2: form A; a1, a3: B
                     uint32_t j = 0;
                     for (; j + 2 <= n; j += 2) {
-                        const uint4 e0 = q[j], e1 = q[j + 1];
+                        const uint4 e0 = q[j * R], e1 = q[(j + 1) * R];
                         const float v0 = QX_AT(sml, e0.x), v1 = QX_AT(sml, e0.z), v2 = QX_AT(sml, e1.x),
                                     v3 = QX_AT(sml, e1.z);
                         a0 = fmaf(__uint_as_float(e0.y), v0, a0);
@@ -484,16 +506,15 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         a3 = fmaf(__uint_as_float(e1.w), v3, a3);
                     }
                     if (j < n) {
-                        const uint4 e = q[j];
+                        const uint4 e = q[j * R];
                         a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
                         a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
                     }
-                    if (fl & QX_R_LAST) {
+                    if ((fl & (QX_R_LAST | QX_R_NOP)) == QX_R_LAST) {
                         put_all(&QX_AT(sml, h.x), a0 + a2, C);
                         put_all(&QX_AT(sml, h.y), a1 + a3, C);
                     }
-                    st.rp += 1 + n;
-                    st.left -= 1 + (int)n;
+                    st.skip(n);
                 }
                 st.finish();
                 break;
@@ -507,9 +528,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // (k relu(F[b] + cb)) + two quads per unit with an a form, [F[a] row, F[b] row,
                 // coef, ca] [cb, ...] (coef (F[a] + ca) relu(F[b] + cb)); ONE is 1 on every
                 // machine (no sublayer writes it), so its constant terms enter as plain constants
+                // (a bundle's records share n and n_const piece by piece)
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
-                Stream st;
+                Stream<R> st;
                 st.start(d.stream, ring, b0, b1, lane);
                 float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
                 while (true) {
@@ -517,42 +539,41 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         if (!st.more()) break;
                         st.advance();
                     }
-                    const uint4 h = st.rp[0];
+                    const uint4 h = st.rp[way];
                     const uint32_t n = h.w & 0xFFFFFFu, fl = h.w >> 24;
                     if (fl & QX_R_SKIP) {
                         st.left = 0;
                         continue;
                     }
-                    const uint4 *q = st.rp + 1;
+                    const uint4 *q = st.rp + R + way;
                     if (fl & QX_R_FIRST) acc0 = acc1 = acc2 = acc3 = 0.0f;
                     const uint32_t nc = h.y;
                     uint32_t j = 0;
                     for (; j + 2 <= nc; j += 2) {
-                        const uint4 u0 = q[j], u1 = q[j + 1];
+                        const uint4 u0 = q[j * R], u1 = q[(j + 1) * R];
                         const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x);
                         acc0 = fmaf(__uint_as_float(u0.y), relu(f0 + __uint_as_float(u0.z)), acc0);
                         acc1 = fmaf(__uint_as_float(u1.y), relu(f1 + __uint_as_float(u1.z)), acc1);
                     }
                     if (j < nc) {
-                        const uint4 u0 = q[j];
+                        const uint4 u0 = q[j * R];
                         acc2 = fmaf(__uint_as_float(u0.y), relu(QX_AT(sml, u0.x) + __uint_as_float(u0.z)), acc2);
                         j++;
                     }
                     for (; j < n; j += 2) {
-                        const uint4 u = q[j], u2 = q[j + 1];
+                        const uint4 u = q[j * R], u2 = q[(j + 1) * R];
                         const float av = QX_AT(sml, u.x) + __uint_as_float(u.w);
                         const float bv = QX_AT(sml, u.y) + __uint_as_float(u2.x);
                         acc1 += __fmul_rn(__fmul_rn(__uint_as_float(u.z), av), relu(bv));
                     }
-                    if (fl & QX_R_LAST) {
+                    if ((fl & (QX_R_LAST | QX_R_NOP)) == QX_R_LAST) {
                         const float tot = (acc0 + acc1) + (acc2 + acc3);
                         if (fl & QX_R_STORE)
                             put_all(&QX_AT(sml, h.x), QX_AT(sml, h.x) + tot, C);  // the row's only record
                         else
                             add_all(&QX_AT(sml, h.x), tot, C);  // records into one row meet
                     }
-                    st.rp += 1 + n;
-                    st.left -= 1 + (int)n;
+                    st.skip(n);
                 }
                 st.finish();
                 break;
@@ -564,9 +585,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // (R_QUERY) the query's top-qhot positive channels.  A record split into parts
                 // (R_MERGE) merges each part's selection into the slot words by atomic maxima
                 // (the slots start at 0: cleared by the value-head serving phase before)
+                // (a bundle holds keys only or queries only)
                 const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
-                Stream st;
+                Stream<R> st;
                 st.start(d.stream, ring, b0, b1, lane);
                 float bk = 0.0f, qb[QH];
                 int ik = -1, npos = 0, qi[QH], base = 0;
@@ -575,13 +597,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         if (!st.more()) break;
                         st.advance();
                     }
-                    const uint4 h = st.rp[0];
+                    const uint4 h = st.rp[way];
                     const uint32_t n = h.w & 0xFFFFFFu, fl = h.w >> 24;
                     if (fl & QX_R_SKIP) {
                         st.left = 0;
                         continue;
                     }
-                    const uint4 *q = st.rp + 1;
+                    const uint4 *q = st.rp + R + way;
                     const float com = QX_AT(sml, h.y), x1 = QX_AT(sml, h.z);
                     const uint32_t slot = h.x & 0xFFFFu, qhot = (h.x >> 16) & 0xFFu;
                     if (fl & QX_R_FIRST) {
@@ -597,7 +619,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     }
                     if (!(fl & QX_R_QUERY)) {
                         for (uint32_t j = 0; j < n; j++) {
-                            const uint4 c = q[j];
+                            const uint4 c = q[j * R];
                             const float v = relu(fmaf(__uint_as_float(c.z), x1,
                                                       __uint_as_float(c.y) + fmaf(__uint_as_float(c.w), com, QX_AT(sml, c.x))));
                             npos += v > 0.0f;
@@ -608,7 +630,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         }
                     } else {
                         for (uint32_t j = 0; j < n; j++) {
-                            const uint4 c = q[j];
+                            const uint4 c = q[j * R];
                             float v = relu(fmaf(__uint_as_float(c.z), x1,
                                                 __uint_as_float(c.y) + fmaf(__uint_as_float(c.w), com, QX_AT(sml, c.x))));
                             int vi = base + (int)j;
@@ -629,9 +651,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         }
                     }
                     base += (int)n;
-                    if (fl & QX_R_LAST) {
+                    if ((fl & (QX_R_LAST | QX_R_NOP)) == QX_R_LAST) {
                         if (!(fl & QX_R_QUERY)) {
-                            uint32_t *kp = &ksel[slot * 32 + lane];
+                            uint32_t *kp = &ksel[slot * 32 + ml];
                             const uint32_t w = ik >= 0 ? kq_word(bk, ik) : 0u;
                             bool err = npos > 1;
                             // merged: a positive channel of another part shows as a word that
@@ -640,7 +662,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             else if (w) err |= kq_insert(kp, 0, 1, w, C);
                             if (err && act) atomicOr(&d.err[m], QX_E_KEY);
                         } else {
-                            uint32_t *qp = &qsel[slot * d.qhot_max * 32 + lane];
+                            uint32_t *qp = &qsel[slot * d.qhot_max * 32 + ml];
                             bool err = npos > (int)qhot;
                             if (!(fl & QX_R_MERGE)) {
 #pragma unroll
@@ -655,8 +677,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             if (err && act) atomicOr(&d.err[m], QX_E_QUERY);
                         }
                     }
-                    st.rp += 1 + n;
-                    st.left -= 1 + (int)n;
+                    st.skip(n);
                 }
                 st.finish();
                 break;
@@ -665,10 +686,13 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // per value head, lanes walk machines: list every machine whose decay, write or
                 // read touches a state row (record: value head, machine, decay factor, write row,
                 // query rows) in the CTA's worklist, which lives in the idle stream rings
+                // (R record slots: R value heads a warp at a time, each over its M machines)
                 const uint32_t n = ph.b - ph.a;
                 uint2 *wl = reinterpret_cast<uint2 *>(rings);
-                for (uint32_t i = gw; i < n; i += nwv) {
-                    const qx_vhead vh = d.vheads[ph.a + i];
+                for (uint32_t i0 = gw * R; i0 < n; i0 += nwv * R) {
+                    const uint32_t i = i0 + way;
+                    const bool vin = R == 1 || i < n;
+                    const qx_vhead vh = d.vheads[ph.a + (vin ? i : i0)];
                     const float x0 = QX_AT(sml, d.one_row);
                     uint32_t fcode = 0;  // decay factor: 0 -> 1, 1 -> 1/2, 2 -> 0
                     if (vh.nrows > 0) {
@@ -676,30 +700,31 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         fcode = av == 0.0f ? 0u : (av == 110.0f ? 1u : 2u);
                     }
                     const float bv = fmaf(vh.cb, x0, QX_AT(sml, vh.b_row)) + vh.bconst;
-                    const int kr = kq_channel(ksel[vh.slot * 32 + lane]);
+                    const int kr = kq_channel(ksel[vh.slot * 32 + ml]);
                     const int wrow = (kr >= 0 && bv == 1.0f) ? kr : -1;
                     uint32_t qpack = 0;
                     bool anyq = false;
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
-                        const int qj = j < d.qhot_max ? kq_channel(qsel[(vh.slot * d.qhot_max + j) * 32 + lane]) : -1;
+                        const int qj = j < d.qhot_max ? kq_channel(qsel[(vh.slot * d.qhot_max + j) * 32 + ml]) : -1;
                         qpack |= (uint32_t)(qj + 1) << (8 * j);
                         anyq |= qj >= 0;
                     }
-                    const bool need = act && (fcode != 0 || wrow >= 0 || anyq);
+                    const bool need = act && vin && (fcode != 0 || wrow >= 0 || anyq);
                     const unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
                     if (!mask) continue;
                     // the value head's records, padded to a multiple of four (pad records: bit 31)
                     // so that every batch of four the serving warps take shares one value head
-                    const unsigned nrec = __popc(mask), npad = ((nrec + 3u) & ~3u) - nrec;
+                    const unsigned gm = R == 1 ? mask : (mask >> (way * M)) & ((1u << (M & 31)) - 1u);
+                    const unsigned nrec = __popc(gm), npad = ((nrec + 3u) & ~3u) - nrec;
                     unsigned base = 0;
-                    if (lane == 0) base = atomicAdd(wcount + vpar, nrec + npad);
-                    base = __shfl_sync(0xFFFFFFFFu, base, 0);
+                    if (ml == 0 && gm) base = atomicAdd(wcount + vpar, nrec + npad);
+                    base = __shfl_sync(0xFFFFFFFFu, base, way * M);
                     if (need) {
-                        const unsigned pos = base + __popc(mask & ((1u << lane) - 1u));
-                        wl[pos] = make_uint2(i | (uint32_t)lane << 8 | fcode << 13 | (uint32_t)(wrow + 1) << 16, qpack);
+                        const unsigned pos = base + __popc(gm & ((1u << ml) - 1u));
+                        wl[pos] = make_uint2(i | (uint32_t)ml << 8 | fcode << 13 | (uint32_t)(wrow + 1) << 16, qpack);
                     }
-                    if ((unsigned)lane < npad) wl[base + nrec + lane] = make_uint2(i | 1u << 31, 0u);
+                    if (gm && (unsigned)ml < npad) wl[base + nrec + ml] = make_uint2(i | 1u << 31, 0u);
                 }
                 break;
             }
@@ -869,8 +894,8 @@ __global__ void __launch_bounds__(QX_NT, 1)
             case QX_PH_VHSUM: {
                 // the phase's output deltas into this copy's rows (L2 reads: the adds bypassed L1)
                 const float *Dp = D0 + dpar * (QX_DELTA_ROWS * 32);
-                for (uint32_t j = warp; j < ph.b; j += QX_NW)
-                    QX_AT(sml, d.vhsum_rows[ph.a + j]) += __ldcg(Dp + j * 32 + lane);
+                for (uint32_t j = warp * R + way; j < ph.b; j += QX_NW * R)
+                    QX_AT(sml, d.vhsum_rows[ph.a + j]) += __ldcg(Dp + j * 32 + ml);
                 dprev = ph.b;
                 dpar ^= 1;
                 break;
@@ -933,7 +958,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     }
                     dec_i[lane] = fid | kind << 24;
                     dec_i[32 + lane] = pay;
-                    if (act) {
+                    if (lact) {
                         if (crank == 0) {
                             if (bad) atomicOr(&d.err[m], QX_E_CODE);
                             if (tokens) tokens[(size_t)t * d.B + m] = (int32_t)tok;
@@ -946,7 +971,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 __syncthreads();
                 // next embedding (FreeRun: table row for small families, base + payload bits;
                 // a text token: its base + the rows of its bits; no token: the bare text base)
-                for (int mm = warp; mm < 32; mm += QX_NW) {
+                for (int mm = warp; mm < M; mm += QX_NW) {
                     const int fid = dec_i[mm] & 0xFFFFFF, kind = dec_i[mm] >> 24, p = dec_i[32 + mm];
                     float *smw = sm + mm;
                     float *xm = d.x + (size_t)(mbase + mm) * d.D;
@@ -1041,11 +1066,11 @@ __global__ void __launch_bounds__(QX_NT, 1)
         }
     }
     if (RUN && crank == 0) {
-        for (int i = warp; i < d.n_born0; i += QX_NW) {
+        for (int i = warp * R + way; i < d.n_born0; i += QX_NW * R) {
             uint2 p = d.pairs[i];
             if (act) d.x[(size_t)m * d.D + p.y] = QX_AT(sml, p.x);
         }
-        if (warp == 0 && act) {
+        if (warp == 0 && lact) {
             d.hash[m] = hash;
             d.count[m] = count;
             d.halt_at[m] = halt_at;
@@ -1062,15 +1087,21 @@ __global__ void __launch_bounds__(QX_NT, 1)
 
 // QH: query rows a value head reads, at most (2 when the plan's heads read at most 2, else 4);
 // TC: the plan has tensor-core form phases (the CTA holds tensor memory); a plan without them
-// runs an instantiation that contains no tensor-core code at all
-template __global__ void qx_token_kernel<0, 2, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1, 2, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<0, 4, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1, 4, 0>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<0, 2, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1, 2, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<0, 4, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
-template __global__ void qx_token_kernel<1, 4, 1>(const __grid_constant__ QxDev, int32_t, int32_t *);
+// runs an instantiation that contains no tensor-core code at all; R: record slots a warp (groups
+// of 32 / R machines a CTA)
+#define QX_TOKEN_INST(RUN, QH, TC, R) \
+    template __global__ void qx_token_kernel<RUN, QH, TC, R>(const __grid_constant__ QxDev, int32_t, int32_t *);
+#define QX_TOKEN_INST_QH(QH, TC, R) QX_TOKEN_INST(0, QH, TC, R) QX_TOKEN_INST(1, QH, TC, R)
+QX_TOKEN_INST_QH(2, 0, 1)
+QX_TOKEN_INST_QH(4, 0, 1)
+QX_TOKEN_INST_QH(2, 1, 1)
+QX_TOKEN_INST_QH(4, 1, 1)
+QX_TOKEN_INST_QH(2, 0, 2)
+QX_TOKEN_INST_QH(4, 0, 2)
+QX_TOKEN_INST_QH(2, 0, 4)
+QX_TOKEN_INST_QH(4, 0, 4)
+QX_TOKEN_INST_QH(2, 0, 8)
+QX_TOKEN_INST_QH(4, 0, 8)
 
 // Sets rows [row0, row0 + n) of x to the embeddings of the given tokens (FreeRun.load): chip
 // tokens through the family tables, text tokens (merged graphs) through their bits.

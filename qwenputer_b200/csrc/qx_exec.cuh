@@ -6,7 +6,7 @@
 
 #define QX_NW 16                 // warps per CTA
 #define QX_NT (QX_NW * 32)       // threads per CTA
-#define QX_RP 33                 // floats per smem row (32 machines + 1 pad)
+#define QX_RP 33                 // floats per smem row of a 32-machine group (32 machines + 1 pad)
 #define QX_MAX_HL 16             // head sublayers a plan may have
 #define QX_HD 128
 
@@ -51,6 +51,8 @@ struct QxDev {
     int32_t qhot_max, ksel_slots, n_hl, halt_tok;
     uint32_t zero_row;  // byte offset of the row kept at zero
     int32_t cluster;    // CTAs sharing one group of 32 machines (a thread-block cluster)
+    int32_t group;      // machines a CTA runs: 32, or 16 / 8 / 4 (a warp's lanes then run
+                        // 32 / group records side by side; rows are group + 1 floats)
     int32_t n_zero_rows;
     // tensor-core form phases
     const qx_mma_phase *mma_phases;
@@ -99,15 +101,18 @@ __device__ __forceinline__ size_t qx_copy(const QxDev &d, uint32_t hl, int m) {
 #define QX_R_STORE 4u
 #define QX_R_QUERY 8u
 #define QX_R_MERGE 0x10u  // a part of a split key / query record: merged into the slot words
+#define QX_R_NOP 0x20u    // a bundle's padding record: computes on the zero row, stores nothing
 #define QX_R_SKIP 0x80u
 #define QX_RING_BYTES (QX_NW * 2 * QX_RING_QUADS * 16)
 
 __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
-    // rows (plus the zero row), key-select slots, decode area, counters
-    size_t o = (size_t)(d.smem_rows + 1) * QX_RP * 4 + (size_t)d.ksel_slots * 32 * (1 + d.qhot_max) * 4 +
+    // rows (plus the zero row) of group + 1 floats, key-select slots, decode area, counters
+    size_t o = (size_t)(d.smem_rows + 1) * (d.group + 1) * 4 + (size_t)d.ksel_slots * 32 * (1 + d.qhot_max) * 4 +
                (size_t)32 * (2 + 16) * 4 + 64;
     return (o + 15) & ~(size_t)15;
 }
-__host__ __device__ inline size_t qx_smem_bytes(const QxDev &d) {
-    return qx_ring_offset(d) + (size_t)QX_NW * 2 * QX_RING_QUADS * 16;
+// the per-warp stream rings: two chunks of QX_RING_QUADS lines of 32 / group quads
+__host__ __device__ inline size_t qx_ring_bytes(const QxDev &d) {
+    return (size_t)QX_NW * 2 * QX_RING_QUADS * 16 * (32 / d.group);
 }
+__host__ __device__ inline size_t qx_smem_bytes(const QxDev &d) { return qx_ring_offset(d) + qx_ring_bytes(d); }

@@ -105,11 +105,22 @@ def load_graph(c=None) -> graphfile.GraphData:
     return graphfile.export_graph(c)
 
 
-def plan_for(g: graphfile.GraphData, cluster: int = 1, tc: bool = False):
-    key = (id(g), cluster, tc)
+def plan_for(g: graphfile.GraphData, cluster: int = 1, tc: bool = False, group: int = 32):
+    key = (id(g), cluster, tc, group)
     if key not in _plans:
-        _plans[key] = (g, compile_plan(g, cluster=cluster, tc=tc))
+        _plans[key] = (g, compile_plan(g, cluster=cluster, tc=tc, group=group))
     return _plans[key][1]
+
+
+def pick_group(batch: int, device: int) -> int:
+    """Machines a CTA runs: the smallest group (4, 8, 16 or 32) whose CTAs, one per SM, the
+    device holds at once, so that few machines per GPU still spread over the SMs with every CTA
+    independent (4,096 machines on a 148-SM B200: 32; 512: 4)."""
+    sms = _torch().cuda.get_device_properties(device).multi_processor_count
+    for g in (4, 8, 16):
+        if -(-batch // g) <= sms:
+            return g
+    return 32
 
 
 def cluster_capacity(g: graphfile.GraphData, cluster: int, device: int) -> int:
@@ -192,9 +203,12 @@ class Executor:
     """Executor2's surface (tritonexec.py:173-289) on the B200 kernel."""
 
     def __init__(self, c=None, batch: int = 1, device="cuda", cluster: int | None = None, tc: bool = False,
-                 table_images: int | None = None):
-        """``tc``: run the linear forms on the tensor cores (tcgen05 MMA phases) instead of the
-        CUDA cores; the results are the same bits either way.  ``table_images``: machines running
+                 table_images: int | None = None, group: int | None = None):
+        """``group``: machines one CTA runs (32, or 16 / 8 / 4 with a warp's lanes running that
+        many fewer machines and 32 / group stream records side by side; default: pick_group, or 32
+        when ``cluster`` or ``tc`` is given).  ``cluster``: CTAs (a thread-block cluster) sharing a
+        group of 32 machines.  ``tc``: run the linear forms on the tensor cores (tcgen05 MMA
+        phases) instead of the CUDA cores; the results are the same bits either way.  ``table_images``: machines running
         the same firmware share one copy of its read-only ROM / DROM tables, in that many image
         slots (qx_set_table_images); the head sublayers holding only those tables then expose
         ``S`` as [table_images, V, 128, 128] and ``table_image`` gives each machine's slot."""
@@ -205,11 +219,14 @@ class Executor:
         self.dev = torch.device(device)
         if self.dev.index is None:
             self.dev = torch.device("cuda", torch.cuda.current_device())
+        if group is None:
+            group = 32 if (cluster is not None or tc) else pick_group(self.B, self.dev.index)
+        self.group = int(group)
         if cluster is None:
-            cluster = pick_cluster(self.B, self.g, self.dev.index)
+            cluster = 1 if self.group < 32 else pick_cluster(self.B, self.g, self.dev.index)
         self.cluster = int(cluster)
         self.tc = bool(tc)
-        self.plan = plan_for(self.g, self.cluster, self.tc)
+        self.plan = plan_for(self.g, self.cluster, self.tc, self.group)
         self.D = int(self.g.D)
         blob = self.plan.blob()
         self._blob = C.create_string_buffer(blob, len(blob))

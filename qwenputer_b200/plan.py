@@ -57,7 +57,12 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 16
+VERSION = 17
+# machines one CTA runs (its group): 32 (a lane per machine) or, for few machines per GPU, 16, 8
+# or 4 -- then a warp's lanes are WAYS = 32 / group record slots of `group` machines each, and the
+# stream of a phase comes in lines of WAYS quads (one per slot) whose records the plan compiler
+# pads to a common shape (bundles); a residual row is group + 1 floats
+GROUPS = (32, 16, 8, 4)
 NW_DEFAULT = 16
 RING_QUADS = 32  # quads per half of a warp's stream ring
 PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRITEOUT=9,
@@ -65,9 +70,11 @@ PH = dict(ZERO=1, LOADX=2, STAGE=3, FORMS=4, UNITS=5, KSEL=6, VH=7, APPLY=8, WRI
 NOSYNC = 0x100  # phase kind flag: no barrier after the phase
 # stream pieces: a header quad [x, y, z, n | flags << 24] and n <= PIECE_MAX - 1 body quads, never
 # crossing a ring chunk of RING_QUADS quads (counted from the warp's range start); a record longer
-# than a piece continues in the next pieces of the same warp
+# than a piece continues in the next pieces of the same warp.  In a bundled plan (group < 32) the
+# same holds for lines of WAYS quads: a piece is a header line and n body lines, a ring chunk
+# RING_QUADS lines; R_NOP marks a padding record of a bundle (it stores nothing)
 PIECE_MAX = 16
-R_FIRST, R_LAST, R_STORE, R_QUERY, R_MERGE, R_SKIP = 1, 2, 4, 8, 0x10, 0x80
+R_FIRST, R_LAST, R_STORE, R_QUERY, R_MERGE, R_NOP, R_SKIP = 1, 2, 4, 8, 0x10, 0x20, 0x80
 # value heads a VH phase lists: its worklist of (value head, machine) records, 8 bytes each,
 # lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps); with a
 # cluster the rings also hold the CTA's output deltas (one row per output row of the phase)
@@ -78,6 +85,11 @@ UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most t
 # cluster size), each on its own warp; the parts merge into the slots with atomic maxima of
 # packed selection words (a positive channel's value bits above bit 7, 127 - channel below)
 KSEL_PART = {1: 128, 2: 64, 3: 48, 4: 32, 5: 32, 6: 24, 7: 24, 8: 16}
+# the same for bundled plans, by record slots a warp (WAYS): the key-select phase of a group
+# spreads over more slots when each part is shorter
+KSEL_PART_WAYS = {1: 128, 2: 64, 4: 32, 8: 32}
+# FFN nodes of a bundled plan split into records of at most this many units
+UNIT_CHUNK_WAYS = {1: 64, 2: 64, 4: 32, 8: 32}
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
        "VHEADS", "VFORM", "ZFORM", "OUT_ROW", "OUT_W", "HL_V", "HL_NE", "FAM_ROW", "PAY_ROW",
        "FEAT_ROW", "FAM_IDS", "FAM_SIZE", "FAM_ROW0", "EMB_BASE", "EMB_BITS", "EMB_TABLE",
@@ -115,14 +127,20 @@ DT = {
                      ("t1", "<u4"), ("pad0", "<u4"), ("pad1", "<u4")]),
     "tile": np.dtype([("data", "<u4"), ("fb", "<u4"), ("kb", "<u4"), ("acc", "<u4")]),
 }
-HEADER = struct.Struct("<QII" + "I" * 16 + "48Q48Q")
+HEADER = struct.Struct("<QII" + "I" * 18 + "48Q48Q")
 
 
-def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int) -> int:
-    """Shared memory after the rows: key-select slots, the decode area, a counter block and the
-    per-warp stream rings (two halves of RING_QUADS quads)."""
-    return (ROW_PAD * 4 + ksel_slots * 32 * (1 + qhot) * 4 + 32 * 18 * 4 + 64 + 16
-            + nw * 2 * RING_QUADS * 16)
+def row_pad(group: int) -> int:
+    """Floats per residual row: the group's machines plus one (conflict-free both when lanes walk
+    machines and when they walk rows)."""
+    return group + 1
+
+
+def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int, group: int = 32) -> int:
+    """Shared memory after the rows: the zero row, key-select slots, the decode area, a counter
+    block and the per-warp stream rings (two halves of RING_QUADS lines of 32 / group quads)."""
+    return (row_pad(group) * 4 + ksel_slots * 32 * (1 + qhot) * 4 + 32 * 18 * 4 + 64 + 16
+            + nw * 2 * RING_QUADS * 16 * (32 // group))
 
 
 def _bf16_bits(w: float) -> int:
@@ -176,7 +194,8 @@ class Plan:
         head = HEADER.pack(MAGIC, VERSION, h["D"], h["n_slots"], h["n_scratch"], h["nw"],
                            h["n_head_levels"], h["one_row"], h["n_ksel_slots"], h["qhot_max"],
                            h["n_fam"], h["n_pay"], h["n_feat"], h["n_emb_rows"], h["n_families"],
-                           h["vocab"], h["n_born0"], h["cluster"], h.get("flags", 0), *offs, *cnts)
+                           h["vocab"], h["n_born0"], h["cluster"], h.get("flags", 0),
+                           h.get("group", 32), 0, *offs, *cnts)
         out = bytearray(pos)
         out[:len(head)] = head
         for p, b in parts:
@@ -186,36 +205,44 @@ class Plan:
 
 def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAULT,
                  ksel_slots: int | None = None, cluster: int = 1, tc: bool = False,
-                 defer: bool | None = None, ksel_part: int | None = None) -> Plan:
+                 defer: bool | None = None, ksel_part: int | None = None, group: int = 32) -> Plan:
     """The phase program and stream of the graph, for CTAs of ``nw`` warps; one group of 32
     machines runs on a cluster of ``cluster`` CTAs, so stream records are balanced over
     nw * cluster warps.  ``tc``: linear forms run as tensor-core phases (tcgen05) instead of
     stream records on the CUDA cores (every CTA of a cluster then computes all of them).
+    ``group`` < 32: one CTA runs that many machines and a warp WAYS = 32 / group records side by
+    side (bundles of records padded to one shape, lines of WAYS quads); no cluster, no tensor cores.
     ``defer`` (default: merged graphs): a token feature gets its row only from the sublayer that
     first uses it, loaded there from the executor's x (where the decode writes it), so that the
     rows of features used late are free before; ``ksel_slots`` (default 16, fewer when the rows
     do not fit otherwise): key heads one key-select phase serves; ``ksel_part`` (default by
-    cluster size, KSEL_PART): channels per part of a key or query record."""
+    cluster size, KSEL_PART, or by record slots, KSEL_PART_WAYS): channels per part of a key or
+    query record."""
     if defer is None:
         defer = g.merged
     if ksel_slots is None:
         for k in (16, 12, 8):
             try:
-                return compile_plan(g, smem_rows, nw, k, cluster, tc, defer, ksel_part)
+                return compile_plan(g, smem_rows, nw, k, cluster, tc, defer, ksel_part, group)
             except RowsExhausted:
                 if k == 8:
                     raise
     assert 1 <= cluster <= 8, cluster
+    assert group in GROUPS, group
+    ways = 32 // group
+    assert ways == 1 or (cluster == 1 and not tc), "bundled plans run on one CTA, on the CUDA cores"
     if ksel_part is None:
-        ksel_part = KSEL_PART[cluster]
+        ksel_part = KSEL_PART[cluster] if ways == 1 else KSEL_PART_WAYS[ways]
     assert 1 <= ksel_part <= 128
+    unit_chunk = UNIT_CHUNK if ways == 1 else UNIT_CHUNK_WAYS[ways]
     # the kernel takes the ONE dim as 1 on every machine: no sublayer may write it
     assert ONE not in set(int(d) for d in g.ffn_out) and ONE not in set(int(d) for d in g.out_dim)
-    ring_bytes = nw * 2 * RING_QUADS * 16
+    ring_bytes = nw * 2 * RING_QUADS * 16 * ways
     qhot = int(g.head_qhot.max())
     assert qhot <= 4, "queries may read at most 4 rows"
+    rp = row_pad(group)
     if smem_rows is None:
-        smem_rows = (SMEM_MAX - smem_extra_bytes(ksel_slots, qhot, nw)) // (ROW_PAD * 4)
+        smem_rows = (SMEM_MAX - smem_extra_bytes(ksel_slots, qhot, nw, group)) // (rp * 4)
     D = g.D
     levels = [int(x) for x in g.levels]
     kinds = [int(k) for k in g.level_kind]
@@ -331,8 +358,8 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
     zero_row = smem_rows  # an extra row the kernel keeps at zero (reads of "no form")
 
     def W(r: int) -> int:
-        """Shared-memory byte offset of a row (rows are ROW_PAD floats apart)."""
-        return r * ROW_PAD * 4
+        """Shared-memory byte offset of a row (rows are row_pad(group) floats apart)."""
+        return r * rp * 4
 
     ZW = W(zero_row)
     one_w = W(slot[ONE])
@@ -391,25 +418,45 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
             if i >= len(body):
                 return out
 
+    def zip_lanes(lane_recs: list[list[list[tuple]]]) -> list[list[tuple]]:
+        """WAYS records of one shape (pieces of equal lengths) as one bundle: its piece k holds,
+        line by line, one quad of every record's piece k (record slot s = quad s of a line)."""
+        out = []
+        for k in range(len(lane_recs[0])):
+            n = len(lane_recs[0][k])
+            assert all(len(lr) == len(lane_recs[0]) and len(lr[k]) == n for lr in lane_recs)
+            out.append([lr[k][j] for j in range(n) for lr in lane_recs])
+        return out
+
     def stream_phase(kind: int, records: list[list[list[tuple]]], costs: list[float], prog, a=0, b=0):
-        """Emit per-warp quad ranges of the records (each a list of pieces) as one phase: a piece
-        that would cross a ring chunk is moved to the next chunk behind an R_SKIP header."""
+        """Emit per-warp quad ranges of the records (each a list of pieces; in a bundled plan a
+        record is a bundle of WAYS records) as one phase: a piece that would cross a ring chunk
+        is moved to the next chunk behind an R_SKIP header line."""
         per = balance(costs)
         wp = len(warp_ptr_l)
         warp_ptr_l.append(len(stream))
+        chunk = RING_QUADS * ways
         for w in range(nwv):
             start = len(stream)
             for i in per[w]:
                 for pc in records[i]:
-                    assert len(pc) <= PIECE_MAX
-                    room = RING_QUADS - (len(stream) - start) % RING_QUADS
+                    assert len(pc) <= PIECE_MAX * ways and len(pc) % ways == 0
+                    room = chunk - (len(stream) - start) % chunk
                     if len(pc) > room:
-                        stream.append((0, 0, 0, R_SKIP << 24))
-                        stream.extend([(0, 0, 0, 0)] * (room - 1))
+                        stream.extend([(0, 0, 0, R_SKIP << 24)] * ways)
+                        stream.extend([(0, 0, 0, 0)] * (room - ways))
                         stats["pad_quads"] += room
                     stream.extend(pc)
             warp_ptr_l.append(len(stream))
         prog.append((kind, a, b, wp))
+
+    def bundles(items: list, shape) -> list[list]:
+        """Items in bundles of WAYS, similar shapes together (one bundle per item when WAYS = 1,
+        in the given order)."""
+        if ways == 1:
+            return [[it] for it in items]
+        order = sorted(items, key=shape, reverse=True)
+        return [order[i:i + ways] for i in range(0, len(order), ways)]
 
     def forms_phase(form_list: list[tuple], dst_rows: list[int], rowmap, prog):
         """Forms in pairs of similar length: pieces [dst A, dst B, 0, n | flags] + n quads
@@ -417,18 +464,27 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         runs two independent sums; an odd last form pairs with an empty one into the zero row."""
         recs, costs = [], []
         items = sorted(zip(form_list, dst_rows), key=lambda fd: -len(fd[0]))
+        prs = []
         for i in range(0, len(items), 2):
             ta, da = items[i]
             tb, db = items[i + 1] if i + 1 < len(items) else ((), None)
             ea = [(W(rowmap(t)), _fbits(w)) for t, w in ta]
             eb = [(W(rowmap(t)), _fbits(w)) for t, w in tb]
-            n = max(len(ea), len(eb))
-            ea += [(ZW, 0)] * (n - len(ea))
-            eb += [(ZW, 0)] * (n - len(eb))
-            body = [(ea[j][0], ea[j][1], eb[j][0], eb[j][1]) for j in range(n)]
-            recs.append(pieces(W(da), W(db) if db is not None else ZW, 0, body))
-            costs.append(4 * n + 14 * len(recs[-1]))
+            prs.append((ea, eb, W(da), W(db) if db is not None else ZW))
             stats["form_nnz"] += len(ta) + len(tb)
+        for bd in bundles(prs, lambda pr: max(len(pr[0]), len(pr[1]))):
+            n = max(max(len(ea), len(eb)) for ea, eb, _, _ in bd)
+            lanes = []
+            for k in range(ways):
+                # a bundle's padding record: zero-weight entries on the zero row, stores nothing
+                ea, eb, xa, xb = bd[k] if k < len(bd) else ([], [], ZW, ZW)
+                ea = ea + [(ZW, 0)] * (n - len(ea))
+                eb = eb + [(ZW, 0)] * (n - len(eb))
+                body = [(ea[j][0], ea[j][1], eb[j][0], eb[j][1]) for j in range(n)]
+                lanes.append(pieces(xa, xb, 0, body, 0 if k < len(bd) else R_NOP))
+            recs.append(lanes[0] if ways == 1 else zip_lanes(lanes))
+            costs.append(4 * n + 14 * len(recs[-1]))
+            stats["bundle_pad_quads"] += sum(n - max(len(ea), len(eb)) for ea, eb, _, _ in bd) + n * (ways - len(bd))
         stream_phase(PH["FORMS"], recs, costs, prog)
 
     mma_l: list[tuple] = []
@@ -583,31 +639,45 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         else:
                             cq.append((rb, _fbits(np.float32(cf) * np.float32(ca)), _fbits(cb), 0))
                     units_all = [("c", q) for q in cq] + [("h", q) for q in hq]
-                    for c0 in range(0, max(len(units_all), 1), UNIT_CHUNK):
-                        chunk = units_all[c0:c0 + UNIT_CHUNK]
+                    for c0 in range(0, max(len(units_all), 1), unit_chunk):
+                        chunk = units_all[c0:c0 + unit_chunk]
                         parts.append((out, [q for k, q in chunk if k == "c"], [q for k, q in chunk if k == "h"]))
                     stats["units"] += int(g.ffn_uptr[n + 1] - g.ffn_uptr[n])
                     stats["unit_groups"] += 0
                 # a row that only one record of the phase adds into is updated with a plain
                 # read-add-store (R_STORE); rows several records meet take atomic adds
                 nrec = collections.Counter(out for out, _, _ in parts)
-                recs, costs = [], []
-                for out, cq, hq in parts:
+
+                def unit_pieces(out, cq, hq, fl0):
                     body_q = cq + [q for pair in hq for q in pair]
-                    store = R_STORE if nrec[out] == 1 else 0
                     pcs, i = [], 0
                     while True:
                         e = min(i + PIECE_MAX - 1, len(body_q))
                         if e > len(cq) and (e - len(cq)) % 2:
                             e -= 1  # a unit's two quads stay in one piece
                         nc = max(0, min(e, len(cq)) - i)
-                        fl = store | (R_FIRST if i == 0 else 0) | (R_LAST if e >= len(body_q) else 0)
+                        fl = fl0 | (R_FIRST if i == 0 else 0) | (R_LAST if e >= len(body_q) else 0)
                         pcs.append([(out, nc, 0, (e - i) | fl << 24)] + body_q[i:e])
                         i = e
                         if i >= len(body_q):
-                            break
-                    recs.append(pcs)
-                    costs.append(4 * len(cq) + 9 * len(hq) + 12 * len(pcs))
+                            return pcs
+
+                recs, costs = [], []
+                # bundles share their pieces' shape: constant-gate units padded with k = 0 on the
+                # zero row, units with an a form with coef = 0 (both add +0)
+                for bd in bundles(parts, lambda pt: (len(pt[2]), len(pt[1]))):
+                    ncq = max(len(cq) for _, cq, _ in bd)
+                    nhq = max(len(hq) for _, _, hq in bd)
+                    lanes = []
+                    for k in range(ways):
+                        out, cq, hq = bd[k] if k < len(bd) else (ZW, [], [])
+                        fl0 = (R_STORE if nrec[out] == 1 else 0) if k < len(bd) else R_NOP
+                        cq = cq + [(ZW, 0, 0, 0)] * (ncq - len(cq))
+                        hq = hq + [((ZW, ZW, 0, 0), (0, 0, 0, 0))] * (nhq - len(hq))
+                        lanes.append(unit_pieces(out, cq, hq, fl0))
+                    recs.append(lanes[0] if ways == 1 else zip_lanes(lanes))
+                    costs.append(4 * ncq + 9 * nhq + 12 * len(recs[-1]))
+                    stats["bundle_pad_quads"] += sum(ncq - len(cq) + 2 * (nhq - len(hq)) for _, cq, hq in bd) + (ncq + 2 * nhq) * (ways - len(bd))
                 stream_phase(PH["UNITS"], recs, costs, body)
             group_stats.append((lv, "ffn", len(groups)))
         else:
@@ -710,7 +780,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 # a key head is two records, on any warps: key pieces [slot | qhot << 16, common
                 # row, lag-ONE row, n | flags] and query pieces (R_QUERY); channel quads [row, c0,
                 # c1, 1.0 if the common form applies else 0]
-                recs, costs = [], []
+                specs = []
                 one_f = _fbits(1.0)
                 for sl, h in enumerate(gheads):
                     for nm, qf_flag in (("k", 0), ("q", R_QUERY)):
@@ -735,12 +805,31 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         for lo in range(0, max(len(chans), 1), max(plen, 1)):
                             part = chans[lo:lo + plen]
                             fl = qf_flag | (R_MERGE if npart > 1 else 0)
-                            rec = pieces(sl | int(g.head_qhot[h]) << 16 | lo << 24, com_row, one_row, part, fl)
-                            recs.append(rec)
-                            costs.append((12 if nm == "k" else 18) * len(part) + 12 * len(rec)
-                                         + (40 * cluster if npart > 1 else 0))
+                            specs.append((sl | int(g.head_qhot[h]) << 16 | lo << 24, com_row, one_row, part, fl))
                         stats["kq_channels"] += len(chans)
                         stats["kq_parts"] += npart
+                # bundles hold keys or queries only (their channel loops differ); padding
+                # channels on the zero row never count as positive, padding records store nothing
+                recs, costs = [], []
+                kq_bundles = []
+                if ways == 1:
+                    kq_bundles = [[sp] for sp in specs]
+                else:
+                    for qk in (0, R_QUERY):
+                        kq_bundles += bundles([sp for sp in specs if sp[4] & R_QUERY == qk], lambda sp: len(sp[3]))
+                for bd in kq_bundles:
+                    n = max(len(sp[3]) for sp in bd)
+                    lanes = []
+                    for k in range(ways):
+                        x, com_row, one_row, part, fl = bd[k] if k < len(bd) else (
+                            bd[0][0] & 0xFF0000, ZW, ZW, [], (bd[0][4] & R_QUERY) | R_NOP)
+                        part = part + [(ZW, 0, 0, 0)] * (n - len(part))
+                        lanes.append(pieces(x, com_row, one_row, part, fl))
+                    recs.append(lanes[0] if ways == 1 else zip_lanes(lanes))
+                    key = not bd[0][4] & R_QUERY
+                    costs.append((12 if key else 18) * n + 12 * len(recs[-1])
+                                 + (40 * cluster if bd[0][4] & R_MERGE else 0))
+                    stats["bundle_pad_quads"] += sum(n - len(sp[3]) for sp in bd) + n * (ways - len(bd))
                 stream_phase(PH["KSEL"], recs, costs, body)
                 v0 = len(vheads_l)
                 for sl, h in enumerate(gheads):
@@ -920,7 +1009,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
                  n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
                  vocab=int(g.vocab), n_born0=len(born0), cluster=cluster,
-                 flags=(FLAG_MMA if mma_l else 0) | (FLAG_MERGED if merged else 0))
+                 flags=(FLAG_MMA if mma_l else 0) | (FLAG_MERGED if merged else 0), group=group)
     stats["n_slots"] = n_slots
     stats["ksel_slots"] = ksel_slots
     stats["deferred_features"] = len(deferred)

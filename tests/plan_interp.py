@@ -38,9 +38,12 @@ class PlanInterp:
         self.s = s
         h = P.hdr
         self.rows = h["n_slots"] + h["n_scratch"]
-        # indexed by shared-memory word offset (byte offset / 4, rows 33 words apart); the row
-        # after the last is zero
-        self.Xw = np.zeros(((self.rows + 1) * 33, B), np.float32)
+        # machines a CTA runs, and record slots a warp (bundled plans: lines of `ways` quads)
+        self.group = h.get("group", 32)
+        self.ways = 32 // self.group
+        # indexed by shared-memory word offset (byte offset / 4, rows group + 1 words apart); the
+        # row after the last is zero
+        self.Xw = np.zeros(((self.rows + 1) * (self.group + 1), B), np.float32)
         self.X = _ByteIndexed(self.Xw)
         self.hl_v = s["HL_V"]
         self.S = [np.zeros((B, int(v), 128, 128), np.float32) for v in s["HL_V"]]
@@ -54,28 +57,37 @@ class PlanInterp:
 
     def warp_records(self, c, k):
         """Per warp, its records of a stream phase: lists of (header, body quads) pieces, the
-        R_SKIP padding dropped (a record's pieces are consecutive and end with R_LAST)."""
-        from qwenputer_b200.plan import R_LAST, R_SKIP
+        R_SKIP padding dropped (a record's pieces are consecutive and end with R_LAST).  In a
+        bundled plan a piece is a header line and n body lines of `ways` quads: record slot s
+        reads quad s of each line; the bundle's padding records (R_NOP) are dropped."""
+        from qwenputer_b200.plan import R_LAST, R_NOP, R_SKIP
 
         st = self.s["STREAM"].astype(np.int64)
         wp = self.s["WARP_PTR"].astype(np.int64)
         nw = self.P.hdr["nw"] * self.P.hdr["cluster"]  # the warps of a group's cluster
+        R = self.ways
         out = []
         for w in range(nw):
             i, end, start = wp[c + w], wp[c + w + 1], wp[c + w]
-            recs, cur = [], []
+            recs, cur = [], [[] for _ in range(R)]
             while i < end:
-                h = st[i]
-                n, fl = int(h[3]) & 0xFFFFFF, int(h[3]) >> 24
+                hs = st[i:i + R]
+                n, fl = int(hs[0][3]) & 0xFFFFFF, int(hs[0][3]) >> 24
                 if fl & R_SKIP:
-                    i = start + ((i - start) // 32 + 1) * 32
+                    i = start + ((i - start) // (32 * R) + 1) * (32 * R)
                     continue
-                cur.append((h, st[i + 1:i + 1 + n]))
-                i += 1 + n
+                body = st[i + R:i + R * (1 + n)].reshape(n, R, 4) if n else np.zeros((0, R, 4), np.int64)
+                for sl in range(R):
+                    fs = int(hs[sl][3]) >> 24
+                    assert int(hs[sl][3]) & 0xFFFFFF == n and (fs ^ fl) & 3 == 0, "a bundle's pieces differ"
+                    cur[sl].append((hs[sl], body[:, sl]))
+                i += R * (1 + n)
                 if fl & R_LAST:
-                    recs.append(cur)
-                    cur = []
-            assert not cur
+                    for sl in range(R):
+                        if not (int(cur[sl][0][0][3]) >> 24) & R_NOP:
+                            recs.append(cur[sl])
+                    cur = [[] for _ in range(R)]
+            assert not any(cur)
             out.append(recs)
         return out
 

@@ -59,53 +59,66 @@ def test_bad_plans_are_rejected():
     assert lib.qx_create(bytes(blob[:1000]), C.c_size_t(1000), 4, 0, C.byref(h)) == 1
 
 
-@pytest.mark.parametrize("cluster,tc", [(1, False), (4, False), (1, True), (4, True)])
-def test_plan_is_consistent(graph, cluster, tc):
+@pytest.mark.parametrize("cluster,tc,group", [(1, False, 32), (4, False, 32), (1, True, 32), (4, True, 32),
+                                              (1, False, 16), (1, False, 8), (1, False, 4)])
+def test_plan_is_consistent(graph, cluster, tc, group):
     from qwenputer_b200.plan import PH, RING_QUADS, SMEM_MAX, compile_plan, smem_extra_bytes
 
-    P = compile_plan(graph, cluster=cluster, tc=tc)
+    P = compile_plan(graph, cluster=cluster, tc=tc, group=group)
     s = P.sec
-    rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * 33 * 4  # byte offsets, zero row included
-    assert P.hdr["cluster"] == cluster
+    R = 32 // group  # record slots a warp: the stream comes in lines of R quads
+    rb = (group + 1) * 4  # bytes per residual row
+    rows = (P.hdr["n_slots"] + P.hdr["n_scratch"] + 1) * rb  # byte offsets, zero row included
+    assert P.hdr["cluster"] == cluster and P.hdr["group"] == group
     nw = P.hdr["nw"] * cluster  # the warps of a machine group's cluster
     st = s["STREAM"].astype(np.int64)
     wp = s["WARP_PTR"].astype(np.int64)
     # walk every stream piece of every phase: rows in range, pieces inside one ring chunk,
-    # records complete, ranges end on their warp's range
-    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_SKIP
+    # records complete, a bundle's records of one shape, ranges end on their warp's range
+    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_NOP, R_QUERY, R_SKIP
 
+    chunk = RING_QUADS * R
     for ph in s["RUN_PROG"]:
         k = int(ph["kind"]) & 0xFF
         if k not in (PH["FORMS"], PH["UNITS"], PH["KSEL"]):
             continue
         seg = wp[ph["c"]:ph["c"] + nw + 1]
-        assert np.all(np.diff(seg) >= 0)
+        assert np.all(np.diff(seg) >= 0) and np.all(seg % R == 0)
         for w in range(nw):
             i, end, start = seg[w], seg[w + 1], seg[w]
             open_rec = False
             while i < end:
-                h = st[i]
-                n, fl = int(h[3]) & 0xFFFFFF, int(h[3]) >> 24
+                hs = st[i:i + R]
+                n, fl = int(hs[0][3]) & 0xFFFFFF, int(hs[0][3]) >> 24
                 if fl & R_SKIP:
-                    i = start + ((i - start) // RING_QUADS + 1) * RING_QUADS
+                    assert all(int(h[3]) >> 24 & R_SKIP for h in hs)
+                    i = start + ((i - start) // chunk + 1) * chunk
                     continue
                 assert 1 + n <= PIECE_MAX
-                assert (i - start) // RING_QUADS == (i + n - start) // RING_QUADS, "piece crosses a chunk"
+                assert (i - start) // chunk == (i + R * (1 + n) - 1 - start) // chunk, "piece crosses a chunk"
                 assert bool(fl & R_FIRST) != open_rec
-                body = st[i + 1:i + 1 + n]
-                if k == PH["FORMS"]:
-                    assert h[0] < rows and h[0] % 132 == 0 and h[1] < rows and h[1] % 132 == 0
-                    assert np.all(body[:, 0] < rows) and np.all(body[:, 2] < rows)
-                elif k == PH["UNITS"]:
-                    nc = int(h[1])
-                    assert h[0] < rows and nc <= n and (n - nc) % 2 == 0
-                    assert np.all(body[:nc, 0] < rows)
-                    assert np.all(body[nc::2, 0] < rows) and np.all(body[nc::2, 1] < rows)
-                else:
-                    assert (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"] and h[1] < rows and h[2] < rows
-                    assert np.all(body[:, 0] < rows)
+                body = st[i + R:i + R * (1 + n)].reshape(n, R, 4)
+                for sl in range(R):
+                    h, b = hs[sl], body[:, sl]
+                    fs = int(h[3]) >> 24
+                    assert int(h[3]) & 0xFFFFFF == n and fs & 3 == fl & 3, "a bundle's pieces differ"
+                    if k == PH["FORMS"]:
+                        assert h[0] < rows and h[0] % rb == 0 and h[1] < rows and h[1] % rb == 0
+                        assert np.all(b[:, 0] < rows) and np.all(b[:, 2] < rows)
+                    elif k == PH["UNITS"]:
+                        nc = int(h[1])
+                        assert nc == int(hs[0][1]), "a bundle's constant-gate counts differ"
+                        assert h[0] < rows and nc <= n and (n - nc) % 2 == 0
+                        assert np.all(b[:nc, 0] < rows)
+                        assert np.all(b[nc::2, 0] < rows) and np.all(b[nc::2, 1] < rows)
+                    else:
+                        assert fs & R_QUERY == fl & R_QUERY, "a bundle mixes keys and queries"
+                        assert (h[0] & 0xFFFF) < P.hdr["n_ksel_slots"] and h[1] < rows and h[2] < rows
+                        assert np.all(b[:, 0] < rows)
+                    if fs & R_NOP:  # a padding record: zero weights only
+                        assert not (b[:, 1] | (b[:, 3] if k == PH["FORMS"] else 0)).any()
                 open_rec = not (fl & R_LAST)
-                i += 1 + n
+                i += R * (1 + n)
             assert not open_rec
             assert i == end
     kinds = [int(k) & 0xFF for k in s["RUN_PROG"]["kind"]]
@@ -138,7 +151,7 @@ def test_plan_is_consistent(graph, cluster, tc):
             commits += -(-(t1 - t0) // 16)
         assert all(int(mp["pad1"]) == commits for mp in s["MMA_PHASES"])
     assert len(s["TABLES"]) == 198
-    smem = (P.hdr["n_slots"] + P.hdr["n_scratch"]) * 33 * 4 + smem_extra_bytes(P.hdr["n_ksel_slots"], P.hdr["qhot_max"], P.hdr["nw"])
+    smem = (P.hdr["n_slots"] + P.hdr["n_scratch"]) * rb + smem_extra_bytes(P.hdr["n_ksel_slots"], P.hdr["qhot_max"], P.hdr["nw"], group)
     assert smem <= SMEM_MAX, smem
     assert RING_QUADS == 32
     assert P.hdr["n_born0"] == P.hdr["n_feat"]
@@ -179,9 +192,10 @@ def test_gdn_step_rejects_bad_shapes_before_any_launch():
         gdn_check_args(**ok)
 
 
-@pytest.mark.parametrize("merged,tc,cluster", [(False, False, 1), (False, True, 1), (True, False, 1),
-                                               (True, True, 4), (False, False, 8)])
-def test_library_accepts_every_plan_variant(graph, merged, tc, cluster):
+@pytest.mark.parametrize("merged,tc,cluster,group", [(False, False, 1, 32), (False, True, 1, 32), (True, False, 1, 32),
+                                                     (True, True, 4, 32), (False, False, 8, 32), (False, False, 1, 4),
+                                                     (True, False, 1, 8), (False, False, 1, 16)])
+def test_library_accepts_every_plan_variant(graph, merged, tc, cluster, group):
     """qx_create validates a plan before it touches a device: every plan the compiler emits
     (standalone or merged graph, CUDA-core or tensor-core forms, cluster sizes) passes the
     library's validation (without a GPU the call then fails on the device, status 3)."""
@@ -196,7 +210,7 @@ def test_library_accepts_every_plan_variant(graph, merged, tc, cluster):
     lib = C.CDLL(str(build.build()))
     lib.qx_last_error.restype = C.c_char_p
     g = load_graph(merged_graph_path()) if merged else graph
-    blob = compile_plan(g, cluster=cluster, tc=tc).blob()
+    blob = compile_plan(g, cluster=cluster, tc=tc, group=group).blob()
     h = C.c_void_p()
     st = lib.qx_create(blob, C.c_size_t(len(blob)), 4, 0, C.byref(h))
     assert st == 3, (st, lib.qx_last_error())

@@ -83,18 +83,20 @@ def test_load_over_used_state(qx, oracle_, programs):
     assert ex.errors() == 0
 
 
-@pytest.mark.parametrize("batch,cluster,tc", [(1, None, False), (5, 1, False), (37, None, False), (37, 2, False),
-                                              (1, None, True), (37, 1, True), (37, 4, True)])
-def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster, tc):
+@pytest.mark.parametrize("batch,cluster,tc,group", [(1, None, False, None), (5, 1, False, None),
+                                                    (37, None, False, None), (37, 2, False, None),
+                                                    (37, None, False, 16), (37, None, False, 8),
+                                                    (1, None, True, None), (37, 1, True, None), (37, 4, True, None)])
+def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster, tc, group):
     """Teacher-forced steps: every dim of every row equals the oracle's Executor2 step (cluster
-    None: the executor's own choice, 8 CTAs a group at these batches; tc: linear forms on the
-    tensor cores)."""
+    and group None: the executor's own choice, 4 machines a CTA at these batches; a cluster:
+    groups of 32 on that many CTAs; tc: linear forms on the tensor cores)."""
     pool = ["gen_small_7", "div_fuzz_0", "mul_fuzz_1", "digit_file", "gen_base_1", "refresh_70",
             "zba_rodata", "gen_many_11", "csr_putchar"]
     names = [pool[i % len(pool)] for i in range(batch)]
     progs = [programs[n]["prog"] for n in names]
     traces = [programs[n]["trace"] for n in names]
-    ex = qx.Executor(None, batch=batch, cluster=cluster, tc=tc)
+    ex = qx.Executor(None, batch=batch, cluster=cluster, tc=tc, group=group)
     ex.load_machines(0, progs)
     ost = _oracle_state(oracle_, progs)
     T = 60 if batch > 8 else 120
@@ -112,9 +114,11 @@ def test_step_matches_oracle(qx, oracle_, graph, programs, batch, cluster, tc):
     assert ex.errors() == 0
 
 
-@pytest.mark.parametrize("batch,n,cluster,tc", [(1, 3000, None, False), (40, 1500, None, False),
-                                                (40, 1500, 1, False), (40, 1500, 1, True), (1, 3000, None, True)])
-def test_free_run_matches_machine(qx, programs, batch, n, cluster, tc):
+@pytest.mark.parametrize("batch,n,cluster,tc,group", [(1, 3000, None, False, None), (40, 1500, None, False, None),
+                                                      (40, 1500, None, False, 8), (40, 1500, None, False, 16),
+                                                      (40, 1500, 1, False, None), (40, 1500, 1, True, None),
+                                                      (1, 3000, None, True, None)])
+def test_free_run_matches_machine(qx, programs, batch, n, cluster, tc, group):
     """Free-running generation: every token equals the traced machine's, and the machine state
     read back from the heads equals the traced state after the last complete record."""
     from qwenputer_b200 import workload
@@ -122,7 +126,7 @@ def test_free_run_matches_machine(qx, programs, batch, n, cluster, tc):
     progs = [programs[k]["prog"] for k in sorted(programs)]
     progs += workload.workload_programs("many", max(0, batch - len(progs)), 500)
     progs = progs[:batch]
-    ex = qx.Executor(None, batch=batch, cluster=cluster, tc=tc)
+    ex = qx.Executor(None, batch=batch, cluster=cluster, tc=tc, group=group)
     ex.load_machines(0, progs)
     ex.reset()
     go = int(oracle.lib().qxo_tok_family(18, 0))  # GO: the seventh control after 12 families
@@ -145,6 +149,36 @@ def test_free_run_matches_machine(qx, programs, batch, n, cluster, tc):
     assert ex.errors() == 0
 
 
+def test_machine_groups_agree(qx):
+    """Groups of 32, 16, 8 and 4 machines a CTA (the smaller ones with 2, 4 and 8 stream records
+    side by side in a warp): the same tokens, states, checksums and residuals (100 machines of the
+    bignum workload, a partial last group, 400 tokens)."""
+    from qwenputer_b200 import workload
+
+    B = 100
+    progs = workload.workload_programs("bignum", B, 78)
+    go = int(oracle.lib().qxo_tok_family(18, 0))
+    outs = []
+    for group in (32, 16, 8, 4):
+        ex = qx.Executor(None, batch=B, group=group, cluster=1 if group == 32 else None)
+        assert ex.group == group and ex.info(2) == -(-B // group)
+        ex.load_machines(0, progs)
+        ex.reset()
+        ex.set_tokens(0, [go] * B)
+        out = torch.zeros(400, B, dtype=torch.int32, device="cuda")
+        ex.run(400, out)
+        heads = [s["S"] for s in ex.steps if s["kind"] == "head"]
+        outs.append((out.cpu().numpy(), ex.checksums().cpu().numpy(),
+                     [float(h.double().sum()) for h in heads], ex.x.cpu().numpy()))
+        assert ex.errors() == 0
+        del ex
+    for o in outs[1:]:
+        assert np.array_equal(o[0], outs[0][0])
+        assert np.array_equal(o[1], outs[0][1])
+        assert o[2] == outs[0][2]
+        assert np.array_equal(o[3], outs[0][3])
+
+
 def test_cluster_sizes_agree(qx):
     """One group of 32 machines on 1, 2, 4 or 8 CTAs of a cluster, linear forms on the CUDA cores
     or the tensor cores: the same tokens, states and checksums (96 machines of the bignum
@@ -156,6 +190,7 @@ def test_cluster_sizes_agree(qx):
     outs = []
     for cluster, tc in ((1, False), (2, False), (4, False), (8, False), (1, True), (2, True), (8, True)):
         ex = qx.Executor(None, batch=96, cluster=cluster, tc=tc)
+        assert ex.group == 32
         assert ex.info(0) == cluster and ex.info(2) == 3 * cluster and ex.info(1) >= 1
         ex.load_machines(0, progs)
         ex.reset()

@@ -8,14 +8,17 @@ import oracle
 from plan_interp import PlanInterp
 
 
-@pytest.mark.parametrize("names,cluster,tc", [(["gen_small_7", "div_fuzz_0"], 1, False),
-                                               (["digit_file", "refresh_70"], 8, False),
-                                               (["gen_bignum_5", "mul_fuzz_1"], 1, True),
-                                               (["zba_rodata", "div_fuzz_1"], 4, True)])
-def test_plan_program_matches_oracle(oracle_, graph, programs, names, cluster, tc):
+@pytest.mark.parametrize("names,cluster,tc,group", [(["gen_small_7", "div_fuzz_0"], 1, False, 32),
+                                                     (["digit_file", "refresh_70"], 8, False, 32),
+                                                     (["gen_bignum_5", "mul_fuzz_1"], 1, True, 32),
+                                                     (["zba_rodata", "div_fuzz_1"], 4, True, 32),
+                                                     (["gen_bignum_5", "digit_file"], 1, False, 16),
+                                                     (["mul_fuzz_1", "refresh_70"], 1, False, 8),
+                                                     (["div_fuzz_0", "zba_rodata"], 1, False, 4)])
+def test_plan_program_matches_oracle(oracle_, graph, programs, names, cluster, tc, group):
     from qwenputer_b200.plan import compile_plan
 
-    P = compile_plan(graph, cluster=cluster, tc=tc)
+    P = compile_plan(graph, cluster=cluster, tc=tc, group=group)
     B = len(names)
     it = PlanInterp(P, B)
     ost = oracle_.new_state(B)
