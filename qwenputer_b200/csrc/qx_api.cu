@@ -203,6 +203,53 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
     return QX_OK;
 }
 
+// The pieces of one stream phase's warp ranges: each a header line and n body lines of 32 / group
+// quads inside one ring chunk; every slot of a line agrees on n, on the first / last flags and on
+// R_SPLIT (which only form phases of bundled plans use, and which the whole warp then takes);
+// every row a header names lies inside the rows (the zero row included).
+bool stream_ranges_ok(const qx_plan_header &h, const uint8_t *plan, uint32_t kind, const uint32_t *wp) {
+    const uint4 *st = reinterpret_cast<const uint4 *>(plan + h.off[QX_S_STREAM]);
+    const uint32_t R = 32 / h.group, chunk = QX_RING_QUADS * R;
+    const uint64_t rows_end = (uint64_t)(h.n_slots + h.n_scratch + 1) * (h.group + 1) * 4;
+    for (uint32_t w = 0; w < h.nw * h.cluster; w++) {
+        const uint32_t start = wp[w], end = wp[w + 1];
+        uint32_t i = start;
+        while (i < end) {
+            const uint32_t fl = st[i].w >> 24, n = st[i].w & 0xFFFFFFu;
+            if (fl & QX_R_SKIP) {
+                i = start + ((i - start) / chunk + 1) * chunk;
+                continue;
+            }
+            if (n + 1 > (uint32_t)QX_RING_QUADS || (i - start) / chunk != (i - start + R * (n + 1) - 1) / chunk ||
+                i + R * (n + 1) > end)
+                return false;
+            if ((fl & QX_R_SPLIT) && (kind != QX_PH_FORMS || R == 1)) return false;
+            const uint32_t nc = st[i].y;  // (units: the piece's constant-gate quads)
+            for (uint32_t k = 0; k < R; k++) {
+                const uint4 hk = st[i + k];
+                if ((hk.w & 0xFFFFFFu) != n || ((hk.w >> 24) ^ fl) & (QX_R_FIRST | QX_R_LAST | QX_R_SPLIT | QX_R_SKIP))
+                    return false;
+                if (kind == QX_PH_FORMS && (hk.x >= rows_end || hk.y >= rows_end)) return false;
+                if (kind == QX_PH_UNITS && (hk.x >= rows_end || hk.y != nc || nc > n || (n - nc) % 2)) return false;
+                if (kind == QX_PH_KSEL &&
+                    ((hk.x & 0xFFFFu) >= h.n_ksel_slots || hk.y >= rows_end || hk.z >= rows_end))
+                    return false;
+            }
+            for (uint32_t j = 0; j < n; j++) {
+                for (uint32_t k = 0; k < R; k++) {
+                    const uint4 b = st[i + R * (1 + j) + k];
+                    const bool second = kind == QX_PH_UNITS && j >= nc && (j - nc) % 2;  // a unit's constants
+                    if (!second && b.x >= rows_end) return false;
+                    if (kind == QX_PH_FORMS && b.z >= rows_end) return false;
+                    if (kind == QX_PH_UNITS && j >= nc && !second && b.y >= rows_end) return false;
+                }
+            }
+            i += R * (n + 1);
+        }
+    }
+    return true;
+}
+
 // every snapshot table names head state, every program ends, and every value-head phase names at most QX_VH_CHUNK heads of the section
 qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
     {
@@ -243,6 +290,8 @@ qx_status validate_programs(const qx_plan_header &h, const uint8_t *plan) {
                         return fail(QX_ERR_INVALID_PLAN, "stream phase %llu: a warp range outside the stream",
                                     (unsigned long long)i);
                 }
+                if (!stream_ranges_ok(h, plan, kind, wp + p[i].c))
+                    return fail(QX_ERR_INVALID_PLAN, "stream phase %llu: a malformed piece", (unsigned long long)i);
             }
             if ((kind == QX_PH_VH || kind == QX_PH_VHRUN) &&
                 (p[i].b < p[i].a || p[i].b - p[i].a > QX_VH_CHUNK || p[i].b > h.cnt[QX_S_VHEADS] ||
@@ -439,6 +488,11 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.D = (int32_t)h.D;
     d.smem_rows = (int32_t)(h.n_slots + h.n_scratch);
     d.group = (int32_t)h.group;
+    d.n_run_prog = (int32_t)h.cnt[QX_S_RUN_PROG];
+    d.n_step_prog = (int32_t)h.cnt[QX_S_STEP_PROG];
+    d.n_warp_ptr = (int32_t)h.cnt[QX_S_WARP_PTR];
+    d.tables_smem = d.group < 32 && (size_t)std::max(d.n_run_prog, d.n_step_prog) * sizeof(qx_phase) +
+                                            (size_t)d.n_warp_ptr * 4 <= QX_TABLE_BYTES;
     d.zero_row = (uint32_t)d.smem_rows * (d.group + 1) * 4;
     d.cluster = (int32_t)h.cluster;
     d.one_row = (int32_t)h.one_row;
@@ -499,6 +553,11 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
         if (cudaMemset(p, 0, vb) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "delta init"));
     }
     if (cudaMemset(d.state_bytes, 0, 64) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "counter init"));
+#ifdef QX_PHASE_CLOCKS
+    if ((s = dev_alloc(ex, &p, 256 * 16)) != QX_OK) return bail(s);
+    d.phase_clk = static_cast<unsigned long long *>(p);
+    if (cudaMemset(p, 0, 256 * 16) != cudaSuccess) return bail(fail(QX_ERR_CUDA, "phase clocks"));
+#endif
     if (cudaMemset(d.x, 0, xb) != cudaSuccess || cudaMemset(d.err, 0, (size_t)batch * 4) != cudaSuccess ||
         cudaMemset(d.count, 0, (size_t)batch * 8) != cudaSuccess ||
         cudaMemset(d.halt_at, 0xFF, (size_t)batch * 8) != cudaSuccess ||
@@ -606,6 +665,9 @@ qx_status qx_buffer(qx_t *ex, int32_t kind, int32_t i, void **ptr, size_t *bytes
     case 8:
         if (!d.img) return fail(QX_ERR_INVALID_ARG, "qx_buffer: the executor shares no tables");
         *ptr = d.img; *bytes = (size_t)ex->B * 4; return QX_OK;
+#ifdef QX_PHASE_CLOCKS
+    case 9: *ptr = d.phase_clk; *bytes = 256 * 16; return QX_OK;  // per-phase cycle counters
+#endif
     default: return fail(QX_ERR_INVALID_ARG, "qx_buffer: kind %d", kind);
     }
 }

@@ -422,14 +422,28 @@ __global__ void __launch_bounds__(QX_NT, 1)
             halt_at = d.halt_at[m];
         }
     }
+    // the running program and the warp ranges: from shared memory when the plan's tables fit there
+    const qx_phase *prog = RUN ? d.run_prog : d.step_prog;
+    const uint32_t *warp_ptr = d.warp_ptr;
+    if (R > 1 && d.tables_smem) {
+        const int np = RUN ? d.n_run_prog : d.n_step_prog;
+        qx_phase *sp = reinterpret_cast<qx_phase *>(rings + qx_ring_bytes(d));
+        uint32_t *sw = reinterpret_cast<uint32_t *>(sp + np);
+        for (int i = threadIdx.x; i < np; i += QX_NT) sp[i] = prog[i];
+        for (int i = threadIdx.x; i < d.n_warp_ptr; i += QX_NT) sw[i] = warp_ptr[i];
+        prog = sp;
+        warp_ptr = sw;
+    }
     phase_sync(C);  // (with C > 1, also: every CTA of the cluster runs before rows are shared)
     if (TC) tc_after();
-    const qx_phase *prog = RUN ? d.run_prog : d.step_prog;
     for (int32_t t = 0; t < n_tokens; t++) {
         for (int pc = 0;; pc++) {
             const qx_phase ph = prog[pc];
             const uint32_t kind = ph.kind & 0xFFu;
             if (kind == QX_PH_END) break;
+#ifdef QX_PHASE_CLOCKS
+            const long long pclk0 = clock64();  // (thread 0: the phase up to its barrier's release)
+#endif
             switch (kind) {
             case QX_PH_ZERO:
                 for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) QX_AT(sml, d.rows[ph.a + i]) = 0.0f;
@@ -477,7 +491,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // two forms a record: pieces [dst A, dst B, 0, n | flags] + n quads [row, w of A,
                 // row, w of B]: F = sum w * X[row], two independent sums a lane (a bundled plan:
                 // lines of R quads, this lane's record is quad `way` of each line)
-                const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
+                const uint32_t b0 = warp_ptr[ph.c + gw], b1 = warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream<R> st;
                 st.start(d.stream, ring, b0, b1, lane);
@@ -510,9 +524,21 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         a0 = fmaf(__uint_as_float(e.y), QX_AT(sml, e.x), a0);
                         a1 = fmaf(__uint_as_float(e.w), QX_AT(sml, e.z), a1);
                     }
-                    if ((fl & (QX_R_LAST | QX_R_NOP)) == QX_R_LAST) {
-                        put_all(&QX_AT(sml, h.x), a0 + a2, C);
-                        put_all(&QX_AT(sml, h.y), a1 + a3, C);
+                    if (fl & QX_R_LAST) {
+                        float sa = a0 + a2, sb = a1 + a3;
+                        if (R > 1 && (fl & QX_R_SPLIT)) {
+                            // one pair over every slot (the whole warp takes this branch): the
+                            // slots' partial sums meet across the lanes of each machine
+#pragma unroll
+                            for (int off = M; off < 32; off <<= 1) {
+                                sa += __shfl_xor_sync(0xFFFFFFFFu, sa, off);
+                                sb += __shfl_xor_sync(0xFFFFFFFFu, sb, off);
+                            }
+                        }
+                        if (!(fl & QX_R_NOP) && (!(fl & QX_R_SPLIT) || way == 0)) {
+                            put_all(&QX_AT(sml, h.x), sa, C);
+                            put_all(&QX_AT(sml, h.y), sb, C);
+                        }
                     }
                     st.skip(n);
                 }
@@ -529,7 +555,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // coef, ca] [cb, ...] (coef (F[a] + ca) relu(F[b] + cb)); ONE is 1 on every
                 // machine (no sublayer writes it), so its constant terms enter as plain constants
                 // (a bundle's records share n and n_const piece by piece)
-                const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
+                const uint32_t b0 = warp_ptr[ph.c + gw], b1 = warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream<R> st;
                 st.start(d.stream, ring, b0, b1, lane);
@@ -586,7 +612,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // (R_MERGE) merges each part's selection into the slot words by atomic maxima
                 // (the slots start at 0: cleared by the value-head serving phase before)
                 // (a bundle holds keys only or queries only)
-                const uint32_t b0 = d.warp_ptr[ph.c + gw], b1 = d.warp_ptr[ph.c + gw + 1];
+                const uint32_t b0 = warp_ptr[ph.c + gw], b1 = warp_ptr[ph.c + gw + 1];
                 if (b0 == b1) break;
                 Stream<R> st;
                 st.start(d.stream, ring, b0, b1, lane);
@@ -711,6 +737,18 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         anyq |= qj >= 0;
                     }
                     const bool need = act && vin && (fcode != 0 || wrow >= 0 || anyq);
+                    if (need && anyq) {
+                        // the rows the serving phase will read: on their way into L2 now
+                        const float *Sq = d.S[vh.hl] + qx_copy(d, vh.hl, m) * ((size_t)d.V[vh.hl] * (QX_HD * QX_HD)) +
+                                          (size_t)vh.vh * (QX_HD * QX_HD);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const uint32_t qj = qpack >> (8 * j) & 0xFFu;
+                            if (qj)
+                                asm volatile("cp.async.bulk.prefetch.L2.global [%0], 512;" ::"l"(Sq + (qj - 1) * QX_HD)
+                                             : "memory");
+                        }
+                    }
                     const unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
                     if (!mask) continue;
                     // the value head's records, padded to a multiple of four (pad records: bit 31)
@@ -796,8 +834,15 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         }
                     }
                     unsigned int rows = 0;  // 512-byte row transfers
+                    // per record: decay, write, then the read of its query rows as decayed and
+                    // written (o), and its normaliser; the four records' chains are independent
+                    float4 o[4];
+                    float norm[4], inv[4];
+                    bool any[4], pw2[4];
 #pragma unroll
                     for (int b = 0; b < 4; b++) {
+                        o[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        any[b] = false;
                         if (!valid[b]) continue;
                         float *Sb = const_cast<float *>(S0) + qx_copy(d, vh.hl, mbase + mmv[b]) * mstride;
                         const float *smm = sm + mmv[b];
@@ -824,8 +869,6 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             rows++;
                         }
                         // the read: sum of the query rows as decayed and written
-                        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                        bool any = false;
 #pragma unroll
                         for (int j = 0; j < QH; j++) {
                             if (qr[b][j] < 0) continue;
@@ -836,53 +879,83 @@ __global__ void __launch_bounds__(QX_NT, 1)
                                 sv.x = __fmul_rn(sv.x, f[b]); sv.y = __fmul_rn(sv.y, f[b]);
                                 sv.z = __fmul_rn(sv.z, f[b]); sv.w = __fmul_rn(sv.w, f[b]);
                             }
-                            o.x = __fadd_rn(o.x, sv.x); o.y = __fadd_rn(o.y, sv.y);
-                            o.z = __fadd_rn(o.z, sv.z); o.w = __fadd_rn(o.w, sv.w);
-                            any = true;
+                            o[b].x = __fadd_rn(o[b].x, sv.x); o[b].y = __fadd_rn(o[b].y, sv.y);
+                            o[b].z = __fadd_rn(o[b].z, sv.z); o[b].w = __fadd_rn(o[b].w, sv.w);
+                            any[b] = true;
                             rows++;
                         }
-                        if (!any) continue;
-                        float ref = __fadd_rn(__fmul_rn(o.x, o.x), __fmul_rn(o.y, o.y));
+                    }
+                    // ref = o0^2 + o1^2 of each read (columns 0 and 1: lane 0), norm = sqrt(ref / 128);
+                    // when norm is a power of two (the usual read: the markers give ref = 128 * 4^e),
+                    // multiplying by its exact reciprocal rounds the same as the division
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        float ref = __fadd_rn(__fmul_rn(o[b].x, o[b].x), __fmul_rn(o[b].y, o[b].y));
                         ref = __shfl_sync(0xFFFFFFFFu, ref, 0);  // (uniform: the batch's records are)
-                        const float norm = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
-                        // o / norm; when norm is a power of two (the usual read: the markers
-                        // give ref = 128 * 4^e), multiplying by its exact reciprocal rounds the same
-                        const uint32_t nb = __float_as_uint(norm);
-                        const bool pow2 = (nb & 0x7FFFFFu) == 0u && nb >= 0x01000000u && nb < 0x7E800000u;
-                        const float inv = pow2 ? __uint_as_float(0x7F000000u - nb) : 0.0f;
-                        const float oc[4] = {o.x, o.y, o.z, o.w};
-                        if (vh.nout != QX_OUT_DIRECT) {
-                            // at most 4 output rows: per-row sums over the warp, one add per row
-                            float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+                        any[b] = any[b] && ref > 0.0f;  // a zero read adds nothing
+                        norm[b] = __fsqrt_rn(__fdiv_rn(ref, 128.0f));
+                        const uint32_t nb = __float_as_uint(norm[b]);
+                        pw2[b] = (nb & 0x7FFFFFu) == 0u && nb >= 0x01000000u && nb < 0x7E800000u;
+                        inv[b] = pw2[b] ? __uint_as_float(0x7F000000u - nb) : 0.0f;
+                    }
+                    if (vh.nout != QX_OUT_DIRECT) {
+                        // at most 4 output rows: per (record, row) the sum over the warp's columns,
+                        // reduced-and-scattered over the lanes (16 sums in 16 shuffles: lane L
+                        // ends with sum (L >> 1), record (L >> 3), row (L >> 1) & 3), one L2 add each
+                        float pv[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) pv[i] = 0.0f;
+#pragma unroll
+                        for (int b = 0; b < 4; b++) {
+                            if (!any[b]) continue;
+                            const float *smm = sm + mmv[b];
+                            const float x0m = QX_ATC(smm, d.one_row);
+                            const float oc[4] = {o[b].x, o[b].y, o[b].z, o[b].w};
 #pragma unroll
                             for (int k = 0; k < 4; k++) {
                                 if (orow[k] == QX_NONE32) continue;
                                 const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
-                                const float out = ref > 0.0f ? (pow2 ? oc[k] * inv : __fdiv_rn(oc[k], norm)) : 0.0f;
+                                const float out = pw2[b] ? oc[k] * inv[b] : __fdiv_rn(oc[k], norm[b]);
                                 const float val = __fmul_rn(__fmul_rn(out, z), ow[k]);
-                                p0 += orow[k] == 0 ? val : 0.0f;
-                                p1 += orow[k] == 1 ? val : 0.0f;
-                                p2 += orow[k] == 2 ? val : 0.0f;
-                                p3 += orow[k] == 3 ? val : 0.0f;
-                            }
 #pragma unroll
-                            for (int off = 16; off > 0; off >>= 1) {
-                                p0 += __shfl_xor_sync(0xFFFFFFFFu, p0, off);
-                                p1 += __shfl_xor_sync(0xFFFFFFFFu, p1, off);
-                                p2 += __shfl_xor_sync(0xFFFFFFFFu, p2, off);
-                                p3 += __shfl_xor_sync(0xFFFFFFFFu, p3, off);
+                                for (int r = 0; r < 4; r++) pv[4 * b + r] += orow[k] == (uint32_t)r ? val : 0.0f;
                             }
-                            if ((uint32_t)lane < vh.nout) {
-                                const uint32_t r = lane == 0 ? vh.out4[0] : lane == 1 ? vh.out4[1] : lane == 2 ? vh.out4[2] : vh.out4[3];
-                                const float pr = lane == 0 ? p0 : lane == 1 ? p1 : lane == 2 ? p2 : p3;
-                                atomicAdd(Dp + (r >> 2) + mmv[b], pr);  // an L2 reduction
+                        }
+#pragma unroll
+                        for (int half = 8, bit = 16; half >= 1; half >>= 1, bit >>= 1) {
+                            // keep half of the sums (the upper half where this lane's bit is set),
+                            // add the partner's copy of the same half
+                            const bool up = lane & bit;
+#pragma unroll
+                            for (int i = 0; i < half; i++) {
+                                const float give = up ? pv[i] : pv[half + i];
+                                const float keep = up ? pv[half + i] : pv[i];
+                                pv[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, give, bit);
                             }
-                        } else {
+                        }
+                        pv[0] += __shfl_xor_sync(0xFFFFFFFFu, pv[0], 1);
+                        const int sb = lane >> 3, sr = (lane >> 1) & 3;
+                        if (!(lane & 1) && (uint32_t)sr < vh.nout) {
+                            bool hit = false;
+                            int mm = 0;
+#pragma unroll
+                            for (int b = 0; b < 4; b++)
+                                if (b == sb) { hit = any[b]; mm = mmv[b]; }
+                            const uint32_t orw = sr == 0 ? vh.out4[0] : sr == 1 ? vh.out4[1] : sr == 2 ? vh.out4[2] : vh.out4[3];
+                            if (hit) atomicAdd(Dp + (orw >> 2) + mm, pv[0]);  // an L2 reduction
+                        }
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < 4; b++) {
+                            if (!any[b]) continue;
+                            const float *smm = sm + mmv[b];
+                            const float x0m = QX_ATC(smm, d.one_row);
+                            const float oc[4] = {o[b].x, o[b].y, o[b].z, o[b].w};
 #pragma unroll
                             for (int k = 0; k < 4; k++) {
                                 if (orow[k] == QX_NONE32) continue;
                                 const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
-                                const float out = ref > 0.0f ? (pow2 ? oc[k] * inv : __fdiv_rn(oc[k], norm)) : 0.0f;
+                                const float out = pw2[b] ? oc[k] * inv[b] : __fdiv_rn(oc[k], norm[b]);
                                 atomicAdd(Dp + (orow[k] >> 2) + mmv[b], __fmul_rn(__fmul_rn(out, z), ow[k]));
                             }
                         }
@@ -1042,6 +1115,12 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 break;
             }
             if (!(ph.kind & QX_PH_NOSYNC)) phase_sync(C);
+#ifdef QX_PHASE_CLOCKS
+            if (threadIdx.x == 0 && d.phase_clk && pc < 256) {
+                atomicAdd(&d.phase_clk[2 * pc], (unsigned long long)(clock64() - pclk0));
+                atomicAdd(&d.phase_clk[2 * pc + 1], 1ull);
+            }
+#endif
         }
     }
     if (threadIdx.x == 0 && d.state_bytes) atomicAdd(d.state_bytes, 512ull * *touched);

@@ -45,6 +45,8 @@ struct QxDev {
     int64_t *count;             // [B] tokens generated
     int64_t *halt_at;           // [B] index (1-based) of the first HALT token, -1 none
     unsigned long long *state_bytes;  // [1] head-state bytes the kernel read or wrote (512 B rows)
+    unsigned long long *phase_clk;    // [256][2] per program position: SM cycles, visits (builds
+                                      // with QX_PHASE_CLOCKS only; null otherwise)
     // sizes
     int32_t B, Bpad, D;
     int32_t smem_rows, one_row, n_fam, n_pay, n_feat, n_families, n_emb_rows, n_born0;
@@ -54,6 +56,8 @@ struct QxDev {
     int32_t group;      // machines a CTA runs: 32, or 16 / 8 / 4 (a warp's lanes then run
                         // 32 / group records side by side; rows are group + 1 floats)
     int32_t n_zero_rows;
+    int32_t n_run_prog, n_step_prog, n_warp_ptr;  // entries of the programs and of WARP_PTR
+    int32_t tables_smem;  // 1: the kernel copies the running program and WARP_PTR to shared memory
     // tensor-core form phases
     const qx_mma_phase *mma_phases;
     const qx_mma_tile *mma_tiles;
@@ -102,6 +106,7 @@ __device__ __forceinline__ size_t qx_copy(const QxDev &d, uint32_t hl, int m) {
 #define QX_R_QUERY 8u
 #define QX_R_MERGE 0x10u  // a part of a split key / query record: merged into the slot words
 #define QX_R_NOP 0x20u    // a bundle's padding record: computes on the zero row, stores nothing
+#define QX_R_SPLIT 0x40u  // a bundle that is one form pair over every record slot (warp-reduced)
 #define QX_R_SKIP 0x80u
 #define QX_RING_BYTES (QX_NW * 2 * QX_RING_QUADS * 16)
 
@@ -115,4 +120,10 @@ __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
 __host__ __device__ inline size_t qx_ring_bytes(const QxDev &d) {
     return (size_t)QX_NW * 2 * QX_RING_QUADS * 16 * (32 / d.group);
 }
-__host__ __device__ inline size_t qx_smem_bytes(const QxDev &d) { return qx_ring_offset(d) + qx_ring_bytes(d); }
+// bundled plans (groups of fewer than 32 machines) keep the running phase program and the warp
+// ranges in shared memory, after the rings (tables_smem: they fit QX_TABLE_BYTES)
+#define QX_TABLE_BYTES 8192
+__host__ __device__ inline size_t qx_table_bytes(const QxDev &d) { return d.group < 32 ? QX_TABLE_BYTES : 0; }
+__host__ __device__ inline size_t qx_smem_bytes(const QxDev &d) {
+    return qx_ring_offset(d) + qx_ring_bytes(d) + qx_table_bytes(d);
+}

@@ -72,9 +72,13 @@ NOSYNC = 0x100  # phase kind flag: no barrier after the phase
 # crossing a ring chunk of RING_QUADS quads (counted from the warp's range start); a record longer
 # than a piece continues in the next pieces of the same warp.  In a bundled plan (group < 32) the
 # same holds for lines of WAYS quads: a piece is a header line and n body lines, a ring chunk
-# RING_QUADS lines; R_NOP marks a padding record of a bundle (it stores nothing)
+# RING_QUADS lines; R_NOP marks a padding record of a bundle (it stores nothing), R_SPLIT a bundle
+# that is one long form pair split over the record slots (line j holds its terms j * WAYS ..
+# j * WAYS + WAYS - 1; the slots' partial sums meet in a warp reduction, slot 0 stores)
 PIECE_MAX = 16
-R_FIRST, R_LAST, R_STORE, R_QUERY, R_MERGE, R_NOP, R_SKIP = 1, 2, 4, 8, 0x10, 0x20, 0x80
+R_FIRST, R_LAST, R_STORE, R_QUERY, R_MERGE, R_NOP, R_SPLIT, R_SKIP = 1, 2, 4, 8, 0x10, 0x20, 0x40, 0x80
+# form pairs of a bundled plan at least this long are split over the record slots
+FORM_SPLIT_MIN = {1: 1 << 30, 2: 24, 4: 24, 8: 24}
 # value heads a VH phase lists: its worklist of (value head, machine) records, 8 bytes each,
 # lives in the stream rings (NW x 2 x RING_QUADS x 16 bytes = 2048 records for 16 warps); with a
 # cluster the rings also hold the CTA's output deltas (one row per output row of the phase)
@@ -87,7 +91,7 @@ UNIT_CHUNK = 64  # FFN nodes with more units are split into records of at most t
 KSEL_PART = {1: 128, 2: 64, 3: 48, 4: 32, 5: 32, 6: 24, 7: 24, 8: 16}
 # the same for bundled plans, by record slots a warp (WAYS): the key-select phase of a group
 # spreads over more slots when each part is shorter
-KSEL_PART_WAYS = {1: 128, 2: 64, 4: 32, 8: 32}
+KSEL_PART_WAYS = {1: 128, 2: 64, 4: 16, 8: 16}
 # FFN nodes of a bundled plan split into records of at most this many units
 UNIT_CHUNK_WAYS = {1: 64, 2: 64, 4: 32, 8: 32}
 SEC = ["RUN_PROG", "STEP_PROG", "ROWS", "PAIRS", "STREAM", "VHSUM_ROWS", "WARP_PTR", "STAGES",
@@ -102,6 +106,8 @@ TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
                + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
                + [f"bn2.{i}" for i in range(4)] + [f"ram{i}" for i in range(32)])
 SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
+# bundled plans: shared memory for the running phase program and the warp ranges
+TABLE_BYTES = 8192
 # tensor-core form phases (PH["MMA"]): F[form, machine] = sum W[form, k] X[k, machine] on tcgen05
 # as M = 128 forms (a form block) x N = 32 machines x K = 16 source rows (a K block) tiles, bf16
 # operands (every weight and every value a form reads is bf16-exact) and fp32 accumulators in
@@ -140,7 +146,7 @@ def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int, group: int = 32) -> in
     """Shared memory after the rows: the zero row, key-select slots, the decode area, a counter
     block and the per-warp stream rings (two halves of RING_QUADS lines of 32 / group quads)."""
     return (row_pad(group) * 4 + ksel_slots * 32 * (1 + qhot) * 4 + 32 * 18 * 4 + 64 + 16
-            + nw * 2 * RING_QUADS * 16 * (32 // group))
+            + nw * 2 * RING_QUADS * 16 * (32 // group) + (TABLE_BYTES if group < 32 else 0))
 
 
 def _bf16_bits(w: float) -> int:
@@ -472,6 +478,19 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
             eb = [(W(rowmap(t)), _fbits(w)) for t, w in tb]
             prs.append((ea, eb, W(da), W(db) if db is not None else ZW))
             stats["form_nnz"] += len(ta) + len(tb)
+        split = [pr for pr in prs if max(len(pr[0]), len(pr[1])) >= FORM_SPLIT_MIN[ways]]
+        prs = [pr for pr in prs if max(len(pr[0]), len(pr[1])) < FORM_SPLIT_MIN[ways]]
+        for ea, eb, xa, xb in split:
+            # one pair over the WAYS slots: slot s takes terms s, s + WAYS, ... (zero-padded)
+            n = -(-max(len(ea), len(eb)) // ways)
+            ea = ea + [(ZW, 0)] * (n * ways - len(ea))
+            eb = eb + [(ZW, 0)] * (n * ways - len(eb))
+            lanes = [pieces(xa, xb, 0, [(ea[j * ways + k][0], ea[j * ways + k][1], eb[j * ways + k][0],
+                                          eb[j * ways + k][1]) for j in range(n)], R_SPLIT)
+                     for k in range(ways)]
+            recs.append(zip_lanes(lanes))
+            costs.append(4 * n + 14 * len(recs[-1]) + 12)
+            stats["split_pairs"] += 1
         for bd in bundles(prs, lambda pr: max(len(pr[0]), len(pr[1]))):
             n = max(max(len(ea), len(eb)) for ea, eb, _, _ in bd)
             lanes = []

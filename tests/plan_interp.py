@@ -60,7 +60,7 @@ class PlanInterp:
         R_SKIP padding dropped (a record's pieces are consecutive and end with R_LAST).  In a
         bundled plan a piece is a header line and n body lines of `ways` quads: record slot s
         reads quad s of each line; the bundle's padding records (R_NOP) are dropped."""
-        from qwenputer_b200.plan import R_LAST, R_NOP, R_SKIP
+        from qwenputer_b200.plan import R_LAST, R_NOP, R_SKIP, R_SPLIT
 
         st = self.s["STREAM"].astype(np.int64)
         wp = self.s["WARP_PTR"].astype(np.int64)
@@ -83,9 +83,13 @@ class PlanInterp:
                     cur[sl].append((hs[sl], body[:, sl]))
                 i += R * (1 + n)
                 if fl & R_LAST:
-                    for sl in range(R):
-                        if not (int(cur[sl][0][0][3]) >> 24) & R_NOP:
-                            recs.append(cur[sl])
+                    if fl & R_SPLIT:  # one record over the slots: its pieces hold every slot's terms
+                        recs.append([(pc[0], np.concatenate([cur[sl][j][1] for sl in range(R)]))
+                                     for j, pc in enumerate(cur[0])])
+                    else:
+                        for sl in range(R):
+                            if not (int(cur[sl][0][0][3]) >> 24) & R_NOP:
+                                recs.append(cur[sl])
                     cur = [[] for _ in range(R)]
             assert not any(cur)
             out.append(recs)

@@ -75,7 +75,7 @@ def test_plan_is_consistent(graph, cluster, tc, group):
     wp = s["WARP_PTR"].astype(np.int64)
     # walk every stream piece of every phase: rows in range, pieces inside one ring chunk,
     # records complete, a bundle's records of one shape, ranges end on their warp's range
-    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_NOP, R_QUERY, R_SKIP
+    from qwenputer_b200.plan import PIECE_MAX, R_FIRST, R_LAST, R_NOP, R_QUERY, R_SKIP, R_SPLIT
 
     chunk = RING_QUADS * R
     for ph in s["RUN_PROG"]:
@@ -102,6 +102,7 @@ def test_plan_is_consistent(graph, cluster, tc, group):
                     h, b = hs[sl], body[:, sl]
                     fs = int(h[3]) >> 24
                     assert int(h[3]) & 0xFFFFFF == n and fs & 3 == fl & 3, "a bundle's pieces differ"
+                    assert (fs ^ fl) & R_SPLIT == 0 and (not fs & R_SPLIT or (k == PH["FORMS"] and R > 1))
                     if k == PH["FORMS"]:
                         assert h[0] < rows and h[0] % rb == 0 and h[1] < rows and h[1] % rb == 0
                         assert np.all(b[:, 0] < rows) and np.all(b[:, 2] < rows)
