@@ -145,7 +145,8 @@ typedef struct {
                                       for few machines per GPU: a warp then runs 32 / group stream
                                       records side by side (lines of 32 / group quads), residual
                                       rows are group + 1 floats; no cluster, no tensor cores */
-    uint32_t reserved;
+    uint32_t table_bytes;          /* shared memory after the stream rings for plan tables the
+                                      token loop reads (0 for groups of 32) */
     /* sections: byte offset from the blob start, element count */
     uint64_t off[48];
     uint64_t cnt[48];
@@ -197,11 +198,14 @@ enum { /* section ids of qx_plan_header.off / cnt */
 #define QX_PLAN_FLAG_MMA 1u    /* the programs use QX_PH_MMA phases (the kernel holds tensor memory) */
 #define QX_PLAN_FLAG_MERGED 2u /* merged readout: the next token from the signs of the code dims,
                                   a Q code naming the text token PRINTABLE[payload] */
+#define QX_PLAN_FLAG_DIRECT_OUT 4u /* value-head outputs add straight into the residual rows
+                                      (plans of one CTA a group): OUT_ROW and out4 name residual
+                                      rows, the programs have no QX_PH_VHSUM phase */
 #define QX_FEAT_DEFERRED 0x80000000u /* FEAT_ROW: the feature goes to x[machine][low bits] and is
                                         loaded where it is first used (a LOADX phase) */
 #define QX_TEXT_TOKEN (1 << 24) /* a text token in the machine's stream: QX_TEXT_TOKEN | qid */
 
-#define QX_PLAN_VERSION 17
+#define QX_PLAN_VERSION 18
 #define QX_RING_QUADS 32   /* quads per half of a warp's stream ring in shared memory */
 
 /* ---- machine images (the traced machine's state, ref.Machine, ref.py:386-414) --------------- */

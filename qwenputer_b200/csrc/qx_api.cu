@@ -172,6 +172,10 @@ qx_status validate(const qx_plan_header &h, size_t bytes) {
         return fail(QX_ERR_INVALID_PLAN, "groups of %u machines (32, 16, 8 or 4)", h.group);
     if (h.group != 32 && (h.cluster != 1 || (h.flags & QX_PLAN_FLAG_MMA)))
         return fail(QX_ERR_INVALID_PLAN, "a group of %u machines runs on one CTA, without tensor-core phases", h.group);
+    if ((h.flags & QX_PLAN_FLAG_DIRECT_OUT) && h.cluster != 1)
+        return fail(QX_ERR_INVALID_PLAN, "direct value-head outputs need one CTA a group");
+    if (h.table_bytes % 16 || h.table_bytes > 65536 || (h.group == 32 && h.table_bytes))
+        return fail(QX_ERR_INVALID_PLAN, "plan-table area of %u bytes", h.table_bytes);
     if (h.n_head_levels > QX_MAX_HL) return fail(QX_ERR_INVALID_PLAN, "too many head sublayers");
     if (h.n_pay > 16 || h.n_fam > 16) return fail(QX_ERR_INVALID_PLAN, "output code too wide");
     if (h.n_born0 > h.n_feat) return fail(QX_ERR_INVALID_PLAN, "embedding dims mismatch");
@@ -466,6 +470,7 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.mma_tiles = sec<qx_mma_tile>(ex, QX_S_MMA_TILES);
     d.tiledata = sec<uint4>(ex, QX_S_TILEDATA);
     d.has_mma = (h.flags & QX_PLAN_FLAG_MMA) ? 1 : 0;
+    d.direct_out = (h.flags & QX_PLAN_FLAG_DIRECT_OUT) ? 1 : 0;
     d.feat_dim = sec<uint32_t>(ex, QX_S_FEAT_DIM);
     d.code_row = sec<uint32_t>(ex, QX_S_CODE_ROW);
     d.text_words = sec<uint32_t>(ex, QX_S_TEXT_WORDS);
@@ -491,8 +496,24 @@ qx_status qx_create(const void *plan, size_t plan_bytes, int32_t batch, int32_t 
     d.n_run_prog = (int32_t)h.cnt[QX_S_RUN_PROG];
     d.n_step_prog = (int32_t)h.cnt[QX_S_STEP_PROG];
     d.n_warp_ptr = (int32_t)h.cnt[QX_S_WARP_PTR];
-    d.tables_smem = d.group < 32 && (size_t)std::max(d.n_run_prog, d.n_step_prog) * sizeof(qx_phase) +
-                                            (size_t)d.n_warp_ptr * 4 <= QX_TABLE_BYTES;
+    {
+        // plan tables into the shared-memory table area, in order, while they fit
+        d.table_bytes = h.table_bytes;
+        const uint64_t words[6] = {(uint64_t)std::max(d.n_run_prog, d.n_step_prog) * (sizeof(qx_phase) / 4),
+                                   h.cnt[QX_S_WARP_PTR], h.cnt[QX_S_VHEADS] * (sizeof(qx_vhead) / 4),
+                                   h.cnt[QX_S_ROWS], h.cnt[QX_S_VHSUM_ROWS], h.cnt[QX_S_STAGES] * (sizeof(qx_stage) / 4)};
+        uint64_t at = 0;
+        for (int t = 0; t < 6; t++) {
+            const uint64_t bytes = (words[t] * 4 + 15) & ~15ull;
+            d.tab_words[t] = (uint32_t)words[t];
+            if (d.group < 32 && at + bytes <= d.table_bytes) {
+                d.tab_off[t] = (uint32_t)at;
+                at += bytes;
+            } else {
+                d.tab_off[t] = QX_NONE32;
+            }
+        }
+    }
     d.zero_row = (uint32_t)d.smem_rows * (d.group + 1) * 4;
     d.cluster = (int32_t)h.cluster;
     d.one_row = (int32_t)h.one_row;

@@ -422,17 +422,32 @@ __global__ void __launch_bounds__(QX_NT, 1)
             halt_at = d.halt_at[m];
         }
     }
-    // the running program and the warp ranges: from shared memory when the plan's tables fit there
+    // the plan tables the token loop reads: copied into the shared-memory table area where the
+    // executor placed them (bundled plans), else read from global memory
     const qx_phase *prog = RUN ? d.run_prog : d.step_prog;
-    const uint32_t *warp_ptr = d.warp_ptr;
-    if (R > 1 && d.tables_smem) {
-        const int np = RUN ? d.n_run_prog : d.n_step_prog;
-        qx_phase *sp = reinterpret_cast<qx_phase *>(rings + qx_ring_bytes(d));
-        uint32_t *sw = reinterpret_cast<uint32_t *>(sp + np);
-        for (int i = threadIdx.x; i < np; i += QX_NT) sp[i] = prog[i];
-        for (int i = threadIdx.x; i < d.n_warp_ptr; i += QX_NT) sw[i] = warp_ptr[i];
-        prog = sp;
-        warp_ptr = sw;
+    const uint32_t *warp_ptr = d.warp_ptr, *rows_t = d.rows, *vhsum_t = d.vhsum_rows;
+    const qx_vhead *vheads_t = d.vheads;
+    const qx_stage *stages_t = d.stages;
+    if (R > 1 && d.table_bytes) {
+        const void *src[6] = {prog, warp_ptr, vheads_t, rows_t, vhsum_t, stages_t};
+        const void *dst[6];
+        char *area = rings + qx_ring_bytes(d);
+#pragma unroll
+        for (int t = 0; t < 6; t++) {
+            dst[t] = src[t];
+            if (d.tab_off[t] == QX_NONE32) continue;
+            uint32_t *to = reinterpret_cast<uint32_t *>(area + d.tab_off[t]);
+            const uint32_t *from = static_cast<const uint32_t *>(src[t]);
+            const uint32_t nw = t == QX_TAB_PROG ? (RUN ? d.n_run_prog : d.n_step_prog) * 4 : d.tab_words[t];
+            for (uint32_t i = threadIdx.x; i < nw; i += QX_NT) to[i] = __ldg(from + i);
+            dst[t] = to;
+        }
+        prog = static_cast<const qx_phase *>(dst[QX_TAB_PROG]);
+        warp_ptr = static_cast<const uint32_t *>(dst[QX_TAB_WARP_PTR]);
+        vheads_t = static_cast<const qx_vhead *>(dst[QX_TAB_VHEADS]);
+        rows_t = static_cast<const uint32_t *>(dst[QX_TAB_ROWS]);
+        vhsum_t = static_cast<const uint32_t *>(dst[QX_TAB_VHSUM]);
+        stages_t = static_cast<const qx_stage *>(dst[QX_TAB_STAGES]);
     }
     phase_sync(C);  // (with C > 1, also: every CTA of the cluster runs before rows are shared)
     if (TC) tc_after();
@@ -446,7 +461,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
 #endif
             switch (kind) {
             case QX_PH_ZERO:
-                for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) QX_AT(sml, d.rows[ph.a + i]) = 0.0f;
+                for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) QX_AT(sml, rows_t[ph.a + i]) = 0.0f;
                 break;
             case QX_PH_LOADX:
                 for (uint32_t i = warp * R + way; i < ph.b; i += QX_NW * R) {
@@ -473,7 +488,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 float *H = d.hist[ph.c];
                 const size_t ne = d.NE[ph.c], bp = d.Bpad;
                 for (uint32_t i = gw * R + way; i < ph.b; i += nwv * R) {
-                    const qx_stage s = d.stages[ph.a + i];
+                    const qx_stage s = stages_t[ph.a + i];
                     float *h = H + (size_t)s.e * bp + m;
                     float h0 = h[0];
                     float h1 = s.ml >= 2 ? h[ne * bp] : 0.0f;
@@ -718,7 +733,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 for (uint32_t i0 = gw * R; i0 < n; i0 += nwv * R) {
                     const uint32_t i = i0 + way;
                     const bool vin = R == 1 || i < n;
-                    const qx_vhead vh = d.vheads[ph.a + (vin ? i : i0)];
+                    const qx_vhead vh = vheads_t[ph.a + (vin ? i : i0)];
                     const float x0 = QX_AT(sml, d.one_row);
                     uint32_t fcode = 0;  // decay factor: 0 -> 1, 1 -> 1/2, 2 -> 0
                     if (vh.nrows > 0) {
@@ -790,7 +805,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     uint2 rec[4];
 #pragma unroll
                     for (int b = 0; b < 4; b++) rec[b] = wl[r0 + b];
-                    const qx_vhead vh = d.vheads[ph.a + (rec[0].x & 0xFFu)];
+                    const qx_vhead vh = vheads_t[ph.a + (rec[0].x & 0xFFu)];
                     const size_t mstride = (size_t)d.V[vh.hl] * (QX_HD * QX_HD);
                     const float *S0 = d.S[vh.hl] + (size_t)vh.vh * (QX_HD * QX_HD) + lane * 4;
                     int mmv[4], wr[4], qr[4][QH];
@@ -942,7 +957,10 @@ __global__ void __launch_bounds__(QX_NT, 1)
                             for (int b = 0; b < 4; b++)
                                 if (b == sb) { hit = any[b]; mm = mmv[b]; }
                             const uint32_t orw = sr == 0 ? vh.out4[0] : sr == 1 ? vh.out4[1] : sr == 2 ? vh.out4[2] : vh.out4[3];
-                            if (hit) atomicAdd(Dp + (orw >> 2) + mm, pv[0]);  // an L2 reduction
+                            if (hit) {
+                                if (d.direct_out) add_all(&QX_AT(sm + mm, orw), pv[0], 1);  // the residual row
+                                else atomicAdd(Dp + (orw >> 2) + mm, pv[0]);  // an L2 reduction
+                            }
                         }
                     } else {
 #pragma unroll
@@ -956,7 +974,9 @@ __global__ void __launch_bounds__(QX_NT, 1)
                                 if (orow[k] == QX_NONE32) continue;
                                 const float z = zf[k].live ? relu(fmaf(zf[k].c, x0m, QX_ATC(smm, zf[k].row))) : 0.0f;
                                 const float out = pw2[b] ? oc[k] * inv[b] : __fdiv_rn(oc[k], norm[b]);
-                                atomicAdd(Dp + (orow[k] >> 2) + mmv[b], __fmul_rn(__fmul_rn(out, z), ow[k]));
+                                const float val = __fmul_rn(__fmul_rn(out, z), ow[k]);
+                                if (d.direct_out) add_all(&QX_AT(sm + mmv[b], orow[k]), val, 1);
+                                else atomicAdd(Dp + (orow[k] >> 2) + mmv[b], val);
                             }
                         }
                     }
@@ -968,7 +988,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 // the phase's output deltas into this copy's rows (L2 reads: the adds bypassed L1)
                 const float *Dp = D0 + dpar * (QX_DELTA_ROWS * 32);
                 for (uint32_t j = warp * R + way; j < ph.b; j += QX_NW * R)
-                    QX_AT(sml, d.vhsum_rows[ph.a + j]) += __ldcg(Dp + j * 32 + ml);
+                    QX_AT(sml, vhsum_t[ph.a + j]) += __ldcg(Dp + j * 32 + ml);
                 dprev = ph.b;
                 dpar ^= 1;
                 break;

@@ -57,12 +57,16 @@ struct QxDev {
                         // 32 / group records side by side; rows are group + 1 floats)
     int32_t n_zero_rows;
     int32_t n_run_prog, n_step_prog, n_warp_ptr;  // entries of the programs and of WARP_PTR
-    int32_t tables_smem;  // 1: the kernel copies the running program and WARP_PTR to shared memory
+    // shared-memory copies of plan tables (bundled plans): bytes reserved after the rings, and per
+    // table (QX_TAB_*) its byte offset there, or QX_NONE32 where it stays in global memory
+    uint32_t table_bytes;
+    uint32_t tab_off[6], tab_words[6];
     // tensor-core form phases
     const qx_mma_phase *mma_phases;
     const qx_mma_tile *mma_tiles;
     const uint4 *tiledata;  // [tiles][128 rows][2] (a row: 16 bf16 weights)
     int32_t has_mma;        // the kernel allocates tensor memory
+    int32_t direct_out;     // value-head outputs add into the residual rows (no delta rows)
     // merged readout and text tokens (QX_PLAN_FLAG_MERGED)
     const uint32_t *feat_dim, *code_row, *text_words, *text_touch;
     const float *text_base, *text_bits;
@@ -99,6 +103,8 @@ __device__ __forceinline__ size_t qx_copy(const QxDev &d, uint32_t hl, int m) {
 // value heads one VH phase may list (the record packs the phase-local index in 8 bits); its
 // 8-byte (value head, machine) records live in the stream rings
 #define QX_VH_CHUNK 64
+// plan tables a bundled plan's token loop may read from shared memory, in the order they are placed
+enum { QX_TAB_PROG = 0, QX_TAB_WARP_PTR, QX_TAB_VHEADS, QX_TAB_ROWS, QX_TAB_VHSUM, QX_TAB_STAGES };
 // stream piece flags (header quad .w >> 24)
 #define QX_R_FIRST 1u
 #define QX_R_LAST 2u
@@ -120,10 +126,9 @@ __host__ __device__ inline size_t qx_ring_offset(const QxDev &d) {
 __host__ __device__ inline size_t qx_ring_bytes(const QxDev &d) {
     return (size_t)QX_NW * 2 * QX_RING_QUADS * 16 * (32 / d.group);
 }
-// bundled plans (groups of fewer than 32 machines) keep the running phase program and the warp
-// ranges in shared memory, after the rings (tables_smem: they fit QX_TABLE_BYTES)
-#define QX_TABLE_BYTES 8192
-__host__ __device__ inline size_t qx_table_bytes(const QxDev &d) { return d.group < 32 ? QX_TABLE_BYTES : 0; }
+// bundled plans (groups of fewer than 32 machines) keep the plan tables the token loop reads in
+// shared memory after the rings, as many as fit the plan's table_bytes (tab_off)
+__host__ __device__ inline size_t qx_table_bytes(const QxDev &d) { return d.table_bytes; }
 __host__ __device__ inline size_t qx_smem_bytes(const QxDev &d) {
     return qx_ring_offset(d) + qx_ring_bytes(d) + qx_table_bytes(d);
 }

@@ -57,7 +57,7 @@ NONE = 0xFFFF
 NONE32 = 0xFFFFFFFF
 ROW_PAD = 33
 MAGIC = 0x314E414C50585151
-VERSION = 17
+VERSION = 18
 # machines one CTA runs (its group): 32 (a lane per machine) or, for few machines per GPU, 16, 8
 # or 4 -- then a warp's lanes are WAYS = 32 / group record slots of `group` machines each, and the
 # stream of a phase comes in lines of WAYS quads (one per slot) whose records the plan compiler
@@ -106,8 +106,10 @@ TABLE_ORDER = (["pc", "count", "j", "vcnt", "regs.rs1", "regs.rs2", "regs.rd"]
                + [f"drom{i}" for i in range(16)] + [f"bn1.{i}" for i in range(4)]
                + [f"bn2.{i}" for i in range(4)] + [f"ram{i}" for i in range(32)])
 SMEM_MAX = 232448  # dynamic shared memory one B200 CTA may opt into (227 KB)
-# bundled plans: shared memory for the running phase program and the warp ranges
-TABLE_BYTES = 8192
+# bundled plans: shared memory for plan tables the token loop reads (the running phase program,
+# the warp ranges, value heads, zero-row lists, delta-sum rows, lag stages: those that fit, in
+# that order), by group: as much as leaves the plan its fewest phases
+TABLE_BYTES = {32: 0, 16: 24576, 8: 36864, 4: 24576}
 # tensor-core form phases (PH["MMA"]): F[form, machine] = sum W[form, k] X[k, machine] on tcgen05
 # as M = 128 forms (a form block) x N = 32 machines x K = 16 source rows (a K block) tiles, bf16
 # operands (every weight and every value a form reads is bf16-exact) and fp32 accumulators in
@@ -119,6 +121,9 @@ MMA_MAX_KB = 16
 MMA_MAX_FB = 8
 FLAG_MMA = 1  # header flag: the plan has tensor-core form phases
 FLAG_MERGED = 2  # header flag: merged readout (code-dim signs, text tokens; MERGED_INFO)
+# header flag: value-head outputs add straight into the residual rows (shared-memory reductions;
+# plans of one CTA a group): OUT_ROW / out4 hold residual rows and no VHSUM phase exists
+FLAG_DIRECT_OUT = 4
 DEFERRED = 0x80000000  # FEAT_ROW flag: the feature is loaded where it is first used (low bits: dim)
 
 DT = {
@@ -146,7 +151,7 @@ def smem_extra_bytes(ksel_slots: int, qhot: int, nw: int, group: int = 32) -> in
     """Shared memory after the rows: the zero row, key-select slots, the decode area, a counter
     block and the per-warp stream rings (two halves of RING_QUADS lines of 32 / group quads)."""
     return (row_pad(group) * 4 + ksel_slots * 32 * (1 + qhot) * 4 + 32 * 18 * 4 + 64 + 16
-            + nw * 2 * RING_QUADS * 16 * (32 // group) + (TABLE_BYTES if group < 32 else 0))
+            + nw * 2 * RING_QUADS * 16 * (32 // group) + TABLE_BYTES[group])
 
 
 def _bf16_bits(w: float) -> int:
@@ -201,7 +206,7 @@ class Plan:
                            h["n_head_levels"], h["one_row"], h["n_ksel_slots"], h["qhot_max"],
                            h["n_fam"], h["n_pay"], h["n_feat"], h["n_emb_rows"], h["n_families"],
                            h["vocab"], h["n_born0"], h["cluster"], h.get("flags", 0),
-                           h.get("group", 32), 0, *offs, *cnts)
+                           h.get("group", 32), h.get("table_bytes", 0), *offs, *cnts)
         out = bytearray(pos)
         out[:len(head)] = head
         for p, b in parts:
@@ -241,6 +246,9 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
         ksel_part = KSEL_PART[cluster] if ways == 1 else KSEL_PART_WAYS[ways]
     assert 1 <= ksel_part <= 128
     unit_chunk = UNIT_CHUNK if ways == 1 else UNIT_CHUNK_WAYS[ways]
+    # value-head outputs: straight into the residual rows on one CTA, through L2 delta rows on a
+    # cluster (whose copies each fold them in)
+    direct_out = cluster == 1
     # the kernel takes the ONE dim as 1 on every machine: no sublayer may write it
     assert ONE not in set(int(d) for d in g.ffn_out) and ONE not in set(int(d) for d in g.out_dim)
     ring_bytes = nw * 2 * RING_QUADS * 16 * ways
@@ -880,7 +888,7 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                 # j * 128: 32 machines x fp32) by L2 atomic adds; a VHSUM phase adds them into
                 # the residual rows (of every copy, on a cluster)
                 def fits(nh, nr):
-                    return nh <= VH_CHUNK and nh * 32 * 8 <= ring_bytes and nr <= DELTA_ROWS
+                    return nh <= VH_CHUNK and nh * 32 * 8 <= ring_bytes and (direct_out or nr <= DELTA_ROWS)
 
                 c0 = v0
                 while c0 < len(vheads_l):
@@ -894,6 +902,12 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                         rows += new
                         c1 += 1
                     assert c1 > c0, "one value head has more output rows than the delta buffer"
+                    if direct_out:
+                        # one CTA a group: the outputs add into the residual rows themselves
+                        body.append((PH["VH"], c0, c1, 0))
+                        body.append((PH["VHRUN"], c0, c1, 0))
+                        c0 = c1
+                        continue
                     dpos = {r: i * 128 for i, r in enumerate(rows)}
                     for v in range(c0, c1):
                         col = vheads_l[v][2]
@@ -1028,7 +1042,9 @@ def compile_plan(g: GraphData, smem_rows: int | None = None, nw: int = NW_DEFAUL
                  n_fam=len(g.fam_dims), n_pay=len(g.pay_dims), n_feat=len(feat),
                  n_emb_rows=int(g.emb_table.shape[0]), n_families=len(g.fam_ids),
                  vocab=int(g.vocab), n_born0=len(born0), cluster=cluster,
-                 flags=(FLAG_MMA if mma_l else 0) | (FLAG_MERGED if merged else 0), group=group)
+                 flags=(FLAG_MMA if mma_l else 0) | (FLAG_MERGED if merged else 0)
+                 | (FLAG_DIRECT_OUT if direct_out else 0), group=group,
+                 table_bytes=TABLE_BYTES[group])
     stats["n_slots"] = n_slots
     stats["ksel_slots"] = ksel_slots
     stats["deferred_features"] = len(deferred)

@@ -235,7 +235,8 @@ class PlanInterp:
                     self.X[int(s["VHSUM_ROWS"][a + jj])] += self.delta[jj * 128]
             elif k == PH["VH"]:
                 self.Dw[:] = 0
-                out_rows = self.delta
+                # direct plans (one CTA a group) add the outputs into the residual rows themselves
+                out_rows = self.X if self.P.hdr.get("flags", 0) & 4 else self.delta
                 x0 = self.X[self.one]
                 for vh in s["VHEADS"][a:b]:
                     hl, j, col, sl = int(vh["hl"]), int(vh["vh"]), int(vh["col"]), int(vh["slot"])

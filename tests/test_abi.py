@@ -131,7 +131,7 @@ def test_plan_is_consistent(graph, cluster, tc, group):
 
     assert (PH["FORMS"] in kinds) != tc and (PH["MMA"] in kinds) == tc
     if tc:
-        assert P.hdr["flags"] == 1
+        assert P.hdr["flags"] & 1 and bool(P.hdr["flags"] & 4) == (cluster == 1)
         tiles, n_tiles = s["MMA_TILES"], len(s["TILEDATA"]) // (128 * 16)
         commits = 0
         for mp in s["MMA_PHASES"]:
