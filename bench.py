@@ -188,6 +188,17 @@ def gdn_bench(torch, steps: int, warmup: int, peak_gbs: float, B: int = 1024) ->
             "launches_per_step": 2}
 
 
+def job_config(args, world: int) -> dict:
+    """The workload a run measures (both arms print the same): machines of the job and per GPU,
+    tokens per step, how the job splits, and why no L2 flush is needed."""
+    per_gpu = args.machines if args.weak else -(-args.machines // world)
+    return {"workload": WORKLOAD, "machines_per_gpu": per_gpu,
+            "machines_total": args.machines * (world if args.weak else 1),
+            "tokens_per_step": args.tokens_per_step,
+            "parallelism": f"machines sharded over {world} GPU(s)",
+            "l2": f"no flush: {per_gpu * 12.5e6 / 1e9:.0f} GB of head states per GPU, far above L2"}
+
+
 def reference_arm(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -198,7 +209,7 @@ def reference_arm(args) -> None:
     import oracle
     from qwenputer_b200.graphfile import default_graph_path, load_graph
 
-    B = min(args.machines, 32)
+    B = min(args.machines, 64)
     progs = workload.workload_programs("bignum", B, args.seed)
     g = load_graph(default_graph_path())
     o = oracle.Oracle(g)
@@ -207,7 +218,7 @@ def reference_arm(args) -> None:
         o.snapshot(st, r, oracle.Machine.from_program(progs[r]))
     x = g.embed([GO_TOKEN] * B)
     cores = os.cpu_count() or 1
-    tps = 4  # tokens per step of the CPU sample
+    tps = 16  # tokens per step of the CPU sample
 
     def step(x):
         for _ in range(tps):
@@ -222,15 +233,14 @@ def reference_arm(args) -> None:
         x = step(x)
     dt = time.perf_counter() - t0
     val = B * tps * args.steps / dt
-    sample = f"{B} machines x {tps} free-running tokens per step on {cores} host threads"
+    sample = (f"each step: {B} of the job's machines x {tps} free-running tokens (a bounded sample of "
+              f"a step's {args.machines} x {args.tokens_per_step}) on {cores} host threads")
     emit({
         "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic: seeded RV32IM programs (bignum mix)",
-        "config": {"workload": WORKLOAD,
-                   "machines_total": args.machines * (args.gpus if args.weak else 1),
-                   "tokens_per_step": tps, "sample_machines": B},
+        "config": job_config(args, args.gpus),
         "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
@@ -378,13 +388,10 @@ def main() -> None:
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded RV32IM programs (bignum mix), machines start from their images",
-            "config": {"workload": WORKLOAD,
-                       "machines_per_gpu": B, "machines_total": B * world,
-                       "tokens_per_step": tps, "parallelism": f"machines sharded over {world} GPU(s)",
-                       "machines_per_cta_group": ex.group, "ctas_per_group": ex.cluster,
+            "config": job_config(args, world),
+            "launch": {"machines_per_cta_group": ex.group, "ctas_per_group": ex.cluster,
                        "groups_per_gpu": -(-B // ex.group), "ctas": ex.info(2),
-                       "forms_on": "tensor cores (tcgen05)" if args.tc else "CUDA cores",
-                       "l2": f"no flush: {B * 12.5e6 / 1e9:.0f} GB of head states per GPU, far above L2"},
+                       "forms_on": "tensor cores (tcgen05)" if args.tc else "CUDA cores"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": DRAM_BYTES_PER_MACHINE_TOKEN * B * tps,
