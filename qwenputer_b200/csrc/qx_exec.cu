@@ -525,6 +525,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     const uint4 *q = st.rp + R + way;
                     if (fl & QX_R_FIRST) a0 = a1 = a2 = a3 = 0.0f;  // a0, a2: form A; a1, a3: B
                     uint32_t j = 0;
+#pragma unroll 2
                     for (; j + 2 <= n; j += 2) {
                         const uint4 e0 = q[j * R], e1 = q[(j + 1) * R];
                         const float v0 = QX_AT(sml, e0.x), v1 = QX_AT(sml, e0.z), v2 = QX_AT(sml, e1.x),
@@ -590,6 +591,7 @@ __global__ void __launch_bounds__(QX_NT, 1)
                     if (fl & QX_R_FIRST) acc0 = acc1 = acc2 = acc3 = 0.0f;
                     const uint32_t nc = h.y;
                     uint32_t j = 0;
+#pragma unroll 2
                     for (; j + 2 <= nc; j += 2) {
                         const uint4 u0 = q[j * R], u1 = q[(j + 1) * R];
                         const float f0 = QX_AT(sml, u0.x), f1 = QX_AT(sml, u1.x);
@@ -752,18 +754,6 @@ __global__ void __launch_bounds__(QX_NT, 1)
                         anyq |= qj >= 0;
                     }
                     const bool need = act && vin && (fcode != 0 || wrow >= 0 || anyq);
-                    if (need && anyq) {
-                        // the rows the serving phase will read: on their way into L2 now
-                        const float *Sq = d.S[vh.hl] + qx_copy(d, vh.hl, m) * ((size_t)d.V[vh.hl] * (QX_HD * QX_HD)) +
-                                          (size_t)vh.vh * (QX_HD * QX_HD);
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const uint32_t qj = qpack >> (8 * j) & 0xFFu;
-                            if (qj)
-                                asm volatile("cp.async.bulk.prefetch.L2.global [%0], 512;" ::"l"(Sq + (qj - 1) * QX_HD)
-                                             : "memory");
-                        }
-                    }
                     const unsigned mask = __ballot_sync(0xFFFFFFFFu, need);
                     if (!mask) continue;
                     // the value head's records, padded to a multiple of four (pad records: bit 31)
