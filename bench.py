@@ -39,9 +39,10 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "rv32im_trace_tokens_per_s"
-# DRAM bytes per machine-token of the token kernel: an ncu capture of 256 machines x 4 tokens
-# (dram__bytes_read.sum + dram__bytes_write.sum = 11.62 MB + 8 KB), per machine-token
-DRAM_BYTES_PER_MACHINE_TOKEN = (11.62368e6 + 8192) / 1024
+# DRAM bytes per machine-token of the token kernel: ncu captures of 256 machines x 4 tokens
+# (dram__bytes_read.sum + dram__bytes_write.sum), per machine-token: groups of 32 machines
+# (11.37 MB + 0 B) and bundled groups of 4 (11.84 MB + 16.9 KB; used for every bundled group)
+DRAM_BYTES_PER_MACHINE_TOKEN = {32: 11.368192e6 / 1024, 4: (11.840512e6 + 16896) / 1024}
 WORKLOAD = "rv32im free-run, bignum mix (40% MUL/MULH/DIVU chains, 20% LW/SW over 16 KB)"
 UNIT = "tokens/s"
 GO_TOKEN = 230322  # the run-start control (families then controls: NT .. HALT, GO, SC)
@@ -394,9 +395,10 @@ def main() -> None:
                        "forms_on": "tensor cores (tcgen05)" if args.tc else "CUDA cores"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": DRAM_BYTES_PER_MACHINE_TOKEN * B * tps,
+                         "traffic": DRAM_BYTES_PER_MACHINE_TOKEN[32 if ex.group == 32 else 4] * B * tps,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
-                                           "256-machine x 4-token launch, scaled by machine-tokens",
+                                           f"256-machine x 4-token launch at groups of {32 if ex.group == 32 else 4}, "
+                                           "scaled by machine-tokens",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "weight_bytes_per_token": w_bytes,
                          "state_bytes_per_machine_token": state_per_launch / (tps * B)},
