@@ -1053,69 +1053,153 @@ __global__ void __launch_bounds__(QX_NT, 1)
                 }
                 __syncthreads();
                 // next embedding (FreeRun: table row for small families, base + payload bits;
-                // a text token: its base + the rows of its bits; no token: the bare text base)
-                for (int mm = warp; mm < M; mm += QX_NW) {
-                    const int fid = dec_i[mm] & 0xFFFFFF, kind = dec_i[mm] >> 24, p = dec_i[32 + mm];
-                    float *smw = sm + mm;
-                    float *xm = d.x + (size_t)(mbase + mm) * d.D;
-                    const bool mact = mbase + mm < d.B;
-                    // a feature's value into its row, or (deferred) into x where its sublayer loads it
-                    auto put = [&](int f, float v) {
-                        const uint32_t fr = d.feat_row[f];
-                        if (!(fr & QX_FEAT_DEFERRED)) QX_AT(smw, fr) = v;
-                        else if (mact) xm[fr & ~QX_FEAT_DEFERRED] = v;
-                    };
-                    if (kind != 0) {
-                        const uint32_t *w = d.text_words + (size_t)(kind == 1 ? p : 0) * 5;
-                        uint32_t wv[5];
-#pragma unroll
-                        for (int k = 0; k < 5; k++) wv[k] = kind == 1 ? __ldg(w + k) : 0u;
-                        for (int f = lane; f < d.n_feat; f += 32) put(f, 0.0f);
-                        __syncwarp();
-                        for (int tt = lane; tt < d.n_text_touch; tt += 32) {
-                            const int f = (int)d.text_touch[tt];
-                            float acc = __ldg(d.text_base + f);
-#pragma unroll 1
-                            for (int k = 0; k < 5; k++) {
-                                uint32_t bits = wv[k];
-                                while (bits) {
-                                    const int j = 32 * k + __ffs(bits) - 1;
-                                    bits &= bits - 1;
-                                    acc = __fadd_rn(acc, __ldg(d.text_bits + (size_t)j * d.n_feat + f));
-                                }
-                            }
-                            put(f, acc);
+                // a text token: its base + the rows of their bits; no token: the bare text base).
+                // A group of fewer machines than warps shares each machine's features between
+                // K = 16 / M warps: first every feature that is not a table row's is zeroed, then
+                // (after a barrier) the touched ones are written; warp k of a machine takes
+                // features k * 32 + lane, stepping 32 K.  Larger groups: a warp a machine.
+                if constexpr (M < QX_NW) {
+                    constexpr int K = QX_NW / M;
+                    const int mfirst = warp % M, kk = warp / M;
+                    for (int mm = mfirst; mm < M; mm += QX_NW) {
+                        const int fid = dec_i[mm] & 0xFFFFFF, kind = dec_i[mm] >> 24;
+                        if (kind == 0 && d.fam_row0[fid] >= 0) continue;  // a table row: written below
+                        float *smw = sm + mm;
+                        float *xm = d.x + (size_t)(mbase + mm) * d.D;
+                        const bool mact = mbase + mm < d.B;
+                        for (int f = kk * 32 + lane; f < d.n_feat; f += 32 * K) {
+                            const uint32_t fr = d.feat_row[f];
+                            if (!(fr & QX_FEAT_DEFERRED)) QX_AT(smw, fr) = 0.0f;
+                            else if (mact) xm[fr & ~QX_FEAT_DEFERRED] = 0.0f;
                         }
-                        continue;
                     }
-                    const int row0 = d.fam_row0[fid];
-                    if (row0 >= 0) {
-                        int r = row0 + p;
-                        r = r < 0 ? 0 : (r > d.n_emb_rows - 1 ? d.n_emb_rows - 1 : r);
-                        for (int f = lane; f < d.n_feat; f += 32) put(f, __ldg(d.emb_table + (size_t)r * d.n_feat + f));
-                    } else {
-                        // every feature 0, then the family's touched ones: base + the payload
-                        // bits' rows (four partial sums: exact values, any order)
-                        const int npay = d.merged ? 16 : d.n_pay;  // (a merged graph reads no payload dims)
-                        const float *bits = d.emb_bits + (size_t)fid * npay * d.n_feat;
-                        for (int f = lane; f < d.n_feat; f += 32) put(f, 0.0f);
-                        __syncwarp();
-                        const uint32_t t1 = d.fam_touch_ptr[fid + 1];
-                        for (uint32_t tt = d.fam_touch_ptr[fid] + lane; tt < t1; tt += 32) {
-                            const int f = (int)d.fam_touch[tt];
-                            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                            int i = 0;
-                            for (; i + 4 <= npay; i += 4) {
-                                float w[4];
+                    __syncthreads();
+                    for (int mm = mfirst; mm < M; mm += QX_NW) {
+                        const int fid = dec_i[mm] & 0xFFFFFF, kind = dec_i[mm] >> 24, p = dec_i[32 + mm];
+                        float *smw = sm + mm;
+                        float *xm = d.x + (size_t)(mbase + mm) * d.D;
+                        const bool mact = mbase + mm < d.B;
+                        // a feature's value into its row, or (deferred) into x where its sublayer loads it
+                        auto put = [&](int f, float v) {
+                            const uint32_t fr = d.feat_row[f];
+                            if (!(fr & QX_FEAT_DEFERRED)) QX_AT(smw, fr) = v;
+                            else if (mact) xm[fr & ~QX_FEAT_DEFERRED] = v;
+                        };
+                        if (kind != 0) {
+                            const uint32_t *w = d.text_words + (size_t)(kind == 1 ? p : 0) * 5;
+                            uint32_t wv[5];
 #pragma unroll
-                                for (int u = 0; u < 4; u++) w[u] = __ldg(bits + (size_t)(i + u) * d.n_feat + f);
-#pragma unroll
-                                for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(dec_pay[(i + u) * 32 + mm], w[u]));
+                            for (int k = 0; k < 5; k++) wv[k] = kind == 1 ? __ldg(w + k) : 0u;
+                            for (int tt = kk * 32 + lane; tt < d.n_text_touch; tt += 32 * K) {
+                                const int f = (int)d.text_touch[tt];
+                                float acc = __ldg(d.text_base + f);
+#pragma unroll 1
+                                for (int k = 0; k < 5; k++) {
+                                    uint32_t bits = wv[k];
+                                    while (bits) {
+                                        const int j = 32 * k + __ffs(bits) - 1;
+                                        bits &= bits - 1;
+                                        acc = __fadd_rn(acc, __ldg(d.text_bits + (size_t)j * d.n_feat + f));
+                                    }
+                                }
+                                put(f, acc);
                             }
-                            for (; i < npay; i++)
-                                acc[0] = __fadd_rn(acc[0], __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
-                            const float tot = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-                            put(f, __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), tot));
+                            continue;
+                        }
+                        const int row0 = d.fam_row0[fid];
+                        if (row0 >= 0) {
+                            int r = row0 + p;
+                            r = r < 0 ? 0 : (r > d.n_emb_rows - 1 ? d.n_emb_rows - 1 : r);
+                            for (int f = kk * 32 + lane; f < d.n_feat; f += 32 * K)
+                                put(f, __ldg(d.emb_table + (size_t)r * d.n_feat + f));
+                        } else {
+                            // the family's touched features: base + the payload bits' rows (four
+                            // partial sums: exact values, any order)
+                            const int npay = d.merged ? 16 : d.n_pay;  // (a merged graph reads no payload dims)
+                            const float *bits = d.emb_bits + (size_t)fid * npay * d.n_feat;
+                            const uint32_t t1 = d.fam_touch_ptr[fid + 1];
+                            for (uint32_t tt = d.fam_touch_ptr[fid] + kk * 32 + lane; tt < t1; tt += 32 * K) {
+                                const int f = (int)d.fam_touch[tt];
+                                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                                int i = 0;
+                                for (; i + 4 <= npay; i += 4) {
+                                    float w[4];
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) w[u] = __ldg(bits + (size_t)(i + u) * d.n_feat + f);
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(dec_pay[(i + u) * 32 + mm], w[u]));
+                                }
+                                for (; i < npay; i++)
+                                    acc[0] = __fadd_rn(acc[0], __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
+                                const float tot = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+                                put(f, __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), tot));
+                            }
+                        }
+                    }
+                } else {
+                    for (int mm = warp; mm < M; mm += QX_NW) {
+                        const int fid = dec_i[mm] & 0xFFFFFF, kind = dec_i[mm] >> 24, p = dec_i[32 + mm];
+                        float *smw = sm + mm;
+                        float *xm = d.x + (size_t)(mbase + mm) * d.D;
+                        const bool mact = mbase + mm < d.B;
+                        // a feature's value into its row, or (deferred) into x where its sublayer loads it
+                        auto put = [&](int f, float v) {
+                            const uint32_t fr = d.feat_row[f];
+                            if (!(fr & QX_FEAT_DEFERRED)) QX_AT(smw, fr) = v;
+                            else if (mact) xm[fr & ~QX_FEAT_DEFERRED] = v;
+                        };
+                        if (kind != 0) {
+                            const uint32_t *w = d.text_words + (size_t)(kind == 1 ? p : 0) * 5;
+                            uint32_t wv[5];
+#pragma unroll
+                            for (int k = 0; k < 5; k++) wv[k] = kind == 1 ? __ldg(w + k) : 0u;
+                            for (int f = lane; f < d.n_feat; f += 32) put(f, 0.0f);
+                            __syncwarp();
+                            for (int tt = lane; tt < d.n_text_touch; tt += 32) {
+                                const int f = (int)d.text_touch[tt];
+                                float acc = __ldg(d.text_base + f);
+#pragma unroll 1
+                                for (int k = 0; k < 5; k++) {
+                                    uint32_t bits = wv[k];
+                                    while (bits) {
+                                        const int j = 32 * k + __ffs(bits) - 1;
+                                        bits &= bits - 1;
+                                        acc = __fadd_rn(acc, __ldg(d.text_bits + (size_t)j * d.n_feat + f));
+                                    }
+                                }
+                                put(f, acc);
+                            }
+                            continue;
+                        }
+                        const int row0 = d.fam_row0[fid];
+                        if (row0 >= 0) {
+                            int r = row0 + p;
+                            r = r < 0 ? 0 : (r > d.n_emb_rows - 1 ? d.n_emb_rows - 1 : r);
+                            for (int f = lane; f < d.n_feat; f += 32) put(f, __ldg(d.emb_table + (size_t)r * d.n_feat + f));
+                        } else {
+                            // every feature 0, then the family's touched ones: base + the payload
+                            // bits' rows (four partial sums: exact values, any order)
+                            const int npay = d.merged ? 16 : d.n_pay;  // (a merged graph reads no payload dims)
+                            const float *bits = d.emb_bits + (size_t)fid * npay * d.n_feat;
+                            for (int f = lane; f < d.n_feat; f += 32) put(f, 0.0f);
+                            __syncwarp();
+                            const uint32_t t1 = d.fam_touch_ptr[fid + 1];
+                            for (uint32_t tt = d.fam_touch_ptr[fid] + lane; tt < t1; tt += 32) {
+                                const int f = (int)d.fam_touch[tt];
+                                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                                int i = 0;
+                                for (; i + 4 <= npay; i += 4) {
+                                    float w[4];
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) w[u] = __ldg(bits + (size_t)(i + u) * d.n_feat + f);
+#pragma unroll
+                                    for (int u = 0; u < 4; u++) acc[u] = __fadd_rn(acc[u], __fmul_rn(dec_pay[(i + u) * 32 + mm], w[u]));
+                                }
+                                for (; i < npay; i++)
+                                    acc[0] = __fadd_rn(acc[0], __fmul_rn(dec_pay[i * 32 + mm], __ldg(bits + (size_t)i * d.n_feat + f)));
+                                const float tot = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+                                put(f, __fadd_rn(__ldg(d.emb_base + (size_t)fid * d.n_feat + f), tot));
+                            }
                         }
                     }
                 }
